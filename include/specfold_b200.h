@@ -1,0 +1,208 @@
+/*
+ * specfold_b200.h -- C ABI of the B200 (sm_100a) folded multi-branch verify forward.
+ *
+ * One entry point per launch of the reference's fused path
+ * (specfold/generate/fastdllm_v2_folded.py:237-370, nld_folded.py:255-394 and the
+ * Triton kernels in specfold/generate/triton_kernels.py), plus the whole layer loop
+ * as a single call.  Plain pointers and sizes only; every pointer is device memory
+ * unless documented otherwise.  Buffers are owned by the caller; the library
+ * allocates no device memory.  `stream` is a cudaStream_t passed as void*.
+ *
+ * Element types: `dtype` is SF_DTYPE_F32 or SF_DTYPE_BF16 and applies to every
+ * hidden-state, weight and Q/K/V/O table argument; softmax state (M, Z), rstd and
+ * RoPE q-scales are always float32, indices int64, counters int32.
+ *
+ * Layouts (row-major unless stated; BN = B1*N flat rows, row r = b*N + n):
+ *   Hf        [BN, D]                 layer input hidden states
+ *   q_buf     [BN+1, H*hd]            RoPE'd queries, row BN is the trash row
+ *   kv_buf    [BN+1, 2*Hkv*hd]        RoPE'd keys (heads 0..Hkv-1) then values
+ *   prefix_k/v [Hkv, >=P, hd] each    head h at offset h*kv_head_stride elements
+ *   O_tab     [BN, H*hd]; M_tab, Z_tab [BN, H] float32
+ *
+ * Every function returns 0 (SF_OK) or a status code; sf_last_error() describes the
+ * last failure of the calling thread.  Launch errors are reported, kernel faults
+ * surface at the caller's next synchronisation.  Kernels that wait on barriers give
+ * up after a bounded time and set bits in `err` (a device int32, see SF_DEV_*).
+ */
+#ifndef SPECFOLD_B200_H
+#define SPECFOLD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  SF_OK = 0,
+  SF_ERR_ARG = 1,          /* bad shape / null pointer / unsupported combination */
+  SF_ERR_CUDA = 2,         /* CUDA runtime error on launch */
+  SF_ERR_UNSUPPORTED = 3,  /* device is not sm_100 or feature missing */
+  SF_ERR_WORKSPACE = 4     /* workspace too small */
+};
+enum { SF_DTYPE_F32 = 0, SF_DTYPE_BF16 = 1 };
+/* bits of the device error word */
+enum { SF_DEV_TIMEOUT = 1, SF_DEV_INDEX = 2, SF_DEV_DEPTH = 4, SF_DEV_TMEM = 8 };
+
+const char* sf_last_error(void);
+int sf_abi_version(void);
+/* 0 when the current device is an sm_100 part the kernels run on */
+int sf_check_device(void);
+
+/* ------------------------------------------------------------------ fold gate ----
+ * Replaces residual_delta_gate_kernel (triton_kernels.py:199-239, launched at
+ * fastdllm_v2_folded.py:306-309) together with src_resolve_kernel
+ * (triton_kernels.py:18-26, launched at :310).  Same arguments and outputs, with
+ * the recompute test written the way the PyTorch reference decides it
+ * (fastdllm_v2_folded.py:139-141): ||x - x_par|| > delta * ||x_par|| with the
+ * difference, both norms and the threshold rounded to the model dtype.
+ * Compaction is deterministic: rows[] lists the recomputed flat rows in ascending
+ * order (branch-major, position-ascending), seg[b*N + i] the i-th recomputed row of
+ * branch b.  Also writes xn[slot] = RMSNorm(Hf[rows[slot]]) * ln_w in the model dtype
+ * (the A operand of the QKV projection) when xn != NULL.
+ * f and src hold branch indices; count[0] and segcnt[0..B1) must be zero on entry
+ * (they are accumulated, as in the reference).                                     */
+int sf_residual_delta_gate(int dtype, const void* Hf, const int64_t* par_idx, float* rstd,
+                           int64_t* f, int8_t* rec, int64_t* rows, int32_t* count,
+                           int64_t* seg, int32_t* segcnt, int64_t* src, void* xn,
+                           const void* ln_w, float delta, int B1, int N, int D, int bucket,
+                           float eps, int* err, void* stream);
+
+/* src_resolve_kernel (triton_kernels.py:18-26): src[b,n] = nearest recomputing
+ * ancestor branch, following f (branch indices) until a fixed point.               */
+int sf_src_resolve(const int64_t* f, int64_t* src, int B1, int N, int* err, void* stream);
+
+/* ------------------------------------------------------------- projections -------
+ * Workspace for every GEMM-based entry point below: sf_gemm_workspace_bytes(...)
+ * bytes of device memory (split-K partial sums and tile counters; tile counters must
+ * be zero on the first use and are left zero by every call).                        */
+size_t sf_workspace_bytes(int BN, int D, int H, int Hkv, int hd, int I, int V);
+/* zero the tile counters inside a fresh workspace */
+int sf_workspace_init(void* ws, size_t ws_bytes, void* stream);
+
+/* fused_ln_qkv_rope_scatter_kernel (triton_kernels.py:29-87, launched at
+ * fastdllm_v2_folded.py:313-319): Q/K/V of the recomputed rows, + bias, RoPE on q
+ * and k (rotate-half, cos/sin [N, hd] in the model dtype), optional per-position
+ * q scale (llama-4, nld_folded.py:175-176; NULL = 1), scattered to q_buf / kv_buf
+ * at the flat row.  xn is the normalised compacted input written by the gate;
+ * w_qkv = [Wq; Wk; Wv] ((H+2Hkv)*hd x D), b_qkv the matching bias (NULL = none).   */
+int sf_fused_ln_qkv_rope_scatter(int dtype, const void* xn, const void* w_qkv,
+                                 const void* b_qkv, const int64_t* rows, const int32_t* count,
+                                 const void* cos, const void* sin, const float* q_scale,
+                                 void* q_buf, void* kv_buf, int D, int N, int bucket, int H,
+                                 int Hkv, int hd, void* ws, size_t ws_bytes, int* err,
+                                 void* stream);
+
+/* specfold_flash_attn_gqa_kernel (triton_kernels.py:301-361, launched at
+ * fastdllm_v2_folded.py:329-333): attention of each recomputed row over the prefix
+ * cache (P keys) and the N in-block keys kv_buf[src[b*N+j]*N + j]; writes O (model
+ * dtype, normalised), M (row max) and Z (sum of exp) at the flat row.  P may be 0.
+ * Takes B1 in addition to the reference's arguments (bounds check of src).          */
+int sf_flash_attn_gqa(int dtype, const void* q_buf, const void* prefix_k, const void* prefix_v,
+                      int64_t kv_head_stride, const void* kv_buf, const int64_t* src,
+                      const int64_t* rows, const int32_t* count, void* O_tab, float* M_tab,
+                      float* Z_tab, int P, int N, float scale, int bucket, int B1, int H,
+                      int Hkv, int hd, int* err, void* stream);
+
+/* specfold_chain_correction_gqa_kernel (triton_kernels.py:364-429, launched at
+ * fastdllm_v2_folded.py:334-338): for every folded row (rec == 0) start from the
+ * source row's (m, Z, O) and apply the exact update for every key that changed along
+ * the branch chain up to the source; writes O, M, Z at the folded row.              */
+int sf_chain_correction_gqa(int dtype, const void* q_buf, const void* kv_buf,
+                            const int64_t* src, const int64_t* par_idx, const int8_t* rec,
+                            const int64_t* seg, const int32_t* segcnt, void* O_tab,
+                            float* M_tab, float* Z_tab, int B1, int N, float scale, int H,
+                            int Hkv, int hd, int* err, void* stream);
+
+/* torch.addmm(Hf, O_tab, Wo^T) at fastdllm_v2_folded.py:351 (all BN rows):
+ * hp = Hf + O_tab @ Wo^T, the matmul rounded to the model dtype before the add.     */
+int sf_o_proj_residual(int dtype, const void* Hf, const void* O_tab, const void* w_o,
+                       void* hp, int BN, int D, int q_dim, void* ws, size_t ws_bytes,
+                       int* err, void* stream);
+
+/* fused_ffn_scatter (triton_kernels.py:176-194, called at fastdllm_v2_folded.py:354-359
+ * with store_ffn_only=True): for each recomputed row rows[slot], slot < count:
+ * ffn_buf[rows[slot]] = down(silu(gate(z)) * up(z)), z = RMSNorm(hp_all[rows[slot]]) *
+ * ln_w.  Reads hp_all directly (the reference gathers hp_all[rows] first).  act_buf
+ * [bucket, I] and xn_buf [bucket, D] (model dtype) and rstd_buf [bucket] are scratch. */
+int sf_fused_ffn_scatter(int dtype, const void* hp_all, const void* ln_w, const void* w_gate,
+                         const void* w_up, const void* w_down, const int64_t* rows,
+                         const int32_t* count, void* ffn_buf, int bucket, void* act_buf,
+                         void* xn_buf, float* rstd_buf, float eps, int D, int I, void* ws,
+                         size_t ws_bytes, int* err, void* stream);
+
+/* hidden = hp_all + ffn_buf[src*N + n] (fastdllm_v2_folded.py:361).                 */
+int sf_combine(int dtype, const void* hp_all, const void* ffn_buf, const int64_t* src,
+               void* hidden, int B1, int N, int D, int* err, void* stream);
+
+/* final norm + lm_head (+ the Fast-dLLM logit shift when shift != 0)
+ * (fastdllm_v2_folded.py:365-366, fastdllm_v2_generation.py:121-126;
+ * nld_folded.py:389-390 without shift).  logits [B1, N, V]; xn_buf [BN, D] scratch. */
+int sf_final_norm_lm_head(int dtype, const void* hidden, const void* norm_w,
+                          const void* lm_w, void* logits, void* xn_buf, int B1, int N, int D,
+                          int V, float eps, int shift, void* ws, size_t ws_bytes, int* err,
+                          void* stream);
+
+/* Block KV commit: append n_new committed positions to a preallocated cache,
+ * cache_{k,v}[h, P + t, :] = new_{k,v}[h, t, :], t < n_new.  Replaces the torch.cat
+ * inside DynamicCache.update (modeling_ministral.py:154-158 via nld_generation.py:
+ * 279-289; the Fast-dLLM remote code at fastdllm_v2_generation.py:560-575).
+ * cache head stride = cache_head_stride elements, new head stride = new_head_stride. */
+int sf_kv_append(int dtype, void* cache_k, void* cache_v, int64_t cache_head_stride,
+                 const void* new_k, const void* new_v, int64_t new_head_stride, int Hkv,
+                 int hd, int P, int n_new, void* stream);
+
+/* ------------------------------------------------------------ whole forward -------
+ * The full per-layer loop of SpecFoldTritonFastDLLMV2Generation._batched_block_forward
+ * (fastdllm_v2_folded.py:296-366) in one call: gate -> QKV -> attention -> chain
+ * correction -> o_proj -> FFN -> combine for every layer, then final norm + lm_head.
+ * Host-side work that stays in the caller: the parent map (:263-265), embedding
+ * lookup and RoPE tables (:267-271), and the fold counters / overflow check (:363-369). */
+typedef struct sf_layer {
+  const void* w_qkv;      /* [(H+2Hkv)*hd, D] */
+  const void* b_qkv;      /* [(H+2Hkv)*hd] or NULL */
+  const void* ln1_w;      /* input_layernorm.weight [D] */
+  const void* w_o;        /* o_proj.weight [D, H*hd] */
+  const void* ln2_w;      /* post_attention_layernorm.weight [D] */
+  const void* w_gate;     /* [I, D] */
+  const void* w_up;       /* [I, D] */
+  const void* w_down;     /* [D, I] */
+  const void* prefix_k;   /* [Hkv, >=P, hd] or NULL when P == 0 */
+  const void* prefix_v;
+} sf_layer;
+
+typedef struct sf_verify_args {
+  int dtype;
+  int B1, N, D, H, Hkv, hd, I, V, L;
+  int P;                       /* prefix length (0 = no prefix cache) */
+  int64_t kv_head_stride;      /* elements between prefix heads */
+  int bucket;                  /* compaction capacity (<= B1*N) */
+  float delta, eps, scale;     /* recompute threshold, RMSNorm eps, attention scale */
+  int shift_logits;            /* 1 for Fast-dLLM, 0 for NLD */
+  const sf_layer* layers;      /* HOST array of L layers */
+  const void* final_norm_w;    /* [D] */
+  const void* lm_w;            /* [V, D] */
+  const int64_t* par_idx;      /* [B1] parent branch (0 for main) */
+  const void* hidden_in;       /* [B1*N, D] embeddings */
+  const void* cos;             /* [N, hd] */
+  const void* sin;             /* [N, hd] */
+  const float* q_scale;        /* [N] or NULL */
+  void* logits;                /* [B1, N, V] */
+  int32_t* count_slab;         /* [L] recomputed rows per layer (zeroed by the call) */
+  int32_t* segcnt_slab;        /* [L*B1] recomputed rows per layer and branch */
+  int8_t* rec_slab;            /* [L*B1*N] fold masks per layer, or NULL */
+  void* ws;                    /* sf_verify_workspace_bytes(...) bytes */
+  size_t ws_bytes;
+  int* err;                    /* device error word (SF_DEV_*), accumulated */
+  void* stream;
+} sf_verify_args;
+
+size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
+                                 int V);
+int sf_folded_verify_forward(const sf_verify_args* args);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPECFOLD_B200_H */

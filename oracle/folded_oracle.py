@@ -156,6 +156,10 @@ def folded_forward(model, batched_input: torch.Tensor, past_key_values, delta: f
                 if capture is not None:
                     capture.positions += N
                     capture.recomputed += int(rbar.numel())
+                    # relative distance to the threshold (diagnostic only)
+                    moved = (x[0] - rows[pj][0]).float().norm(dim=-1)
+                    ref = rows[pj][0].float().norm(dim=-1)
+                    st.setdefault("ratio", [None] * B1)[i] = moved / (delta * ref) - 1.0
             R = int(rbar.numel())
 
             # Q/K/V tables: inherit the parent's, overwrite the recomputed positions
@@ -238,11 +242,15 @@ def folded_forward(model, batched_input: torch.Tensor, past_key_values, delta: f
 
         if capture is not None:
             rec = torch.zeros(B1, N, dtype=torch.bool)
+            margin = torch.full((B1, N), float("inf"))
             for b in range(B1):
                 rec[b, st["rbar"][b].cpu()] = True
+                if "ratio" in st and st["ratio"][b] is not None:
+                    margin[b] = st["ratio"][b].abs().cpu()
             capture.layers.append({
                 "hidden_in": torch.cat(rows, 0).detach().clone(),
                 "rec": rec,
+                "margin": margin,
                 "src": nearest_recomputing_ancestor(rec, parent),
                 "q": torch.stack(st["q"]), "k": torch.stack(st["k"]), "v": torch.stack(st["v"]),
                 "m": torch.stack(st["m"]), "Z": torch.stack(st["Z"]), "O": torch.stack(st["O"]),

@@ -1,0 +1,707 @@
+// extern "C" entry points of libspecfold_b200 (declared in include/specfold_b200.h) and
+// the whole-forward layer loop.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/specfold_b200.h"
+#include "sf_kernels.cuh"
+
+using namespace sf;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SF_OK;
+  return fail(SF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+size_t esize(int dtype) { return dtype == SF_DTYPE_BF16 ? 2 : 4; }
+
+bool dtype_ok(int dtype) { return dtype == SF_DTYPE_F32 || dtype == SF_DTYPE_BF16; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+int check_dims(int dtype, int D, int hd, int H, int Hkv) {
+  if (!dtype_ok(dtype)) return fail(SF_ERR_ARG, "dtype %d not supported", dtype);
+  if (D <= 0 || D % 64 != 0) return fail(SF_ERR_ARG, "hidden size %d must be a multiple of 64", D);
+  if (hd != 64 && hd != 128) return fail(SF_ERR_ARG, "head_dim %d must be 64 or 128", hd);
+  if (H <= 0 || Hkv <= 0 || H % Hkv != 0 || H / Hkv > 16)
+    return fail(SF_ERR_ARG, "heads %d / kv heads %d unsupported", H, Hkv);
+  return SF_OK;
+}
+
+// GEMM workspace need for one projection (rows_cap activation rows)
+size_t ws_gemm(int dtype, int rows, int n_out, int K, int kind, int inter) {
+  return gemm_ws_need(dtype, rows, n_out, K, kind, inter);
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Carves the forward's scratch out of one buffer.
+struct Carve {
+  char* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base(static_cast<char*>(b)) {}
+  void* take(size_t bytes) {
+    void* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return p;
+  }
+};
+
+struct FwdBufs {
+  void *q_buf, *kv_buf, *O, *ffn, *act, *hbuf, *hp, *xn, *gemm_ws;
+  float *M, *Z, *rstd, *rstd2;
+  int64_t *f, *src, *seg, *rows;
+  int8_t* rec;
+  size_t gemm_ws_bytes, total;
+};
+
+FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
+                      int V, int bucket) {
+  const size_t es = esize(dtype);
+  const int BN = B1 * N, qd = H * hd, kvd = Hkv * hd;
+  Carve c(ws);
+  FwdBufs b{};
+  b.q_buf = c.take((BN + 1) * static_cast<size_t>(qd) * es);
+  b.kv_buf = c.take((BN + 1) * static_cast<size_t>(2 * kvd) * es);
+  b.O = c.take(static_cast<size_t>(BN) * qd * es);
+  b.M = static_cast<float*>(c.take(static_cast<size_t>(BN) * H * 4));
+  b.Z = static_cast<float*>(c.take(static_cast<size_t>(BN) * H * 4));
+  b.ffn = c.take((BN + 1) * static_cast<size_t>(D) * es);
+  b.act = c.take(static_cast<size_t>(bucket) * I * es);
+  b.hbuf = c.take(static_cast<size_t>(BN) * D * es);
+  b.hp = c.take(static_cast<size_t>(BN) * D * es);
+  b.xn = c.take(static_cast<size_t>(BN) * D * es);
+  b.rstd = static_cast<float*>(c.take(static_cast<size_t>(BN) * 4));
+  b.rstd2 = static_cast<float*>(c.take(static_cast<size_t>(bucket) * 4));
+  b.f = static_cast<int64_t*>(c.take(static_cast<size_t>(BN) * 8));
+  b.src = static_cast<int64_t*>(c.take(static_cast<size_t>(BN) * 8));
+  b.seg = static_cast<int64_t*>(c.take(static_cast<size_t>(BN) * 8));
+  b.rows = static_cast<int64_t*>(c.take(static_cast<size_t>(bucket) * 8));
+  b.rec = static_cast<int8_t*>(c.take(static_cast<size_t>(BN)));
+  size_t g = 0;
+  g = std::max(g, ws_gemm(dtype, bucket, qd + 2 * kvd, D, EPI_QKV, 0));
+  g = std::max(g, ws_gemm(dtype, BN, D, qd, EPI_RESID, 0));
+  g = std::max(g, ws_gemm(dtype, bucket, 2 * I, D, EPI_SWIGLU, I));
+  g = std::max(g, ws_gemm(dtype, bucket, D, I, EPI_SCATTER, 0));
+  g = std::max(g, ws_gemm(dtype, BN, V, D, EPI_LOGITS, 0));
+  b.gemm_ws_bytes = g;
+  b.gemm_ws = c.take(g + 256);
+  b.total = c.off;
+  return b;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sf_last_error(void) { return g_err.c_str(); }
+
+int sf_abi_version(void) { return 1; }
+
+int sf_check_device(void) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0)
+    return fail(SF_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                dev, major, minor);
+  return SF_OK;
+}
+
+int sf_residual_delta_gate(int dtype, const void* Hf, const int64_t* par_idx, float* rstd,
+                           int64_t* f, int8_t* rec, int64_t* rows, int32_t* count,
+                           int64_t* seg, int32_t* segcnt, int64_t* src, void* xn,
+                           const void* ln_w, float delta, int B1, int N, int D, int bucket,
+                           float eps, int* err, void* stream) {
+  if (!dtype_ok(dtype)) return fail(SF_ERR_ARG, "bad dtype");
+  if (B1 < 1 || B1 > kMaxBranches || N < 1 || B1 * N > kMaxRows)
+    return fail(SF_ERR_ARG, "B1=%d N=%d outside the supported range", B1, N);
+  if (D % 64 != 0 || bucket < 1 || bucket > B1 * N)
+    return fail(SF_ERR_ARG, "D=%d bucket=%d unsupported", D, bucket);
+  if (static_cast<size_t>(B1) * D * esize(dtype) > static_cast<size_t>(kMaxGateSmem))
+    return fail(SF_ERR_ARG, "B1*D too large for the gate");
+  if (!Hf || !par_idx || !rstd || !f || !rec || !rows || !count || !seg || !segcnt || !src ||
+      (xn && !ln_w))
+    return fail(SF_ERR_ARG, "null pointer");
+  GateRowsParams g{};
+  g.hidden = const_cast<void*>(Hf);
+  g.par_idx = par_idx;
+  g.rstd = rstd;
+  g.rec = rec;
+  g.f = f;
+  g.delta = delta;
+  g.eps = eps;
+  g.B1 = B1;
+  g.N = N;
+  g.D = D;
+  g.err = err;
+  int s = cuda_status(launch_gate_rows(dtype, g, S(stream)), "gate");
+  if (s) return s;
+  CompactParams c{};
+  c.rec = rec;
+  c.f = f;
+  c.rows = rows;
+  c.count = count;
+  c.seg = seg;
+  c.segcnt = segcnt;
+  c.src = src;
+  c.hidden = Hf;
+  c.rstd = rstd;
+  c.ln_w = ln_w;
+  c.xn = xn;
+  c.B1 = B1;
+  c.N = N;
+  c.D = D;
+  c.bucket = bucket;
+  c.err = err;
+  return cuda_status(launch_compact(dtype, c, S(stream)), "compact");
+}
+
+int sf_src_resolve(const int64_t* f, int64_t* src, int B1, int N, int* err, void* stream) {
+  if (!f || !src || B1 < 1 || N < 1) return fail(SF_ERR_ARG, "bad arguments");
+  return cuda_status(launch_src_resolve(f, src, B1, N, err, S(stream)), "src_resolve");
+}
+
+size_t sf_workspace_bytes(int BN, int D, int H, int Hkv, int hd, int I, int V) {
+  size_t g = 0;
+  const int qd = H * hd, kvd = Hkv * hd;
+  for (int dt = 0; dt < 2; ++dt) {
+    g = std::max(g, ws_gemm(dt, BN, qd + 2 * kvd, D, EPI_QKV, 0));
+    g = std::max(g, ws_gemm(dt, BN, D, qd, EPI_RESID, 0));
+    g = std::max(g, ws_gemm(dt, BN, 2 * I, D, EPI_SWIGLU, I));
+    g = std::max(g, ws_gemm(dt, BN, D, I, EPI_SCATTER, 0));
+    g = std::max(g, ws_gemm(dt, BN, V, D, EPI_LOGITS, 0));
+  }
+  return g + 512;
+}
+
+int sf_workspace_init(void* ws, size_t ws_bytes, void* stream) {
+  if (!ws) return fail(SF_ERR_ARG, "null workspace");
+  return cuda_status(cudaMemsetAsync(ws, 0, ws_bytes, S(stream)), "workspace init");
+}
+
+static int run_gemm(GemmArgs& a, void* stream, const char* what) {
+  if (a.dtype == SF_DTYPE_BF16) {
+    if (!aligned16(a.X) || !aligned16(a.W) || (a.W2 && !aligned16(a.W2)))
+      return fail(SF_ERR_ARG, "%s: operands must be 16-byte aligned", what);
+  }
+  const size_t need = gemm_ws_need(a.dtype, a.rows_cap, a.n_out, a.K, a.epi.kind, a.epi.inter);
+  if (need > a.ws_bytes)
+    return fail(SF_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", what, a.ws_bytes, need);
+  return cuda_status(gemm(a, S(stream)), what);
+}
+
+int sf_fused_ln_qkv_rope_scatter(int dtype, const void* xn, const void* w_qkv,
+                                 const void* b_qkv, const int64_t* rows, const int32_t* count,
+                                 const void* cos, const void* sin, const float* q_scale,
+                                 void* q_buf, void* kv_buf, int D, int N, int bucket, int H,
+                                 int Hkv, int hd, void* ws, size_t ws_bytes, int* err,
+                                 void* stream) {
+  int s = check_dims(dtype, D, hd, H, Hkv);
+  if (s) return s;
+  if (!xn || !w_qkv || !rows || !count || !cos || !sin || !q_buf || !kv_buf)
+    return fail(SF_ERR_ARG, "null pointer");
+  GemmArgs a{};
+  a.dtype = dtype;
+  a.X = xn;
+  a.W = w_qkv;
+  a.n_out = (H + 2 * Hkv) * hd;
+  a.K = D;
+  a.rows_cap = bucket;
+  a.count = count;
+  a.epi.kind = EPI_QKV;
+  a.epi.out = q_buf;
+  a.epi.out2 = kv_buf;
+  a.epi.bias = b_qkv;
+  a.epi.cos = cos;
+  a.epi.sin = sin;
+  a.epi.q_scale = q_scale;
+  a.epi.rows = rows;
+  a.epi.q_dim = H * hd;
+  a.epi.kv_dim = Hkv * hd;
+  a.epi.hd = hd;
+  a.epi.N = N;
+  a.ws = ws;
+  a.ws_bytes = ws_bytes;
+  a.err = err;
+  return run_gemm(a, stream, "qkv");
+}
+
+int sf_flash_attn_gqa(int dtype, const void* q_buf, const void* prefix_k, const void* prefix_v,
+                      int64_t kv_head_stride, const void* kv_buf, const int64_t* src,
+                      const int64_t* rows, const int32_t* count, void* O_tab, float* M_tab,
+                      float* Z_tab, int P, int N, float scale, int bucket, int B1, int H,
+                      int Hkv, int hd, int* err, void* stream) {
+  int s = check_dims(dtype, 64, hd, H, Hkv);
+  if (s) return s;
+  if (P < 0 || (P > 0 && (!prefix_k || !prefix_v)) || !q_buf || !kv_buf || !src || !rows ||
+      !count || !O_tab || !M_tab || !Z_tab || N < 1 || bucket < 1 || B1 < 1 || bucket > B1 * N)
+    return fail(SF_ERR_ARG, "bad attention arguments");
+  if (P > 0 && kv_head_stride < static_cast<int64_t>(P) * hd)
+    return fail(SF_ERR_ARG, "kv_head_stride %lld < P*hd", static_cast<long long>(kv_head_stride));
+  AttnParams p{};
+  p.q_buf = q_buf;
+  p.pk = prefix_k;
+  p.pv = prefix_v;
+  p.kv_head_stride = kv_head_stride;
+  p.kv_buf = kv_buf;
+  p.src = src;
+  p.rows = rows;
+  p.count = count;
+  p.O = O_tab;
+  p.M = M_tab;
+  p.Z = Z_tab;
+  p.P = P;
+  p.N = N;
+  p.bucket = bucket;
+  p.H = H;
+  p.Hkv = Hkv;
+  p.hd = hd;
+  p.B1 = B1;
+  p.scale = scale;
+  p.err = err;
+  return cuda_status(launch_attention(dtype, p, S(stream)), "attention");
+}
+
+int sf_chain_correction_gqa(int dtype, const void* q_buf, const void* kv_buf,
+                            const int64_t* src, const int64_t* par_idx, const int8_t* rec,
+                            const int64_t* seg, const int32_t* segcnt, void* O_tab,
+                            float* M_tab, float* Z_tab, int B1, int N, float scale, int H,
+                            int Hkv, int hd, int* err, void* stream) {
+  int s = check_dims(dtype, 64, hd, H, Hkv);
+  if (s) return s;
+  if (!q_buf || !kv_buf || !src || !par_idx || !rec || !seg || !segcnt || !O_tab || !M_tab ||
+      !Z_tab || B1 < 1 || N < 1)
+    return fail(SF_ERR_ARG, "bad merge arguments");
+  MergeParams p{};
+  p.q_buf = q_buf;
+  p.kv_buf = kv_buf;
+  p.src = src;
+  p.par_idx = par_idx;
+  p.rec = rec;
+  p.seg = seg;
+  p.segcnt = segcnt;
+  p.O = O_tab;
+  p.M = M_tab;
+  p.Z = Z_tab;
+  p.B1 = B1;
+  p.N = N;
+  p.H = H;
+  p.Hkv = Hkv;
+  p.hd = hd;
+  p.scale = scale;
+  p.err = err;
+  return cuda_status(launch_merge(dtype, p, S(stream)), "chain correction");
+}
+
+int sf_o_proj_residual(int dtype, const void* Hf, const void* O_tab, const void* w_o, void* hp,
+                       int BN, int D, int q_dim, void* ws, size_t ws_bytes, int* err,
+                       void* stream) {
+  if (!dtype_ok(dtype) || !Hf || !O_tab || !w_o || !hp || BN < 1 || D % 64 || q_dim % 64)
+    return fail(SF_ERR_ARG, "bad o_proj arguments");
+  GemmArgs a{};
+  a.dtype = dtype;
+  a.X = O_tab;
+  a.W = w_o;
+  a.n_out = D;
+  a.K = q_dim;
+  a.rows_cap = BN;
+  a.epi.kind = EPI_RESID;
+  a.epi.out = hp;
+  a.epi.resid = Hf;
+  a.epi.ld_out = D;
+  a.ws = ws;
+  a.ws_bytes = ws_bytes;
+  a.err = err;
+  return run_gemm(a, stream, "o_proj");
+}
+
+int sf_fused_ffn_scatter(int dtype, const void* hp_all, const void* ln_w, const void* w_gate,
+                         const void* w_up, const void* w_down, const int64_t* rows,
+                         const int32_t* count, void* ffn_buf, int bucket, void* act_buf,
+                         void* xn_buf, float* rstd_buf, float eps, int D, int I, void* ws,
+                         size_t ws_bytes, int* err, void* stream) {
+  if (!dtype_ok(dtype) || !hp_all || !ln_w || !w_gate || !w_up || !w_down || !rows || !count ||
+      !ffn_buf || !act_buf || !xn_buf || D % 64 || I % 64 || bucket < 1)
+    return fail(SF_ERR_ARG, "bad ffn arguments");
+  RmsRowsParams r{};
+  r.x = hp_all;
+  r.rows = rows;
+  r.count = count;
+  r.n = bucket;
+  r.n_src = INT64_MAX;
+  r.w = ln_w;
+  r.out = xn_buf;
+  r.rstd = rstd_buf;
+  r.D = D;
+  r.eps = eps;
+  r.err = err;
+  int s = cuda_status(launch_rmsnorm_rows(dtype, r, S(stream)), "ffn norm");
+  if (s) return s;
+  GemmArgs a{};
+  a.dtype = dtype;
+  a.X = xn_buf;
+  a.W = w_gate;
+  a.W2 = w_up;
+  a.n_out = 2 * I;
+  a.K = D;
+  a.rows_cap = bucket;
+  a.count = count;
+  a.epi.kind = EPI_SWIGLU;
+  a.epi.out = act_buf;
+  a.epi.inter = I;
+  a.ws = ws;
+  a.ws_bytes = ws_bytes;
+  a.err = err;
+  s = run_gemm(a, stream, "gate/up");
+  if (s) return s;
+  GemmArgs d{};
+  d.dtype = dtype;
+  d.X = act_buf;
+  d.W = w_down;
+  d.n_out = D;
+  d.K = I;
+  d.rows_cap = bucket;
+  d.count = count;
+  d.epi.kind = EPI_SCATTER;
+  d.epi.out = ffn_buf;
+  d.epi.rows = rows;
+  d.epi.ld_out = D;
+  d.ws = ws;
+  d.ws_bytes = ws_bytes;
+  d.err = err;
+  return run_gemm(d, stream, "down");
+}
+
+int sf_combine(int dtype, const void* hp_all, const void* ffn_buf, const int64_t* src,
+               void* hidden, int B1, int N, int D, int* err, void* stream) {
+  if (!dtype_ok(dtype) || !hp_all || !ffn_buf || !src || !hidden || D % 64)
+    return fail(SF_ERR_ARG, "bad combine arguments");
+  return cuda_status(launch_combine(dtype, hp_all, ffn_buf, src, hidden, B1, N, D, err, S(stream)),
+                     "combine");
+}
+
+int sf_final_norm_lm_head(int dtype, const void* hidden, const void* norm_w, const void* lm_w,
+                          void* logits, void* xn_buf, int B1, int N, int D, int V, float eps,
+                          int shift, void* ws, size_t ws_bytes, int* err, void* stream) {
+  if (!dtype_ok(dtype) || !hidden || !norm_w || !lm_w || !logits || !xn_buf || D % 64 || V < 1)
+    return fail(SF_ERR_ARG, "bad lm_head arguments");
+  const int BN = B1 * N;
+  RmsRowsParams r{};
+  r.x = hidden;
+  r.n = BN;
+  r.n_src = BN;
+  r.w = norm_w;
+  r.out = xn_buf;
+  r.D = D;
+  r.eps = eps;
+  r.err = err;
+  int s = cuda_status(launch_rmsnorm_rows(dtype, r, S(stream)), "final norm");
+  if (s) return s;
+  GemmArgs a{};
+  a.dtype = dtype;
+  a.X = xn_buf;
+  a.W = lm_w;
+  a.n_out = V;
+  a.K = D;
+  a.rows_cap = BN;
+  a.epi.kind = EPI_LOGITS;
+  a.epi.out = logits;
+  a.epi.ld_out = V;
+  a.epi.N = N;
+  a.epi.shift = shift;
+  a.ws = ws;
+  a.ws_bytes = ws_bytes;
+  a.err = err;
+  return run_gemm(a, stream, "lm_head");
+}
+
+int sf_kv_append(int dtype, void* cache_k, void* cache_v, int64_t cache_head_stride,
+                 const void* new_k, const void* new_v, int64_t new_head_stride, int Hkv, int hd,
+                 int P, int n_new, void* stream) {
+  if (!dtype_ok(dtype) || !cache_k || !cache_v || !new_k || !new_v || Hkv < 1 || P < 0 ||
+      n_new < 0)
+    return fail(SF_ERR_ARG, "bad kv_append arguments");
+  const int vec = dtype == SF_DTYPE_BF16 ? 8 : 4;
+  if (hd % vec || cache_head_stride % vec || new_head_stride % vec || !aligned16(cache_k) ||
+      !aligned16(cache_v) || !aligned16(new_k) || !aligned16(new_v))
+    return fail(SF_ERR_ARG, "kv_append needs 16-byte aligned rows");
+  if (cache_head_stride < static_cast<int64_t>(P + n_new) * hd)
+    return fail(SF_ERR_ARG, "cache capacity %lld < (P + n) * hd",
+                static_cast<long long>(cache_head_stride));
+  if (new_head_stride < static_cast<int64_t>(n_new) * hd)
+    return fail(SF_ERR_ARG, "new_head_stride too small");
+  return cuda_status(launch_kv_append(dtype, cache_k, cache_v, cache_head_stride, new_k, new_v,
+                                      new_head_stride, Hkv, hd, P, n_new, S(stream)),
+                     "kv_append");
+}
+
+size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
+                                 int V) {
+  return carve_forward(nullptr, dtype, B1, N, D, H, Hkv, hd, I, V, B1 * N).total + 256;
+}
+
+int sf_folded_verify_forward(const sf_verify_args* a) {
+  if (!a) return fail(SF_ERR_ARG, "null args");
+  const int dtype = a->dtype;
+  int s = check_dims(dtype, a->D, a->hd, a->H, a->Hkv);
+  if (s) return s;
+  const int B1 = a->B1, N = a->N, D = a->D, H = a->H, Hkv = a->Hkv, hd = a->hd, I = a->I,
+            V = a->V, L = a->L;
+  const int BN = B1 * N;
+  if (B1 < 1 || B1 > kMaxBranches || N < 1 || BN > kMaxRows || L < 1 || I % 64 || V < 1)
+    return fail(SF_ERR_ARG, "shape B1=%d N=%d L=%d I=%d V=%d unsupported", B1, N, L, I, V);
+  const int bucket = a->bucket;
+  if (bucket < 1 || bucket > BN) return fail(SF_ERR_ARG, "bucket %d outside [1, %d]", bucket, BN);
+  if (static_cast<size_t>(B1) * D * esize(dtype) > static_cast<size_t>(kMaxGateSmem))
+    return fail(SF_ERR_ARG, "B1*D too large for the gate");
+  if (!a->layers || !a->final_norm_w || !a->lm_w || !a->par_idx || !a->hidden_in || !a->cos ||
+      !a->sin || !a->logits || !a->count_slab || !a->segcnt_slab || !a->ws)
+    return fail(SF_ERR_ARG, "null pointer in verify args");
+  if (a->P < 0 || (a->P > 0 && a->kv_head_stride < static_cast<int64_t>(a->P) * hd))
+    return fail(SF_ERR_ARG, "prefix length / stride mismatch");
+  FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket);
+  if (b.total > a->ws_bytes)
+    return fail(SF_ERR_WORKSPACE, "workspace %zu < %zu bytes", a->ws_bytes, b.total);
+  cudaStream_t st = S(a->stream);
+  const int qd = H * hd, kvd = Hkv * hd;
+  // split-K tile counters (first 16 KB of the GEMM scratch) start at zero
+  if (b.gemm_ws_bytes > 0) {
+    s = cuda_status(cudaMemsetAsync(b.gemm_ws, 0, std::min<size_t>(b.gemm_ws_bytes, 16384), st),
+                    "memset");
+    if (s) return s;
+  }
+  s = cuda_status(cudaMemsetAsync(a->count_slab, 0, sizeof(int32_t) * L, st), "memset");
+  if (s) return s;
+
+  for (int li = 0; li < L; ++li) {
+    const sf_layer& ly = a->layers[li];
+    if (!ly.w_qkv || !ly.ln1_w || !ly.w_o || !ly.ln2_w || !ly.w_gate || !ly.w_up || !ly.w_down ||
+        (a->P > 0 && (!ly.prefix_k || !ly.prefix_v)))
+      return fail(SF_ERR_ARG, "layer %d: null weight", li);
+    const void* Hf = li == 0 ? a->hidden_in : b.hbuf;
+    int8_t* rec = a->rec_slab ? a->rec_slab + static_cast<int64_t>(li) * BN : b.rec;
+    int32_t* count = a->count_slab + li;
+    int32_t* segcnt = a->segcnt_slab + static_cast<int64_t>(li) * B1;
+
+    GateRowsParams g{};
+    g.hp = li == 0 ? nullptr : b.hp;
+    g.ffn = b.ffn;
+    g.src = b.src;
+    g.hidden = const_cast<void*>(Hf);
+    g.par_idx = a->par_idx;
+    g.rstd = b.rstd;
+    g.rec = rec;
+    g.f = b.f;
+    g.delta = a->delta;
+    g.eps = a->eps;
+    g.B1 = B1;
+    g.N = N;
+    g.D = D;
+    g.err = a->err;
+    if ((s = cuda_status(launch_gate_rows(dtype, g, st), "gate"))) return s;
+
+    CompactParams c{};
+    c.rec = rec;
+    c.f = b.f;
+    c.rows = b.rows;
+    c.count = count;
+    c.seg = b.seg;
+    c.segcnt = segcnt;
+    c.src = b.src;
+    c.hidden = Hf;
+    c.rstd = b.rstd;
+    c.ln_w = ly.ln1_w;
+    c.xn = b.xn;
+    c.B1 = B1;
+    c.N = N;
+    c.D = D;
+    c.bucket = bucket;
+    c.err = a->err;
+    if ((s = cuda_status(launch_compact(dtype, c, st), "compact"))) return s;
+
+    GemmArgs q{};
+    q.dtype = dtype;
+    q.X = b.xn;
+    q.W = ly.w_qkv;
+    q.n_out = qd + 2 * kvd;
+    q.K = D;
+    q.rows_cap = bucket;
+    q.count = count;
+    q.epi.kind = EPI_QKV;
+    q.epi.out = b.q_buf;
+    q.epi.out2 = b.kv_buf;
+    q.epi.bias = ly.b_qkv;
+    q.epi.cos = a->cos;
+    q.epi.sin = a->sin;
+    q.epi.q_scale = a->q_scale;
+    q.epi.rows = b.rows;
+    q.epi.q_dim = qd;
+    q.epi.kv_dim = kvd;
+    q.epi.hd = hd;
+    q.epi.N = N;
+    q.ws = b.gemm_ws;
+    q.ws_bytes = b.gemm_ws_bytes;
+    q.err = a->err;
+    if ((s = run_gemm(q, a->stream, "qkv"))) return s;
+
+    AttnParams at{};
+    at.q_buf = b.q_buf;
+    at.pk = ly.prefix_k;
+    at.pv = ly.prefix_v;
+    at.kv_head_stride = a->kv_head_stride;
+    at.kv_buf = b.kv_buf;
+    at.src = b.src;
+    at.rows = b.rows;
+    at.count = count;
+    at.O = b.O;
+    at.M = b.M;
+    at.Z = b.Z;
+    at.P = a->P;
+    at.N = N;
+    at.bucket = bucket;
+    at.H = H;
+    at.Hkv = Hkv;
+    at.hd = hd;
+    at.B1 = B1;
+    at.scale = a->scale;
+    at.err = a->err;
+    if ((s = cuda_status(launch_attention(dtype, at, st), "attention"))) return s;
+
+    MergeParams m{};
+    m.q_buf = b.q_buf;
+    m.kv_buf = b.kv_buf;
+    m.src = b.src;
+    m.par_idx = a->par_idx;
+    m.rec = rec;
+    m.seg = b.seg;
+    m.segcnt = segcnt;
+    m.O = b.O;
+    m.M = b.M;
+    m.Z = b.Z;
+    m.B1 = B1;
+    m.N = N;
+    m.H = H;
+    m.Hkv = Hkv;
+    m.hd = hd;
+    m.scale = a->scale;
+    m.err = a->err;
+    if ((s = cuda_status(launch_merge(dtype, m, st), "merge"))) return s;
+
+    GemmArgs o{};
+    o.dtype = dtype;
+    o.X = b.O;
+    o.W = ly.w_o;
+    o.n_out = D;
+    o.K = qd;
+    o.rows_cap = BN;
+    o.epi.kind = EPI_RESID;
+    o.epi.out = b.hp;
+    o.epi.resid = Hf;
+    o.epi.ld_out = D;
+    o.ws = b.gemm_ws;
+    o.ws_bytes = b.gemm_ws_bytes;
+    o.err = a->err;
+    if ((s = run_gemm(o, a->stream, "o_proj"))) return s;
+
+    RmsRowsParams r{};
+    r.x = b.hp;
+    r.rows = b.rows;
+    r.count = count;
+    r.n = bucket;
+    r.n_src = BN;
+    r.w = ly.ln2_w;
+    r.out = b.xn;
+    r.rstd = b.rstd2;
+    r.D = D;
+    r.eps = a->eps;
+    r.err = a->err;
+    if ((s = cuda_status(launch_rmsnorm_rows(dtype, r, st), "ffn norm"))) return s;
+
+    GemmArgs gu{};
+    gu.dtype = dtype;
+    gu.X = b.xn;
+    gu.W = ly.w_gate;
+    gu.W2 = ly.w_up;
+    gu.n_out = 2 * I;
+    gu.K = D;
+    gu.rows_cap = bucket;
+    gu.count = count;
+    gu.epi.kind = EPI_SWIGLU;
+    gu.epi.out = b.act;
+    gu.epi.inter = I;
+    gu.ws = b.gemm_ws;
+    gu.ws_bytes = b.gemm_ws_bytes;
+    gu.err = a->err;
+    if ((s = run_gemm(gu, a->stream, "gate/up"))) return s;
+
+    GemmArgs dn{};
+    dn.dtype = dtype;
+    dn.X = b.act;
+    dn.W = ly.w_down;
+    dn.n_out = D;
+    dn.K = I;
+    dn.rows_cap = bucket;
+    dn.count = count;
+    dn.epi.kind = EPI_SCATTER;
+    dn.epi.out = b.ffn;
+    dn.epi.rows = b.rows;
+    dn.epi.ld_out = D;
+    dn.ws = b.gemm_ws;
+    dn.ws_bytes = b.gemm_ws_bytes;
+    dn.err = a->err;
+    if ((s = run_gemm(dn, a->stream, "down"))) return s;
+  }
+  // last layer's combine, final norm, lm_head
+  if ((s = cuda_status(launch_combine(dtype, b.hp, b.ffn, b.src, b.hbuf, B1, N, D, a->err, st),
+                       "combine")))
+    return s;
+  RmsRowsParams r{};
+  r.x = b.hbuf;
+  r.n = BN;
+  r.n_src = BN;
+  r.w = a->final_norm_w;
+  r.out = b.xn;
+  r.D = D;
+  r.eps = a->eps;
+  r.err = a->err;
+  if ((s = cuda_status(launch_rmsnorm_rows(dtype, r, st), "final norm"))) return s;
+  GemmArgs lm{};
+  lm.dtype = dtype;
+  lm.X = b.xn;
+  lm.W = a->lm_w;
+  lm.n_out = V;
+  lm.K = D;
+  lm.rows_cap = BN;
+  lm.epi.kind = EPI_LOGITS;
+  lm.epi.out = a->logits;
+  lm.epi.ld_out = V;
+  lm.epi.N = N;
+  lm.epi.shift = a->shift_logits;
+  lm.ws = b.gemm_ws;
+  lm.ws_bytes = b.gemm_ws_bytes;
+  lm.err = a->err;
+  return run_gemm(lm, a->stream, "lm_head");
+}
+
+}  // extern "C"

@@ -1,0 +1,152 @@
+// Internal launcher interface shared by the .cu files of the library.
+#pragma once
+
+#include "sf_common.cuh"
+
+namespace sf {
+
+constexpr int kMaxBranches = 32;         // B1 limit (one warp per branch in the gate)
+constexpr int kMaxRows = 1024;           // B1*N limit of the compaction scan
+constexpr int kMaxGateSmem = 227 * 1024;
+
+struct GateRowsParams {
+  const void* hp;          // combine input (nullptr: gate on `hidden` as is)
+  const void* ffn;         // [BN+1, D]
+  const int64_t* src;      // previous layer's src (combine)
+  void* hidden;            // [BN, D] read, or written by the combine
+  const int64_t* par_idx;  // [B1]
+  float* rstd;             // [BN] or nullptr
+  int8_t* rec;             // [BN] (nullptr: combine + rstd only)
+  int64_t* f;              // [BN]
+  float delta, eps;
+  int B1, N, D;
+  int* err;
+};
+
+struct CompactParams {
+  const int8_t* rec;
+  const int64_t* f;
+  int64_t* rows;           // [bucket]
+  int32_t* count;          // [1]
+  int64_t* seg;            // [BN]
+  int32_t* segcnt;         // [B1]
+  int64_t* src;            // [BN]
+  const void* hidden;      // [BN, D] gate input (for xn)
+  const float* rstd;       // [BN]
+  const void* ln_w;        // [D]
+  void* xn;                // [bucket, D] or nullptr
+  int B1, N, D, bucket;
+  int* err;
+};
+
+struct RmsRowsParams {
+  const void* x;           // [n_src, D]
+  const int64_t* rows;     // gather index or nullptr
+  const int32_t* count;    // device row count or nullptr
+  int n;                   // rows to produce (upper bound)
+  int64_t n_src;           // rows in x
+  const void* w;           // [D]
+  void* out;               // [n, D]
+  float* rstd;             // [n] or nullptr
+  int D;
+  float eps;
+  int* err;
+};
+
+cudaError_t launch_gate_rows(int dtype, const GateRowsParams& p, cudaStream_t st);
+cudaError_t launch_compact(int dtype, const CompactParams& p, cudaStream_t st);
+cudaError_t launch_src_resolve(const int64_t* f, int64_t* src, int B1, int N, int* err,
+                               cudaStream_t st);
+cudaError_t launch_rmsnorm_rows(int dtype, const RmsRowsParams& p, cudaStream_t st);
+cudaError_t launch_combine(int dtype, const void* hp, const void* ffn, const int64_t* src,
+                           void* hidden, int B1, int N, int D, int* err, cudaStream_t st);
+
+// ------------------------------------------------------------------ GEMM + epilogues
+// out-features f in [0, n_out), activation rows j in [0, rows): acc[j][f] =
+// sum_k X[j][k] * W[f][k]; the epilogue turns acc into the layer output.
+enum EpiKind : int {
+  EPI_RAW = 0,       // ws fp32 [rows][n_out] (tests)
+  EPI_QKV = 1,       // + bias, RoPE on q/k, q scale, scatter to q_buf / kv_buf at rows[j]
+  EPI_RESID = 2,     // out[j][f] = T(resid[j][f] + T(acc))
+  EPI_SWIGLU = 3,    // W = [Wg; Wu] (n_out = 2I): act[j][f] = T(T(silu(T(g))) * T(u))
+  EPI_SCATTER = 4,   // out[rows[j]][f] = T(acc)
+  EPI_LOGITS = 5,    // logits[b][n'][f] with the Fast-dLLM shift when shift != 0
+};
+
+struct EpiParams {
+  int kind;
+  void* out;               // q_buf / hp / act / ffn_buf / logits / raw fp32
+  void* out2;              // kv_buf
+  const void* resid;       // EPI_RESID
+  const void* bias;        // EPI_QKV (nullable)
+  const void* cos;         // [N, hd]
+  const void* sin;
+  const float* q_scale;    // [N] nullable
+  const int64_t* rows;     // row index map (QKV / SCATTER)
+  int ld_out;              // leading dimension of `out` (elements)
+  int q_dim, kv_dim, hd, N;
+  int inter;               // SWIGLU: I
+  int shift;               // LOGITS
+};
+
+struct GemmArgs {
+  int dtype;
+  const void* X;           // [rows_cap, K] activations (row-major)
+  const void* W;           // [n_out, K] weights (row-major); SWIGLU: gate half
+  const void* W2;          // SWIGLU: up half [I, K]
+  int n_out, K;
+  int rows_cap;            // static bound on rows (allocation of X)
+  const int32_t* count;    // device row count (nullptr: rows_cap rows)
+  EpiParams epi;
+  void* ws;
+  size_t ws_bytes;
+  int* err;
+};
+
+size_t gemm_ws_need(int dtype, int rows_cap, int n_out, int K, int kind, int inter);
+cudaError_t gemm_simt_bf16(const GemmArgs& a, cudaStream_t st);
+cudaError_t gemm(const GemmArgs& a, cudaStream_t st);
+int gemm_path_is_tc(int dtype);
+
+// ------------------------------------------------------------------ attention
+struct AttnParams {
+  const void* q_buf;       // [BN+1, H*hd]
+  const void* pk;          // [Hkv, .., hd] prefix keys (head stride kv_head_stride)
+  const void* pv;
+  int64_t kv_head_stride;
+  const void* kv_buf;      // [BN+1, 2*Hkv*hd]
+  const int64_t* src;      // [BN]
+  const int64_t* rows;     // [bucket]
+  const int32_t* count;
+  void* O;                 // [BN, H*hd]
+  float* M;                // [BN, H]
+  float* Z;
+  int P, N, bucket, H, Hkv, hd, B1;
+  float scale;
+  int* err;
+};
+cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st);
+cudaError_t launch_attention_simt(int dtype, const AttnParams& p, cudaStream_t st);
+
+struct MergeParams {
+  const void* q_buf;
+  const void* kv_buf;
+  const int64_t* src;
+  const int64_t* par_idx;
+  const int8_t* rec;
+  const int64_t* seg;
+  const int32_t* segcnt;
+  void* O;
+  float* M;
+  float* Z;
+  int B1, N, H, Hkv, hd;
+  float scale;
+  int* err;
+};
+cudaError_t launch_merge(int dtype, const MergeParams& p, cudaStream_t st);
+
+cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, const void* nk,
+                             const void* nv, int64_t n_stride, int Hkv, int hd, int P, int n,
+                             cudaStream_t st);
+
+}  // namespace sf

@@ -1,0 +1,280 @@
+"""Drop-in B200 replacements for the reference's fused SpecFold generators.
+
+``SpecFoldTritonFastDLLMV2Generation`` (specfold/generate/fastdllm_v2_folded.py:226-370)
+and ``SpecFoldTritonNLDGeneration`` (specfold/generate/nld_folded.py:244-394) override
+one method, ``_batched_block_forward(batched_input [B1, N] int64, past_key_values) ->
+logits [B1, N, V]``, the seam the Spiffy decoding loop calls
+(fastdllm_v2_generation.py:634, nld_generation.py:247).  The classes here keep that
+method, its helpers (``_build_parent_map``, ``_pack_layer_weights``, ``fold_ratio``,
+``delta``, ``fold_bucket``) and their meaning, and run the layer loop as one call into
+libspecfold_b200 (hand-written sm_100a kernels).  There is no Triton and no fallback to
+a PyTorch or CPU path: a missing library or a device error raises.
+
+Host-side work kept in Python, as in the reference: the parent map (one host sync),
+the embedding lookup and RoPE tables (the model's own modules), and the fold counters
+(a second small sync that also carries the device error word).
+
+To use them inside the reference's decoding loop, mix ``FoldedVerifyB200`` in front of
+the reference's base generator::
+
+    class Gen(SpecFoldB200FastDLLMV2Generation, FastDLLMV2SpeculativeGeneration): ...
+
+Standalone (tests, benchmarks) they need only ``model_executor.model``.
+"""
+
+from __future__ import annotations
+
+import logging
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from . import _lib
+from .kernels import dtype_code
+
+logger = logging.getLogger(__name__)
+
+
+class FoldedVerifyB200:
+    """Shared implementation; subclasses fix the model family."""
+
+    family = "fastdllm"
+    _packed_weights = None
+
+    def __init__(self, *args, delta: float = 0.1, fold_bucket: Optional[int] = None, **kwargs):
+        mro = type(self).__mro__
+        if mro[mro.index(FoldedVerifyB200) + 1] is object:
+            # standalone: only the executor is needed (positional or keyword)
+            self.model_executor = kwargs.pop("model_executor", args[0] if args else None)
+        else:
+            # mixed in front of a reference generator: its __init__ takes the rest
+            super().__init__(*args, **kwargs)
+        self.delta = float(delta)
+        # None: the compaction bucket is B1*N (every row fits); an int caps it
+        # (fastdllm_v2_folded.py:230-235)
+        self.fold_bucket = None if fold_bucket is None else int(fold_bucket)
+        self._fold_stats: List[dict] = []
+        self._ws: Dict[Tuple, torch.Tensor] = {}
+        self.last_rec_masks: Optional[torch.Tensor] = None
+        self.record_masks = False
+
+    # -------------------------------------------------------------- reference API
+    @property
+    def fold_ratio(self):
+        """1 - recomputed / draft positions over all calls (fastdllm_v2_folded.py:49-53)."""
+        tot = getattr(self, "_fold_draft_positions", 0)
+        rec = getattr(self, "_fold_draft_recomputed", 0)
+        return 1.0 - rec / tot if tot else float("nan")
+
+    @staticmethod
+    def _build_parent_map(batched_input: torch.Tensor) -> Tuple[List[Optional[int]], List[int]]:
+        """par(i): the first branch whose differing-position set (vs the main block) is a
+        one-smaller subset of draft i's, else main (0); one device->host sync
+        (fastdllm_v2_folded.py:55-75)."""
+        B1 = batched_input.shape[0]
+        differs = batched_input != batched_input[0:1]
+        escapes = (differs.unsqueeze(0) & ~differs.unsqueeze(1)).any(-1)
+        both = torch.cat([differs.sum(1, dtype=torch.int64).unsqueeze(1),
+                          escapes.to(torch.int64)], dim=1).tolist()
+        counts = [row[0] for row in both]
+        parent: List[Optional[int]] = [None] + [0] * (B1 - 1)
+        for i in range(1, B1):
+            for j in range(B1):
+                if j != i and counts[j] == counts[i] - 1 and not both[i][1 + j]:
+                    parent[i] = j
+                    break
+        return parent, counts
+
+    def _base(self):
+        m = self.model_executor.model
+        return m.encoder if self.family == "nld" else m.model
+
+    def _head(self):
+        m = self.model_executor.model
+        return m.diffusion_head if self.family == "nld" else m.lm_head
+
+    def _pack_layer_weights(self, layers) -> None:
+        """Per layer: [Wq; Wk; Wv] and its bias packed once (one weight stream for the
+        QKV projection, fastdllm_v2_folded.py:77-87); gate and up stay separate tensors
+        (the kernel reads both per tile), so only the QKV packing copies weights."""
+        packed = []
+        for lyr in layers:
+            a, mlp = lyr.self_attn, lyr.mlp
+            w_qkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous()
+            if a.q_proj.bias is not None:
+                b_qkv = torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0).contiguous()
+            else:
+                b_qkv = None   # NLD: no bias (nld_folded.py:92-102 packs zeros)
+            ws = (w_qkv, b_qkv, lyr.input_layernorm.weight.contiguous(),
+                  a.o_proj.weight.contiguous(), lyr.post_attention_layernorm.weight.contiguous(),
+                  mlp.gate_proj.weight.contiguous(), mlp.up_proj.weight.contiguous(),
+                  mlp.down_proj.weight.contiguous())
+            packed.append(ws)
+        self._packed_weights = packed
+        self._layer_structs = None
+
+    def _shift_logits(self, logits: torch.Tensor) -> torch.Tensor:
+        return torch.cat([logits[:, :1, :], logits[:, :-1, :]], dim=1)
+
+    # -------------------------------------------------------------- the seam
+    @torch.no_grad()
+    def _batched_block_forward(self, batched_input: torch.Tensor, past_key_values) -> torch.Tensor:
+        B1, N = batched_input.shape
+        bucket = B1 * N if self.fold_bucket is None else max(1, min(self.fold_bucket, B1 * N))
+        logits, stats = self._run(batched_input, past_key_values, bucket)
+        if stats["max_count"] > bucket:
+            # the reference re-runs its PyTorch path on overflow (fastdllm_v2_folded.py:367-369);
+            # here the same kernels run again with room for every row
+            logger.warning("SpecFold bucket overflow (%d > %d); re-running with bucket %d",
+                           stats["max_count"], bucket, B1 * N)
+            logits, stats = self._run(batched_input, past_key_values, B1 * N, count_stats=False)
+        return logits
+
+    def _workspace(self, key, nbytes, device) -> torch.Tensor:
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+    def _run(self, batched_input, past_key_values, bucket, count_stats=True):
+        lib = _lib.load()
+        m_ = self.model_executor.model
+        base = self._base()
+        cfg = m_.config
+        dev = batched_input.device
+        if dev.type != "cuda":
+            raise ValueError("the B200 folded forward runs on CUDA tensors only")
+        layers = base.layers
+        L = len(layers)
+        H, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        hd = layers[0].self_attn.head_dim
+        scale = float(layers[0].self_attn.scaling)
+        B1, N = batched_input.shape
+        BN = B1 * N
+        if self._packed_weights is None:
+            self._pack_layer_weights(layers)
+        P = int(past_key_values.get_seq_length()) if past_key_values is not None else 0
+
+        parent, counts = self._build_parent_map(batched_input)
+        par_idx = torch.tensor([0] + [parent[i] for i in range(1, B1)], dtype=torch.int64,
+                               device=dev)
+        hidden = base.embed_tokens(batched_input)
+        dtype = hidden.dtype
+        D = hidden.shape[-1]
+        pos = torch.arange(P, P + N, device=dev).unsqueeze(0)
+        cos, sin = base.rotary_emb(hidden, pos)
+        cos = cos[0].to(dtype).contiguous()
+        sin = sin[0].to(dtype).contiguous()
+        q_scale = self._q_scale(cfg, P, N, dev)
+        hidden = hidden.reshape(BN, D).contiguous()
+        I = self._packed_weights[0][5].shape[0]
+        head = self._head()
+        lm_w = head.weight.contiguous()
+        V = lm_w.shape[0]
+
+        # per-layer structs: weights cached, prefix pointers refreshed per call
+        layer_arr = (_lib.SfLayer * L)()
+        kv_stride = 0
+        keep = []
+        for li in range(L):
+            w = self._packed_weights[li]
+            st = layer_arr[li]
+            st.w_qkv, st.ln1_w, st.w_o, st.ln2_w = (w[0].data_ptr(), w[2].data_ptr(),
+                                                    w[3].data_ptr(), w[4].data_ptr())
+            st.b_qkv = None if w[1] is None else w[1].data_ptr()
+            st.w_gate, st.w_up, st.w_down = w[5].data_ptr(), w[6].data_ptr(), w[7].data_ptr()
+            if P > 0:
+                k, v = past_key_values[li]
+                k0, v0 = self._prefix_view(k), self._prefix_view(v)
+                keep += [k0, v0]
+                if kv_stride == 0:
+                    kv_stride = k0.stride(0)
+                if k0.stride(0) != kv_stride or v0.stride(0) != kv_stride:
+                    k0, v0 = k0.contiguous(), v0.contiguous()
+                    raise ValueError("prefix cache layers must share one head stride")
+                st.prefix_k, st.prefix_v = k0.data_ptr(), v0.data_ptr()
+
+        need = lib.sf_verify_workspace_bytes(dtype_code(hidden), B1, N, D, H, Hkv, hd, I, V)
+        ws = self._workspace((dev.index, dtype, B1, N), need, dev)
+        logits = torch.empty(B1, N, V, dtype=dtype, device=dev)
+        slab = torch.zeros(L + L * B1 + 1, dtype=torch.int32, device=dev)
+        count_slab, segcnt_slab, err = slab[:L], slab[L:L + L * B1], slab[L + L * B1:]
+        rec_slab = torch.zeros(L * BN, dtype=torch.int8, device=dev) if self.record_masks else None
+
+        args = _lib.SfVerifyArgs()
+        args.dtype = dtype_code(hidden)
+        args.B1, args.N, args.D, args.H, args.Hkv, args.hd = B1, N, D, H, Hkv, hd
+        args.I, args.V, args.L, args.P = I, V, L, P
+        args.kv_head_stride = kv_stride
+        args.bucket = bucket
+        args.delta = self.delta
+        args.eps = float(getattr(cfg, "rms_norm_eps", 1e-6))
+        args.scale = scale
+        args.shift_logits = 1 if self.family == "fastdllm" else 0
+        args.layers = layer_arr
+        args.final_norm_w = base.norm.weight.data_ptr()
+        args.lm_w = lm_w.data_ptr()
+        args.par_idx = par_idx.data_ptr()
+        args.hidden_in = hidden.data_ptr()
+        args.cos, args.sin = cos.data_ptr(), sin.data_ptr()
+        args.q_scale = None if q_scale is None else q_scale.data_ptr()
+        args.logits = logits.data_ptr()
+        args.count_slab = count_slab.data_ptr()
+        args.segcnt_slab = segcnt_slab.data_ptr()
+        args.rec_slab = None if rec_slab is None else rec_slab.data_ptr()
+        args.ws = ws.data_ptr()
+        args.ws_bytes = ws.numel()
+        args.err = err.data_ptr()
+        args.stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(lib.sf_folded_verify_forward(args), "folded verify forward")
+
+        # one sync for the fold counters and the device error word (the reference's :363)
+        mx, sm, bits = torch.stack([count_slab.max(), count_slab.sum(), err[0]]).tolist()
+        if bits:
+            raise _lib.SpecFoldError("folded verify forward: " + _lib.describe_device_error(bits))
+        if count_stats:
+            self._fold_draft_positions = getattr(self, "_fold_draft_positions", 0) + (B1 - 1) * N * L
+            self._fold_draft_recomputed = getattr(self, "_fold_draft_recomputed", 0) + int(sm) - L * N
+        if rec_slab is not None:
+            self.last_rec_masks = rec_slab.view(L, B1, N)
+        del keep
+        return logits, {"max_count": int(mx), "sum_count": int(sm)}
+
+    @staticmethod
+    def _prefix_view(t: torch.Tensor) -> torch.Tensor:
+        """[1, Hkv, P, hd] cache tensor -> [Hkv, P, hd] view with contiguous rows."""
+        t0 = t[0]
+        if t0.stride(2) != 1 or t0.stride(1) != t0.shape[2]:
+            t0 = t0.contiguous()
+        return t0
+
+    def _q_scale(self, cfg, P, N, device):
+        return None
+
+
+class SpecFoldB200FastDLLMV2Generation(FoldedVerifyB200):
+    """Fast-dLLM v2 (Qwen2 backbone): QKV bias, shifted logits
+    (replaces SpecFoldTritonFastDLLMV2Generation)."""
+
+    family = "fastdllm"
+
+
+class SpecFoldB200NLDGeneration(FoldedVerifyB200):
+    """Nemotron-Labs-Diffusion (Ministral3 / Llama backbone): no QKV bias, unshifted
+    logits, llama-4 query scale applied in the QKV epilogue instead of falling back
+    (replaces SpecFoldTritonNLDGeneration, nld_folded.py:244-394)."""
+
+    family = "nld"
+
+    def _q_scale(self, cfg, P, N, device):
+        rp = getattr(cfg, "rope_parameters", None) or {}
+        beta = rp.get("llama_4_scaling_beta")
+        omax = rp.get("original_max_position_embeddings")
+        if beta is None or omax is None:
+            return None
+        pos = torch.arange(P, P + N, device=device, dtype=torch.float32)
+        scale = 1.0 + beta * torch.log(1.0 + torch.floor(pos / omax))
+        if bool((scale == 1.0).all()):
+            return None
+        return scale.contiguous()

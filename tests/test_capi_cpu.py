@@ -1,0 +1,68 @@
+"""The C-ABI library loads without a GPU, exports every function include/specfold_b200.h
+declares, and rejects bad arguments before touching the device."""
+import ctypes
+import os
+import re
+
+import torch
+
+from specfold_b200 import _lib
+from specfold_b200.folded import FoldedVerifyB200
+from oracle import folded_oracle as orc
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "specfold_b200.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sf_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    lib = _lib.load()
+    names = declared()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.exported_symbols(), f"{n} not bound in _lib"
+    # and nothing is bound that the header does not declare
+    assert set(_lib.exported_symbols()) <= set(names)
+
+
+def test_abi_version_and_workspace_sizes():
+    lib = _lib.load()
+    assert lib.sf_abi_version() == 1
+    small = lib.sf_verify_workspace_bytes(1, 8, 32, 256, 4, 2, 64, 384, 128)
+    big = lib.sf_verify_workspace_bytes(1, 8, 32, 3584, 28, 4, 128, 18944, 152064)
+    assert 0 < small < big < (1 << 30)
+
+
+def test_argument_validation_without_device():
+    lib = _lib.load()
+    assert lib.sf_folded_verify_forward(None) == 1
+    assert b"null" in lib.sf_last_error()
+    args = _lib.SfVerifyArgs()
+    args.dtype, args.B1, args.N, args.D, args.H, args.Hkv, args.hd = 1, 8, 32, 100, 4, 2, 64
+    assert lib.sf_folded_verify_forward(ctypes.byref(args)) == 1      # D % 64 != 0
+    assert b"multiple of 64" in lib.sf_last_error()
+    args.D, args.hd = 256, 96
+    assert lib.sf_folded_verify_forward(ctypes.byref(args)) == 1      # head_dim
+    # gate: B1 beyond one warp per branch
+    st = lib.sf_residual_delta_gate(1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, None, None, 0.1, 40, 32,
+                                    256, 256, 1e-6, None, None)
+    assert st == 1
+    assert lib.sf_kv_append(1, 16, 16, 100, 16, 16, 1024, 4, 128, 0, 32, None) == 1  # capacity
+
+
+def test_parent_map_matches_oracle():
+    g = torch.Generator().manual_seed(0)
+    for trial in range(50):
+        B1, N = 8, 12
+        base = torch.randint(0, 5, (N,), generator=g)
+        rows = base.repeat(B1, 1)
+        for i in range(1, B1):
+            k = int(torch.randint(0, 4, (1,), generator=g))
+            pos = torch.randperm(N, generator=g)[:k]
+            rows[i, pos] = torch.randint(5, 9, (k,), generator=g)
+        assert FoldedVerifyB200._build_parent_map(rows) == orc.parent_map(rows)
