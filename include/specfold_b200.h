@@ -198,6 +198,19 @@ typedef struct sf_verify_args {
   void* stream;
 } sf_verify_args;
 
+/* ------------------------------------------------------------------ measurement ----
+ * Kernels launched by this library so far (all host threads).                       */
+long long sf_launch_count(void);
+/* CUDA-event timing of sf_folded_verify_forward's launches, per kernel kind (host-side
+ * events only).  sf_profile_begin(capacity) arms up to `capacity` timed launches on the
+ * calling thread; sf_profile_end() waits for them and sums per kind;
+ * sf_profile_kind(k, &ms, &calls) reads kind k (0 <= k < sf_profile_kinds()).       */
+int sf_profile_begin(int capacity);
+int sf_profile_end(void);
+int sf_profile_kinds(void);
+const char* sf_profile_name(int kind);
+int sf_profile_kind(int kind, double* total_ms, int* calls);
+
 size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
                                  int V);
 int sf_folded_verify_forward(const sf_verify_args* args);

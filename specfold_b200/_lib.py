@@ -79,6 +79,12 @@ _SIGS = {
                                       c_size_t, c_void_p, c_void_p]),
     "sf_kv_append": (c_int, [c_int, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
                              c_int, c_int, c_int, c_int, c_void_p]),
+    "sf_launch_count": (C.c_longlong, []),
+    "sf_profile_begin": (c_int, [c_int]),
+    "sf_profile_end": (c_int, []),
+    "sf_profile_kinds": (c_int, []),
+    "sf_profile_name": (C.c_char_p, [c_int]),
+    "sf_profile_kind": (c_int, [c_int, C.POINTER(C.c_double), C.POINTER(c_int)]),
     "sf_verify_workspace_bytes": (c_size_t, [c_int] * 9),
     "sf_folded_verify_forward": (c_int, [C.POINTER(SfVerifyArgs)]),
 }
@@ -128,3 +134,23 @@ def check(status: int, what: str = "") -> None:
 
 def describe_device_error(bits: int) -> str:
     return ", ".join(v for k, v in DEV_ERR_BITS.items() if bits & k) or f"code {bits}"
+
+
+def profile_begin(capacity: int) -> None:
+    check(load().sf_profile_begin(int(capacity)), "profile_begin")
+
+
+def profile_end() -> dict:
+    """{kind name: (total ms, calls)} of the launches timed since profile_begin."""
+    lib = load()
+    check(lib.sf_profile_end(), "profile_end")
+    out = {}
+    for k in range(lib.sf_profile_kinds()):
+        ms, calls = C.c_double(), c_int()
+        check(lib.sf_profile_kind(k, C.byref(ms), C.byref(calls)), "profile_kind")
+        out[lib.sf_profile_name(k).decode()] = (ms.value, calls.value)
+    return out
+
+
+def launch_count() -> int:
+    return int(load().sf_launch_count())

@@ -229,7 +229,7 @@ static cudaError_t attn_t(const AttnParams& p, cudaStream_t st) {
   if (p.hd == 128) attn_simt_kernel<T, 128><<<grid, 128, 0, st>>>(p);
   else if (p.hd == 64) attn_simt_kernel<T, 64><<<grid, 128, 0, st>>>(p);
   else return cudaErrorInvalidValue;
-  return cudaGetLastError();
+  return launched();
 }
 cudaError_t launch_attention_simt(int dtype, const AttnParams& p, cudaStream_t st) {
   if (p.H % p.Hkv != 0 || p.H / p.Hkv > kMaxGroup) return cudaErrorInvalidValue;
@@ -242,7 +242,7 @@ static cudaError_t merge_t(const MergeParams& p, cudaStream_t st) {
   if (p.hd == 128) merge_kernel<T, 128><<<grid, 128, 0, st>>>(p);
   else if (p.hd == 64) merge_kernel<T, 64><<<grid, 128, 0, st>>>(p);
   else return cudaErrorInvalidValue;
-  return cudaGetLastError();
+  return launched();
 }
 cudaError_t launch_merge(int dtype, const MergeParams& p, cudaStream_t st) {
   if (p.H % p.Hkv != 0) return cudaErrorInvalidValue;
@@ -266,7 +266,7 @@ cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, co
     kv_append_kernel<float><<<blocks, 256, 0, st>>>(
         static_cast<float*>(ck), static_cast<float*>(cv), c_stride, static_cast<const float*>(nk),
         static_cast<const float*>(nv), n_stride, Hkv, hd, P, n);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st) {

@@ -2,12 +2,19 @@
 // the whole-forward layer loop.
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <string>
+#include <vector>
 
 #include "../../include/specfold_b200.h"
 #include "sf_kernels.cuh"
 
 using namespace sf;
+
+namespace sf {
+static std::atomic<long long> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+}  // namespace sf
 
 namespace {
 
@@ -51,6 +58,52 @@ size_t ws_gemm(int dtype, int rows, int n_out, int K, int kind, int inter) {
 }
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// ---------------------------------------------------------------- profiling
+// CUDA-event timing of the forward's launches, per kernel kind.  Host-side events
+// only; one host thread at a time.
+enum ProfKind {
+  K_GATE = 0, K_COMPACT, K_QKV, K_ATTN, K_MERGE, K_OPROJ, K_FFN_NORM, K_GATEUP, K_DOWN,
+  K_COMBINE, K_FINAL_NORM, K_LM_HEAD, K_NUM
+};
+const char* kProfNames[K_NUM] = {"gate", "compact", "qkv", "attention", "merge", "o_proj",
+                                 "ffn_norm", "gate_up", "down", "combine", "final_norm",
+                                 "lm_head"};
+struct Profiler {
+  bool on = false;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> kind;
+  int used = 0, dropped = 0;
+  double total_ms[K_NUM] = {};
+  int calls[K_NUM] = {};
+};
+Profiler g_prof;
+
+void prof_mark(int kind, cudaStream_t st, bool start) {
+  if (!g_prof.on) return;
+  if (start) {
+    if (2 * (g_prof.used + 1) > static_cast<int>(g_prof.ev.size())) {
+      ++g_prof.dropped;
+      g_prof.kind.push_back(-1);
+      return;
+    }
+    cudaEventRecord(g_prof.ev[2 * g_prof.used], st);
+  } else {
+    if (2 * (g_prof.used + 1) > static_cast<int>(g_prof.ev.size())) return;
+    cudaEventRecord(g_prof.ev[2 * g_prof.used + 1], st);
+    if (static_cast<int>(g_prof.kind.size()) <= g_prof.used) g_prof.kind.resize(g_prof.used + 1);
+    g_prof.kind[g_prof.used] = kind;
+    ++g_prof.used;
+  }
+}
+
+template <typename F>
+int timed(int kind, cudaStream_t st, F&& fn) {
+  prof_mark(kind, st, true);
+  const int r = fn();
+  prof_mark(kind, st, false);
+  return r;
+}
 
 // Carves the forward's scratch out of one buffer.
 struct Carve {
@@ -519,7 +572,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     g.N = N;
     g.D = D;
     g.err = a->err;
-    if ((s = cuda_status(launch_gate_rows(dtype, g, st), "gate"))) return s;
+    if ((s = timed(K_GATE, st, [&] { return cuda_status(launch_gate_rows(dtype, g, st), "gate"); })))
+      return s;
 
     CompactParams c{};
     c.rec = rec;
@@ -538,7 +592,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     c.D = D;
     c.bucket = bucket;
     c.err = a->err;
-    if ((s = cuda_status(launch_compact(dtype, c, st), "compact"))) return s;
+    if ((s = timed(K_COMPACT, st, [&] { return cuda_status(launch_compact(dtype, c, st), "compact"); })))
+      return s;
 
     GemmArgs q{};
     q.dtype = dtype;
@@ -563,7 +618,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     q.ws = b.gemm_ws;
     q.ws_bytes = b.gemm_ws_bytes;
     q.err = a->err;
-    if ((s = run_gemm(q, a->stream, "qkv"))) return s;
+    if ((s = timed(K_QKV, st, [&] { return run_gemm(q, a->stream, "qkv"); }))) return s;
 
     AttnParams at{};
     at.q_buf = b.q_buf;
@@ -586,7 +641,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     at.B1 = B1;
     at.scale = a->scale;
     at.err = a->err;
-    if ((s = cuda_status(launch_attention(dtype, at, st), "attention"))) return s;
+    if ((s = timed(K_ATTN, st, [&] { return cuda_status(launch_attention(dtype, at, st), "attention"); })))
+      return s;
 
     MergeParams m{};
     m.q_buf = b.q_buf;
@@ -606,7 +662,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     m.hd = hd;
     m.scale = a->scale;
     m.err = a->err;
-    if ((s = cuda_status(launch_merge(dtype, m, st), "merge"))) return s;
+    if ((s = timed(K_MERGE, st, [&] { return cuda_status(launch_merge(dtype, m, st), "merge"); })))
+      return s;
 
     GemmArgs o{};
     o.dtype = dtype;
@@ -622,7 +679,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     o.ws = b.gemm_ws;
     o.ws_bytes = b.gemm_ws_bytes;
     o.err = a->err;
-    if ((s = run_gemm(o, a->stream, "o_proj"))) return s;
+    if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, a->stream, "o_proj"); }))) return s;
 
     RmsRowsParams r{};
     r.x = b.hp;
@@ -636,7 +693,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     r.D = D;
     r.eps = a->eps;
     r.err = a->err;
-    if ((s = cuda_status(launch_rmsnorm_rows(dtype, r, st), "ffn norm"))) return s;
+    if ((s = timed(K_FFN_NORM, st, [&] { return cuda_status(launch_rmsnorm_rows(dtype, r, st), "ffn norm"); })))
+      return s;
 
     GemmArgs gu{};
     gu.dtype = dtype;
@@ -653,7 +711,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     gu.ws = b.gemm_ws;
     gu.ws_bytes = b.gemm_ws_bytes;
     gu.err = a->err;
-    if ((s = run_gemm(gu, a->stream, "gate/up"))) return s;
+    if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, a->stream, "gate/up"); }))) return s;
 
     GemmArgs dn{};
     dn.dtype = dtype;
@@ -670,11 +728,13 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     dn.ws = b.gemm_ws;
     dn.ws_bytes = b.gemm_ws_bytes;
     dn.err = a->err;
-    if ((s = run_gemm(dn, a->stream, "down"))) return s;
+    if ((s = timed(K_DOWN, st, [&] { return run_gemm(dn, a->stream, "down"); }))) return s;
   }
   // last layer's combine, final norm, lm_head
-  if ((s = cuda_status(launch_combine(dtype, b.hp, b.ffn, b.src, b.hbuf, B1, N, D, a->err, st),
-                       "combine")))
+  if ((s = timed(K_COMBINE, st, [&] {
+         return cuda_status(launch_combine(dtype, b.hp, b.ffn, b.src, b.hbuf, B1, N, D, a->err, st),
+                            "combine");
+       })))
     return s;
   RmsRowsParams r{};
   r.x = b.hbuf;
@@ -685,7 +745,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   r.D = D;
   r.eps = a->eps;
   r.err = a->err;
-  if ((s = cuda_status(launch_rmsnorm_rows(dtype, r, st), "final norm"))) return s;
+  if ((s = timed(K_FINAL_NORM, st, [&] { return cuda_status(launch_rmsnorm_rows(dtype, r, st), "final norm"); })))
+    return s;
   GemmArgs lm{};
   lm.dtype = dtype;
   lm.X = b.xn;
@@ -701,7 +762,53 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   lm.ws = b.gemm_ws;
   lm.ws_bytes = b.gemm_ws_bytes;
   lm.err = a->err;
-  return run_gemm(lm, a->stream, "lm_head");
+  return timed(K_LM_HEAD, st, [&] { return run_gemm(lm, a->stream, "lm_head"); });
+}
+
+long long sf_launch_count(void) { return sf::g_launches.load(); }
+
+int sf_profile_begin(int capacity) {
+  for (cudaEvent_t e : g_prof.ev) cudaEventDestroy(e);
+  g_prof = Profiler();
+  if (capacity <= 0) return SF_OK;
+  g_prof.ev.resize(2 * static_cast<size_t>(capacity));
+  for (auto& e : g_prof.ev) {
+    cudaError_t r = cudaEventCreate(&e);
+    if (r != cudaSuccess) return cuda_status(r, "cudaEventCreate");
+  }
+  g_prof.on = true;
+  return SF_OK;
+}
+
+int sf_profile_end(void) {
+  g_prof.on = false;
+  for (int i = 0; i < g_prof.used; ++i) {
+    cudaError_t r = cudaEventSynchronize(g_prof.ev[2 * i + 1]);
+    if (r != cudaSuccess) return cuda_status(r, "cudaEventSynchronize");
+    float ms = 0.f;
+    r = cudaEventElapsedTime(&ms, g_prof.ev[2 * i], g_prof.ev[2 * i + 1]);
+    if (r != cudaSuccess) return cuda_status(r, "cudaEventElapsedTime");
+    const int k = g_prof.kind[i];
+    if (k >= 0 && k < K_NUM) {
+      g_prof.total_ms[k] += ms;
+      g_prof.calls[k] += 1;
+    }
+  }
+  if (g_prof.dropped) return fail(SF_ERR_ARG, "profile capacity exceeded (%d launches dropped)", g_prof.dropped);
+  return SF_OK;
+}
+
+int sf_profile_kinds(void) { return K_NUM; }
+
+const char* sf_profile_name(int kind) {
+  return (kind >= 0 && kind < K_NUM) ? kProfNames[kind] : "";
+}
+
+int sf_profile_kind(int kind, double* total_ms, int* calls) {
+  if (kind < 0 || kind >= K_NUM || !total_ms || !calls) return fail(SF_ERR_ARG, "bad profile kind");
+  *total_ms = g_prof.total_ms[kind];
+  *calls = g_prof.calls[kind];
+  return SF_OK;
 }
 
 }  // extern "C"

@@ -287,7 +287,7 @@ static cudaError_t launch_gate_rows_t(const GateRowsParams& p, cudaStream_t st) 
     configured = true;
   }
   gate_rows_kernel<T><<<p.N, 32 * p.B1, smem, st>>>(p);
-  return cudaGetLastError();
+  return launched();
 }
 cudaError_t launch_gate_rows(int dtype, const GateRowsParams& p, cudaStream_t st) {
   return dtype == BF16 ? launch_gate_rows_t<__nv_bfloat16>(p, st) : launch_gate_rows_t<float>(p, st);
@@ -298,14 +298,14 @@ cudaError_t launch_compact(int dtype, const CompactParams& p, cudaStream_t st) {
   const int grid = p.xn ? (BN + 7) / 8 : 1;
   if (dtype == BF16) compact_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
   else compact_kernel<float><<<grid, 256, 0, st>>>(p);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t launch_src_resolve(const int64_t* f, int64_t* src, int B1, int N, int* err,
                                cudaStream_t st) {
   const int BN = B1 * N;
   src_resolve_kernel<<<(BN + 127) / 128, 128, 0, st>>>(f, src, B1, N, err);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t launch_rmsnorm_rows(int dtype, const RmsRowsParams& p, cudaStream_t st) {
@@ -313,7 +313,7 @@ cudaError_t launch_rmsnorm_rows(int dtype, const RmsRowsParams& p, cudaStream_t 
   if (grid == 0) return cudaSuccess;
   if (dtype == BF16) rmsnorm_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
   else rmsnorm_rows_kernel<float><<<grid, 256, 0, st>>>(p);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t launch_combine(int dtype, const void* hp, const void* ffn, const int64_t* src,
@@ -327,7 +327,7 @@ cudaError_t launch_combine(int dtype, const void* hp, const void* ffn, const int
     combine_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(hp),
                                                 static_cast<const float*>(ffn), src,
                                                 static_cast<float*>(hidden), B1, N, D, err);
-  return cudaGetLastError();
+  return launched();
 }
 
 }  // namespace sf

@@ -551,7 +551,7 @@ static cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
   }
   dim3 grid(pl.n_tiles, pl.splits);
   tc_gemm_kernel<<<grid, kTcThreads, smem, st>>>(tmW, tmW2, tmX, p);
-  return cudaGetLastError();
+  return launched();
 }
 
 template <typename T>
@@ -564,12 +564,12 @@ static cudaError_t gemm_simt_t(const GemmArgs& a, cudaStream_t st) {
   simt_gemm_kernel<T><<<grid, 256, 0, st>>>(static_cast<const T*>(a.X), static_cast<const T*>(a.W),
                                             static_cast<const T*>(a.W2), a.n_out, a.K,
                                             a.rows_cap, a.count, a.epi.inter, raw);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launched();
   if (e != cudaSuccess) return e;
   const int64_t total = static_cast<int64_t>(a.rows_cap) * a.n_out;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
   epilogue_kernel<T><<<blocks, 256, 0, st>>>(raw, a.n_out, a.rows_cap, a.count, a.epi);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t gemm(const GemmArgs& a, cudaStream_t st) {

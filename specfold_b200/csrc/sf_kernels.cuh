@@ -9,6 +9,15 @@ constexpr int kMaxBranches = 32;         // B1 limit (one warp per branch in the
 constexpr int kMaxRows = 1024;           // B1*N limit of the compaction scan
 constexpr int kMaxGateSmem = 227 * 1024;
 
+// number of kernels this library has launched (all threads, all devices)
+void count_launch(int n = 1);
+// launch status of the kernel just launched; counts it when it launched
+inline cudaError_t launched(int n = 1) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) count_launch(n);
+  return e;
+}
+
 struct GateRowsParams {
   const void* hp;          // combine input (nullptr: gate on `hidden` as is)
   const void* ffn;         // [BN+1, D]
