@@ -132,6 +132,24 @@ int sf_fused_ffn_scatter(int dtype, const void* hp_all, const void* ln_w, const 
                          void* xn_buf, float* rstd_buf, float eps, int D, int I, void* ws,
                          size_t ws_bytes, int* err, void* stream);
 
+/* sf_fused_ffn_scatter without caller-provided scratch.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory (code inside a
+ * stream capture, runtimes without an allocator, hosts whose memory pool belongs to
+ * someone else).  Same inputs and outputs as sf_fused_ffn_scatter minus act_buf,
+ * xn_buf, rstd_buf and the workspace; the scratch is a fixed 32 MiB __device__ array
+ * inside the library, held on every GPU where the library's module is loaded until the
+ * process exits.  It calls no cudaMalloc/cudaFree.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, that device current): make it before any stream capture.
+ *  - Shapes needing more than 32 MiB of scratch return SF_ERR_ARG.
+ *  - All calls share the array and it keeps the last call's contents (the split-K
+ *    counters are cleared at each call); calls that overlap on the GPU race and must be
+ *    serialised by the caller.                                                       */
+int sf_fused_ffn_scatter_static(int dtype, const void* hp_all, const void* ln_w,
+                                const void* w_gate, const void* w_up, const void* w_down,
+                                const int64_t* rows, const int32_t* count, void* ffn_buf,
+                                int bucket, float eps, int D, int I, int* err, void* stream);
+
 /* hidden = hp_all + ffn_buf[src*N + n] (fastdllm_v2_folded.py:361).                 */
 int sf_combine(int dtype, const void* hp_all, const void* ffn_buf, const int64_t* src,
                void* hidden, int B1, int N, int D, int* err, void* stream);

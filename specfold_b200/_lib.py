@@ -72,6 +72,9 @@ _SIGS = {
                                      c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                      c_void_p, c_float, c_int, c_int, c_void_p, c_size_t,
                                      c_void_p, c_void_p]),
+    "sf_fused_ffn_scatter_static": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                            c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                            c_float, c_int, c_int, c_void_p, c_void_p]),
     "sf_combine": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                            c_void_p, c_void_p]),
     "sf_final_norm_lm_head": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

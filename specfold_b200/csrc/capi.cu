@@ -162,6 +162,12 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
 
 }  // namespace
 
+namespace sf {
+// lets other translation units of the library set sf_last_error()
+int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+int report_cuda(cudaError_t e, const char* what) { return cuda_status(e, what); }
+}  // namespace sf
+
 extern "C" {
 
 const char* sf_last_error(void) { return g_err.c_str(); }
