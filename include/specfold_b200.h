@@ -98,12 +98,15 @@ int sf_fused_ln_qkv_rope_scatter(int dtype, const void* xn, const void* w_qkv,
  * fastdllm_v2_folded.py:329-333): attention of each recomputed row over the prefix
  * cache (P keys) and the N in-block keys kv_buf[src[b*N+j]*N + j]; writes O (model
  * dtype, normalised), M (row max) and Z (sum of exp) at the flat row.  P may be 0.
- * Takes B1 in addition to the reference's arguments (bounds check of src).          */
+ * Takes B1 in addition to the reference's arguments (bounds check of src) and, for
+ * bf16 with P > 0 (tensor-core prefix pass, split along the keys), a workspace of
+ * sf_attn_workspace_bytes(...) bytes; kv_head_stride must be a multiple of hd.      */
 int sf_flash_attn_gqa(int dtype, const void* q_buf, const void* prefix_k, const void* prefix_v,
                       int64_t kv_head_stride, const void* kv_buf, const int64_t* src,
                       const int64_t* rows, const int32_t* count, void* O_tab, float* M_tab,
                       float* Z_tab, int P, int N, float scale, int bucket, int B1, int H,
-                      int Hkv, int hd, int* err, void* stream);
+                      int Hkv, int hd, void* ws, size_t ws_bytes, int* err, void* stream);
+size_t sf_attn_workspace_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P);
 
 /* specfold_chain_correction_gqa_kernel (triton_kernels.py:364-429, launched at
  * fastdllm_v2_folded.py:334-338): for every folded row (rec == 0) start from the
@@ -230,7 +233,7 @@ const char* sf_profile_name(int kind);
 int sf_profile_kind(int kind, double* total_ms, int* calls);
 
 size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
-                                 int V);
+                                 int V, int P);
 int sf_folded_verify_forward(const sf_verify_args* args);
 
 #ifdef __cplusplus

@@ -61,7 +61,8 @@ _SIGS = {
     "sf_flash_attn_gqa": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_int, c_int, c_float, c_int, c_int, c_int, c_int, c_int,
-                                  c_void_p, c_void_p]),
+                                  c_void_p, c_size_t, c_void_p, c_void_p]),
+    "sf_attn_workspace_bytes": (c_size_t, [c_int] * 6),
     "sf_chain_correction_gqa": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                         c_int, c_float, c_int, c_int, c_int, c_void_p,
@@ -88,7 +89,7 @@ _SIGS = {
     "sf_profile_kinds": (c_int, []),
     "sf_profile_name": (C.c_char_p, [c_int]),
     "sf_profile_kind": (c_int, [c_int, C.POINTER(C.c_double), C.POINTER(c_int)]),
-    "sf_verify_workspace_bytes": (c_size_t, [c_int] * 9),
+    "sf_verify_workspace_bytes": (c_size_t, [c_int] * 10),
     "sf_folded_verify_forward": (c_int, [C.POINTER(SfVerifyArgs)]),
 }
 

@@ -20,8 +20,13 @@ namespace sf {
 constexpr int kAttnKeys = 32;   // keys per smem tile (one per lane)
 constexpr int kMaxGroup = 16;   // q heads per kv head
 
+// With part_O != nullptr the prefix keys were already folded into per-split partials
+// (unnormalised O, running max m, sum l) by the tensor-core kernel: the state starts
+// from their log-sum-exp merge and only the in-block keys are added here.
 template <typename T, int HD>
-__global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p) {
+__global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, const float* part_O,
+                                                        const float* part_ml, int splits,
+                                                        int q_rows) {
   constexpr int DPL = HD / 32;  // dims per lane
   __shared__ float qs[kMaxGroup][HD];
   __shared__ float ks[kAttnKeys][HD + 1];
@@ -55,8 +60,30 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p) {
 #pragma unroll
     for (int t = 0; t < DPL; ++t) acc[i][t] = 0.f;
   }
+  if (part_O != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int g = warp + 4 * i;
+      if (g >= G) break;
+      const int64_t qi = static_cast<int64_t>(slot) * G + g;
+      float mx = -INFINITY;
+      for (int s = 0; s < splits; ++s)
+        mx = fmaxf(mx, part_ml[2 * ((static_cast<int64_t>(s) * p.Hkv + kvh) * q_rows + qi)]);
+      m[i] = mx;
+      for (int s = 0; s < splits; ++s) {
+        const int64_t base = (static_cast<int64_t>(s) * p.Hkv + kvh) * q_rows + qi;
+        const float ms = part_ml[2 * base];
+        if (ms == -INFINITY) continue;
+        const float w = expf(ms - mx);
+        l[i] += part_ml[2 * base + 1] * w;
+#pragma unroll
+        for (int t = 0; t < DPL; ++t) acc[i][t] = fmaf(part_O[base * HD + lane + 32 * t], w, acc[i][t]);
+      }
+    }
+  }
   const int total = p.P + p.N;
-  for (int k0 = 0; k0 < total; k0 += kAttnKeys) {
+  const int key_begin = part_O != nullptr ? p.P : 0;
+  for (int k0 = key_begin; k0 < total; k0 += kAttnKeys) {
     __syncthreads();
     if (threadIdx.x < kAttnKeys) {
       const int key = k0 + threadIdx.x;
@@ -224,16 +251,28 @@ __global__ void kv_append_kernel(T* ck, T* cv, int64_t cs, const T* nk, const T*
 
 // ------------------------------------------------------------------------ launchers
 template <typename T>
-static cudaError_t attn_t(const AttnParams& p, cudaStream_t st) {
+static cudaError_t attn_t(const AttnParams& p, const float* part_O, const float* part_ml,
+                          int splits, int q_rows, cudaStream_t st) {
   dim3 grid(p.bucket, p.Hkv);
-  if (p.hd == 128) attn_simt_kernel<T, 128><<<grid, 128, 0, st>>>(p);
-  else if (p.hd == 64) attn_simt_kernel<T, 64><<<grid, 128, 0, st>>>(p);
-  else return cudaErrorInvalidValue;
+  if (p.hd == 128)
+    attn_simt_kernel<T, 128><<<grid, 128, 0, st>>>(p, part_O, part_ml, splits, q_rows);
+  else if (p.hd == 64)
+    attn_simt_kernel<T, 64><<<grid, 128, 0, st>>>(p, part_O, part_ml, splits, q_rows);
+  else
+    return cudaErrorInvalidValue;
   return launched();
 }
 cudaError_t launch_attention_simt(int dtype, const AttnParams& p, cudaStream_t st) {
   if (p.H % p.Hkv != 0 || p.H / p.Hkv > kMaxGroup) return cudaErrorInvalidValue;
-  return dtype == BF16 ? attn_t<__nv_bfloat16>(p, st) : attn_t<float>(p, st);
+  return dtype == BF16 ? attn_t<__nv_bfloat16>(p, nullptr, nullptr, 0, 0, st)
+                       : attn_t<float>(p, nullptr, nullptr, 0, 0, st);
+}
+cudaError_t launch_attention_simt_partials(int dtype, const AttnParams& p, const float* part_O,
+                                           const float* part_ml, int splits, int q_rows,
+                                           cudaStream_t st) {
+  if (p.H % p.Hkv != 0 || p.H / p.Hkv > kMaxGroup) return cudaErrorInvalidValue;
+  return dtype == BF16 ? attn_t<__nv_bfloat16>(p, part_O, part_ml, splits, q_rows, st)
+                       : attn_t<float>(p, part_O, part_ml, splits, q_rows, st);
 }
 
 template <typename T>
@@ -269,8 +308,5 @@ cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, co
   return launched();
 }
 
-cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st) {
-  return launch_attention_simt(dtype, p, st);
-}
 
 }  // namespace sf

@@ -1,0 +1,421 @@
+// Tensor-core (tcgen05) attention over the shared prefix KV cache, split along the keys.
+//
+// Every recomputed row's queries attend to the same prefix keys of their kv head, so
+// the prefix part is a dense flash-attention tile problem: queries of one kv head are
+// packed (slot*G + g) 128 to a tile by the QKV epilogue (or pack_q_kernel), keys are
+// streamed from the cache by TMA in blocks of 128, and per block
+//     S = Q K^T              tcgen05.mma, accumulator in TMEM
+//     softmax                4 warps, one query row per thread, running (m, l)
+//     O += P V               P (bf16) from shared memory, V as the MN-major operand
+// Each (query tile, kv head, key split) CTA writes its unnormalised partial (O, m, l)
+// in fp32; attn_simt_kernel then merges the splits and adds the N in-block keys,
+// which differ per branch (specfold_flash_attn_gqa_kernel, triton_kernels.py:301-361,
+// covers both parts in one program per (row, kv head)).
+//
+// Warp 0 issues TMA, warp 1 owns TMEM and issues MMAs, warps 2-5 run the softmax.
+// All mbarrier waits are bounded (sf_common.cuh).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "sf_kernels.cuh"
+
+namespace sf {
+
+constexpr int kAttThreads = 192;
+constexpr int kQT = 128;            // queries per tile (MMA M)
+constexpr int kKB = 128;            // keys per block
+constexpr int kMaxKvSplits = 16;
+constexpr int kKeysPerSplit = 256;  // at least two key blocks per split
+
+struct AttnTcParams {
+  const int32_t* count;
+  int bucket, G, q_rows, P, kv_rows, splits, keys_per_split, Hkv;
+  float scale;
+  float* part_O;    // [splits][Hkv][q_rows][HD]
+  float* part_ml;   // [splits][Hkv][q_rows][2]
+  int* err;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttThreads, 1)
+    attn_prefix_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
+  constexpr int KCH = HD / 64;                 // 64-column TMA boxes per row
+  constexpr int kBox = 128 * 64 * 2;           // one 128-row box: 16 KB
+  constexpr int QBYTES = KCH * kBox;
+  constexpr int KVBYTES = KCH * kBox;
+  constexpr int PBYTES = 2 * kBox;             // 128 queries x 128 keys bf16
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* sQ = smem;
+  unsigned char* sK = sQ + QBYTES;             // [2][KVBYTES]
+  unsigned char* sV = sK + 2 * KVBYTES;        // [2][KVBYTES]
+  unsigned char* sP = sV + 2 * KVBYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + PBYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint64_t* drain = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int count = min(*p.count, p.bucket);
+  const int Mq = count * p.G;
+  const int q0 = qt * kQT;
+  if (q0 >= Mq) return;                        // uniform per CTA
+  const int k_begin = split * p.keys_per_split;
+  const int k_end = min(p.P, k_begin + p.keys_per_split);
+  const int nb = k_end > k_begin ? (k_end - k_begin + kKB - 1) / kKB : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  if (warp == 0) {
+    if (lane == 0 && nb > 0) {
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();   // every query tile of this head rereads it
+      mbar_arrive_expect_tx(q_full, QBYTES);
+      for (int c = 0; c < KCH; ++c)
+        tma_load_2d(sQ + c * kBox, &tmQ, q_full, c * 64, kvh * p.q_rows + q0, pol_q);
+      int issued = 0;
+      for (int i = 0; i < nb; ++i) {
+        const int s = i & 1;
+        if (!mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, p.err)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(&kv_full[s], 2 * KVBYTES);
+        const int krow = kvh * p.kv_rows + k_begin + i * kKB;
+        for (int c = 0; c < KCH; ++c) {
+          tma_load_2d(sK + s * KVBYTES + c * kBox, &tmK, &kv_full[s], c * 64, krow, pol_kv);
+          tma_load_2d(sV + s * KVBYTES + c * kBox, &tmV, &kv_full[s], c * 64, krow, pol_kv);
+        }
+        ++issued;
+      }
+      mbar_wait(q_full, 0, p.err);
+      for (int i = max(0, issued - 2); i < issued; ++i)
+        mbar_wait(&kv_full[i & 1], (i >> 1) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nb > 0) {
+      const uint32_t id_s = idesc_bf16(128, kKB);          // S = Q K^T, both K-major
+      const uint32_t id_pv = idesc_bf16(128, HD, 0, 1);    // O += P V, V MN-major
+      bool ok = mbar_wait(q_full, 0, p.err) && mbar_wait(&kv_full[0], 0, p.err);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t q_s = smem_u32(sQ), k_s = smem_u32(sK);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_f16(tS, sdesc_kmajor_sw128(q_s + (kk >> 2) * kBox + (kk & 3) * 32),
+                   sdesc_kmajor_sw128(k_s + (kk >> 2) * kBox + (kk & 3) * 32), id_s,
+                   kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+      }
+      for (int i = 0; ok && i < nb; ++i) {
+        if (!mbar_wait(p_full, i & 1, p.err)) { ok = false; break; }
+        tc_fence_after();
+        if (i + 1 < nb) {
+          const int s1 = (i + 1) & 1;
+          if (!mbar_wait(&kv_full[s1], ((i + 1) >> 1) & 1, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_s = smem_u32(sQ), k_s = smem_u32(sK + s1 * KVBYTES);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk)
+            umma_f16(tS, sdesc_kmajor_sw128(q_s + (kk >> 2) * kBox + (kk & 3) * 32),
+                     sdesc_kmajor_sw128(k_s + (kk >> 2) * kBox + (kk & 3) * 32), id_s,
+                     kk > 0 ? 1u : 0u);
+          umma_commit(s_full);
+        }
+        const uint32_t p_s = smem_u32(sP), v_s = smem_u32(sV + (i & 1) * KVBYTES);
+#pragma unroll
+        for (int kk = 0; kk < kKB / 16; ++kk)
+          umma_f16(tO, sdesc_kmajor_sw128(p_s + (kk >> 2) * kBox + (kk & 3) * 32),
+                   sdesc_mnmajor_sw128(v_s + kk * 2048, kBox), id_pv,
+                   (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(pv_done);
+        umma_commit(&kv_empty[i & 1]);
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warps
+    const int q = warp & 3;
+    const int r = q * 32 + lane;                          // query row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nb; ++i) {
+      ok = ok && !*abort_flag && mbar_wait(s_full, i & 1, p.err);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int nv = min(kKB, k_end - (k_begin + i * kKB));
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKB / 32; ++c) {
+        float v[32];
+        tmem_ld16(tS + lane_off + c * 32, v);
+        tmem_ld16(tS + lane_off + c * 32 + 16, v + 16);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c * 32 + j < nv) mx = fmaxf(mx, v[j] * p.scale);
+      }
+      const float mn = fmaxf(m, mx);
+      const float alpha = expf(m - mn);
+      if (i > 0) {
+        ok = mbar_wait(pv_done, (i - 1) & 1, p.err);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tmem_ld16(tO + lane_off + c * 32, o);
+            tmem_ld16(tO + lane_off + c * 32 + 16, o + 16);
+            tmem_ld_wait();
+            uint32_t u[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(o[j] * alpha);
+            tmem_st16(tO + lane_off + c * 32, u);
+            tmem_st16(tO + lane_off + c * 32 + 16, u + 16);
+          }
+          tmem_st_wait();
+        }
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kKB / 32; ++c) {
+        float v[32];
+        tmem_ld16(tS + lane_off + c * 32, v);
+        tmem_ld16(tS + lane_off + c * 32 + 16, v + 16);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g8 = 0; g8 < 4; ++g8) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const int j0 = g8 * 8 + 2 * h;
+            const float e0 = (c * 32 + j0 < nv) ? expf(v[j0] * p.scale - mn) : 0.f;
+            const float e1 = (c * 32 + j0 + 1 < nv) ? expf(v[j0 + 1] * p.scale - mn) : 0.f;
+            sum += e0 + e1;
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(e0, e1);
+            pk[h] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          const int key = c * 32 + g8 * 8;             // first key of this 16-byte chunk
+          const int half = key >> 6, chunk = (key & 63) >> 3;
+          unsigned char* dst = sP + half * kBox + r * 128 + ((chunk ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+      l = l * alpha + sum;
+      m = mn;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && nb > 0) {
+      ok = mbar_wait(pv_done, (nb - 1) & 1, p.err);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    const int qi = q0 + r;
+    const int64_t base = (static_cast<int64_t>(split) * p.Hkv + kvh) * p.q_rows + qi;
+    if (ok && nb > 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tmem_ld16(tO + lane_off + c * 32, o);
+        tmem_ld16(tO + lane_off + c * 32 + 16, o + 16);
+        tmem_ld_wait();
+        if (qi < Mq) {
+          float4* dst = reinterpret_cast<float4*>(p.part_O + base * HD + c * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        }
+      }
+    } else if (qi < Mq) {
+      m = -INFINITY;
+      l = 0.f;
+      for (int d = 0; d < HD; ++d) p.part_O[base * HD + d] = 0.f;
+    }
+    if (qi < Mq) {
+      p.part_ml[2 * base] = m;
+      p.part_ml[2 * base + 1] = l;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// q_comp[kvh][slot*G + g][:] = q_buf[rows[slot]][(kvh*G + g)*hd : ...]
+__global__ void pack_q_kernel(const __nv_bfloat16* q_buf, const int64_t* rows,
+                              const int32_t* count, int bucket, int H, int Hkv, int hd,
+                              int q_rows, __nv_bfloat16* q_comp) {
+  const int slot = blockIdx.x;
+  const int n = min(*count, bucket);
+  if (slot >= n) return;
+  const int G = H / Hkv;
+  const int64_t r = rows[slot];
+  const int vecs = H * hd / 8;
+  for (int i = threadIdx.x; i < vecs; i += blockDim.x) {
+    const int e = i * 8;
+    const int h = e / hd, d = e % hd;
+    const int kvh = h / G, g = h % G;
+    const uint4 v = *reinterpret_cast<const uint4*>(q_buf + r * H * hd + e);
+    *reinterpret_cast<uint4*>(q_comp + ((static_cast<int64_t>(kvh) * q_rows + slot * G + g) * hd + d)) = v;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 att_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+static bool att_tmap(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols) {
+  auto fn = att_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int kv_splits(int P) {
+  if (P <= 0) return 0;
+  return std::max(1, std::min(kMaxKvSplits, (P + kKeysPerSplit - 1) / kKeysPerSplit));
+}
+
+static size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+size_t attn_scratch_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P,
+                          bool need_q_comp) {
+  if (dtype != BF16 || P <= 0) return 0;
+  const int G = H / Hkv;
+  const size_t q_rows = static_cast<size_t>(bucket) * G;
+  const int S = kv_splits(P);
+  size_t b = 0;
+  if (need_q_comp) b += up256(Hkv * q_rows * hd * 2);
+  b += up256(static_cast<size_t>(S) * Hkv * q_rows * hd * 4);
+  b += up256(static_cast<size_t>(S) * Hkv * q_rows * 2 * 4);
+  return b;
+}
+
+cudaError_t launch_attention_simt_partials(int dtype, const AttnParams& p, const float* part_O,
+                                           const float* part_ml, int splits, int q_rows,
+                                           cudaStream_t st);
+
+template <int HD>
+static cudaError_t prefix_tc(const AttnParams& a, cudaStream_t st) {
+  const int G = a.H / a.Hkv;
+  const int q_rows = a.bucket * G;
+  const int S = kv_splits(a.P);
+  const bool pack = a.q_comp == nullptr;
+  if (a.scratch == nullptr ||
+      a.scratch_bytes < attn_scratch_bytes(BF16, a.bucket, a.H, a.Hkv, HD, a.P, pack))
+    return cudaErrorInvalidValue;
+  if (a.kv_head_stride % HD != 0) return cudaErrorInvalidValue;
+  char* sc = static_cast<char*>(a.scratch);
+  const void* q_comp = a.q_comp;
+  if (pack) {
+    q_comp = sc;
+    pack_q_kernel<<<a.bucket, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(a.q_buf), a.rows,
+                                            a.count, a.bucket, a.H, a.Hkv, HD, q_rows,
+                                            reinterpret_cast<__nv_bfloat16*>(sc));
+    cudaError_t e = launched();
+    if (e != cudaSuccess) return e;
+    sc += up256(static_cast<size_t>(a.Hkv) * q_rows * HD * 2);
+  }
+  AttnTcParams p{};
+  p.count = a.count;
+  p.bucket = a.bucket;
+  p.G = G;
+  p.q_rows = q_rows;
+  p.P = a.P;
+  p.kv_rows = static_cast<int>(a.kv_head_stride / HD);
+  p.splits = S;
+  p.keys_per_split = ((a.P + S - 1) / S + kKB - 1) / kKB * kKB;
+  p.Hkv = a.Hkv;
+  p.scale = a.scale;
+  p.part_O = reinterpret_cast<float*>(sc);
+  p.part_ml = reinterpret_cast<float*>(sc + up256(static_cast<size_t>(S) * a.Hkv * q_rows * HD * 4));
+  p.err = a.err;
+  CUtensorMap tq, tk, tv;
+  if (!att_tmap(&tq, q_comp, static_cast<uint64_t>(a.Hkv) * q_rows, HD) ||
+      !att_tmap(&tk, a.pk, static_cast<uint64_t>(a.Hkv) * p.kv_rows, HD) ||
+      !att_tmap(&tv, a.pv, static_cast<uint64_t>(a.Hkv) * p.kv_rows, HD))
+    return cudaErrorInvalidValue;
+  constexpr int kBox = 128 * 64 * 2;
+  const size_t smem = 1024 + (HD / 64) * kBox * 5 + 2 * kBox + 256;
+  static int configured = 0;
+  if (configured < static_cast<int>(smem)) {
+    cudaError_t e = cudaFuncSetAttribute(attn_prefix_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = static_cast<int>(smem);
+  }
+  dim3 grid((q_rows + kQT - 1) / kQT, a.Hkv, S);
+  attn_prefix_kernel<HD><<<grid, kAttThreads, smem, st>>>(tq, tk, tv, p);
+  cudaError_t e = launched();
+  if (e != cudaSuccess) return e;
+  return launch_attention_simt_partials(BF16, a, p.part_O, p.part_ml, S, q_rows, st);
+}
+
+cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st) {
+  if (dtype == BF16 && p.P > 0 && p.pk != nullptr) {
+    if (p.hd == 128) return prefix_tc<128>(p, st);
+    if (p.hd == 64) return prefix_tc<64>(p, st);
+    return cudaErrorInvalidValue;
+  }
+  return launch_attention_simt(dtype, p, st);
+}
+
+}  // namespace sf

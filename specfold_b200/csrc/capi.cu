@@ -118,15 +118,15 @@ struct Carve {
 };
 
 struct FwdBufs {
-  void *q_buf, *kv_buf, *O, *ffn, *act, *hbuf, *hp, *xn, *gemm_ws;
+  void *q_buf, *kv_buf, *O, *ffn, *act, *hbuf, *hp, *xn, *gemm_ws, *q_comp, *attn_ws;
   float *M, *Z, *rstd, *rstd2;
   int64_t *f, *src, *seg, *rows;
   int8_t* rec;
-  size_t gemm_ws_bytes, total;
+  size_t gemm_ws_bytes, attn_ws_bytes, total;
 };
 
 FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
-                      int V, int bucket) {
+                      int V, int bucket, int P) {
   const size_t es = esize(dtype);
   const int BN = B1 * N, qd = H * hd, kvd = Hkv * hd;
   Carve c(ws);
@@ -156,6 +156,11 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   g = std::max(g, ws_gemm(dtype, BN, V, D, EPI_LOGITS, 0));
   b.gemm_ws_bytes = g;
   b.gemm_ws = c.take(g + 256);
+  // tensor-core attention: query copy per kv head + split-KV partials
+  const bool tc_attn = dtype == SF_DTYPE_BF16 && P > 0;
+  b.q_comp = tc_attn ? c.take(static_cast<size_t>(bucket) * H * hd * es) : nullptr;
+  b.attn_ws_bytes = attn_scratch_bytes(dtype, bucket, H, Hkv, hd, P, false);
+  b.attn_ws = b.attn_ws_bytes ? c.take(b.attn_ws_bytes) : nullptr;
   b.total = c.off;
   return b;
 }
@@ -310,7 +315,7 @@ int sf_flash_attn_gqa(int dtype, const void* q_buf, const void* prefix_k, const 
                       int64_t kv_head_stride, const void* kv_buf, const int64_t* src,
                       const int64_t* rows, const int32_t* count, void* O_tab, float* M_tab,
                       float* Z_tab, int P, int N, float scale, int bucket, int B1, int H,
-                      int Hkv, int hd, int* err, void* stream) {
+                      int Hkv, int hd, void* ws, size_t ws_bytes, int* err, void* stream) {
   int s = check_dims(dtype, 64, hd, H, Hkv);
   if (s) return s;
   if (P < 0 || (P > 0 && (!prefix_k || !prefix_v)) || !q_buf || !kv_buf || !src || !rows ||
@@ -318,6 +323,11 @@ int sf_flash_attn_gqa(int dtype, const void* q_buf, const void* prefix_k, const 
     return fail(SF_ERR_ARG, "bad attention arguments");
   if (P > 0 && kv_head_stride < static_cast<int64_t>(P) * hd)
     return fail(SF_ERR_ARG, "kv_head_stride %lld < P*hd", static_cast<long long>(kv_head_stride));
+  if (P > 0 && kv_head_stride % hd != 0)
+    return fail(SF_ERR_ARG, "kv_head_stride must be a multiple of head_dim");
+  const size_t need = attn_scratch_bytes(dtype, bucket, H, Hkv, hd, P, true);
+  if (need > 0 && (!ws || ws_bytes < need))
+    return fail(SF_ERR_WORKSPACE, "attention workspace %zu < %zu bytes", ws_bytes, need);
   AttnParams p{};
   p.q_buf = q_buf;
   p.pk = prefix_k;
@@ -339,7 +349,14 @@ int sf_flash_attn_gqa(int dtype, const void* q_buf, const void* prefix_k, const 
   p.B1 = B1;
   p.scale = scale;
   p.err = err;
+  p.q_comp = nullptr;   // packed from q_buf into the workspace
+  p.scratch = ws;
+  p.scratch_bytes = ws_bytes;
   return cuda_status(launch_attention(dtype, p, S(stream)), "attention");
+}
+
+size_t sf_attn_workspace_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P) {
+  return attn_scratch_bytes(dtype, bucket, H, Hkv, hd, P, true);
 }
 
 int sf_chain_correction_gqa(int dtype, const void* q_buf, const void* kv_buf,
@@ -516,8 +533,8 @@ int sf_kv_append(int dtype, void* cache_k, void* cache_v, int64_t cache_head_str
 }
 
 size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
-                                 int V) {
-  return carve_forward(nullptr, dtype, B1, N, D, H, Hkv, hd, I, V, B1 * N).total + 256;
+                                 int V, int P) {
+  return carve_forward(nullptr, dtype, B1, N, D, H, Hkv, hd, I, V, B1 * N, P).total + 256;
 }
 
 int sf_folded_verify_forward(const sf_verify_args* a) {
@@ -539,7 +556,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     return fail(SF_ERR_ARG, "null pointer in verify args");
   if (a->P < 0 || (a->P > 0 && a->kv_head_stride < static_cast<int64_t>(a->P) * hd))
     return fail(SF_ERR_ARG, "prefix length / stride mismatch");
-  FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket);
+  FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket, a->P);
   if (b.total > a->ws_bytes)
     return fail(SF_ERR_WORKSPACE, "workspace %zu < %zu bytes", a->ws_bytes, b.total);
   cudaStream_t st = S(a->stream);
@@ -621,6 +638,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     q.epi.kv_dim = kvd;
     q.epi.hd = hd;
     q.epi.N = N;
+    q.epi.q_comp = b.q_comp;
+    q.epi.q_comp_rows = bucket * (H / Hkv);
     q.ws = b.gemm_ws;
     q.ws_bytes = b.gemm_ws_bytes;
     q.err = a->err;
@@ -647,6 +666,9 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     at.B1 = B1;
     at.scale = a->scale;
     at.err = a->err;
+    at.q_comp = b.q_comp;
+    at.scratch = b.attn_ws;
+    at.scratch_bytes = b.attn_ws_bytes;
     if ((s = timed(K_ATTN, st, [&] { return cuda_status(launch_attention(dtype, at, st), "attention"); })))
       return s;
 

@@ -96,6 +96,8 @@ struct EpiParams {
   int q_dim, kv_dim, hd, N;
   int inter;               // SWIGLU: I
   int shift;               // LOGITS
+  void* q_comp;            // QKV: optional query copy [Hkv][q_comp_rows][hd], row slot*G + g
+  int q_comp_rows;         //      (the A operand layout of the tensor-core attention)
 };
 
 struct GemmArgs {
@@ -133,7 +135,14 @@ struct AttnParams {
   int P, N, bucket, H, Hkv, hd, B1;
   float scale;
   int* err;
+  // tensor-core path (bf16): compact queries written by the QKV epilogue (nullptr: the
+  // launcher packs them from q_buf into the scratch) and fp32 split-KV partials
+  const void* q_comp;
+  void* scratch;
+  size_t scratch_bytes;
 };
+size_t attn_scratch_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P,
+                          bool need_q_comp);
 cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attention_simt(int dtype, const AttnParams& p, cudaStream_t st);
 

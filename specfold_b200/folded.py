@@ -195,8 +195,8 @@ class FoldedVerifyB200:
                     raise ValueError("prefix cache layers must share one head stride")
                 st.prefix_k, st.prefix_v = k0.data_ptr(), v0.data_ptr()
 
-        need = lib.sf_verify_workspace_bytes(dtype_code(hidden), B1, N, D, H, Hkv, hd, I, V)
-        ws = self._workspace((dev.index, dtype, B1, N), need, dev)
+        need = lib.sf_verify_workspace_bytes(dtype_code(hidden), B1, N, D, H, Hkv, hd, I, V, P)
+        ws = self._workspace((dev.index, dtype), need, dev)
         logits = torch.empty(B1, N, V, dtype=dtype, device=dev)
         slab = torch.zeros(L + L * B1 + 1, dtype=torch.int32, device=dev)
         count_slab, segcnt_slab, err = slab[:L], slab[L:L + L * B1], slab[L + L * B1:]

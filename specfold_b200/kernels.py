@@ -123,11 +123,16 @@ def flash_attn_gqa(q_buf, pk, pv, kv_head_stride, kv_buf, src, rows, count, O, M
                    bucket, B1, H, Hkv, hd, err=None):
     _check_cuda(q_buf, kv_buf, src, rows, count, O, M, Z)
     err = err if err is not None else error_word(q_buf.device)
-    _lib.check(_lib.load().sf_flash_attn_gqa(
+    lib = _lib.load()
+    need = lib.sf_attn_workspace_bytes(dtype_code(q_buf), bucket, H, Hkv, hd, P)
+    ws = workspace(q_buf.device, need + (16 << 10)) if need else None
+    # the scratch follows the GEMM tile counters, which must stay untouched
+    wp = None if ws is None else ws.data_ptr() + (16 << 10)
+    _lib.check(lib.sf_flash_attn_gqa(
         dtype_code(q_buf), q_buf.data_ptr(), _ptr(pk), _ptr(pv), int(kv_head_stride),
         kv_buf.data_ptr(), src.data_ptr(), rows.data_ptr(), count.data_ptr(), O.data_ptr(),
-        M.data_ptr(), Z.data_ptr(), P, N, float(scale), bucket, B1, H, Hkv, hd, err.data_ptr(),
-        _stream()), "flash_attn_gqa")
+        M.data_ptr(), Z.data_ptr(), P, N, float(scale), bucket, B1, H, Hkv, hd, wp, need,
+        err.data_ptr(), _stream()), "flash_attn_gqa")
     return err
 
 

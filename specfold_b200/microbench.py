@@ -1,0 +1,138 @@
+"""Kernel microbenchmarks of the folded verify forward (one C-ABI entry point at a time).
+
+    python -m specfold_b200.microbench --kernel qkv|o_proj|ffn|lm_head|attention|merge|gate
+        [--shape qwen7b|llama8b|...] [--rows R] [--prefix P] [--fold F] [--branches B1]
+        [--iters K]
+
+Each run builds seeded inputs of the named shape on cuda:0, launches the entry point
+``--iters`` times after 3 warm-ups, and prints one JSON line per configuration with the
+mean CUDA-event time per launch, the algorithmic bytes and FLOPs of one launch, and the
+achieved GB/s / TFLOP/s.  Weight matrices at these shapes exceed L2, so every launch
+streams them from HBM.  Suitable under ``ncu -k regex:<kernel>`` for counter capture.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from . import _lib
+from . import kernels as K
+from .synthetic import SHAPES
+
+
+def _events(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def _report(name, ms, bytes_, flops, extra=None):
+    out = {"kernel": name, "ms": round(ms, 5), "bytes": int(bytes_), "flops": int(flops),
+           "gbs": round(bytes_ / (ms / 1e3) / 1e9, 1),
+           "tflops": round(flops / (ms / 1e3) / 1e12, 2)}
+    out.update(extra or {})
+    print(json.dumps(out), flush=True)
+    return out
+
+
+def _rows(BN, count, g):
+    return torch.randperm(BN, generator=g)[:count].sort().values.cuda()
+
+
+def bench_qkv(dims, rows, iters, g):
+    D, H, Hkv, hd = dims.hidden, dims.heads, dims.kv_heads, dims.head_dim
+    BN = 256
+    n_out = (H + 2 * Hkv) * hd
+    xn = torch.randn(BN, D, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(n_out, D, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    b = (torch.randn(n_out, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    cos = torch.randn(32, hd, generator=g).to(torch.bfloat16).cuda()
+    sin = torch.randn(32, hd, generator=g).to(torch.bfloat16).cuda()
+    r = _rows(BN, rows, g)
+    cnt = torch.tensor([rows], dtype=torch.int32, device="cuda")
+    q_buf = torch.zeros(BN + 1, H * hd, dtype=torch.bfloat16, device="cuda")
+    kv_buf = torch.zeros(BN + 1, 2 * Hkv * hd, dtype=torch.bfloat16, device="cuda")
+    err = K.error_word("cuda")
+    ms = _events(lambda: K.fused_ln_qkv_rope_scatter(xn, w, b, r, cnt, cos, sin, q_buf, kv_buf,
+                                                       32, BN, H, Hkv, hd, err=err), iters)
+    K.raise_device_error(err)
+    return _report("qkv", ms, n_out * D * 2 + rows * D * 2 + rows * n_out * 2,
+                   2 * rows * n_out * D, {"rows": rows})
+
+
+def bench_o_proj(dims, rows, iters, g):
+    D, qd = dims.hidden, dims.heads * dims.head_dim
+    BN = rows
+    Hf = torch.randn(BN, D, generator=g).to(torch.bfloat16).cuda()
+    O = torch.randn(BN, qd, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(D, qd, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    err = K.error_word("cuda")
+    ms = _events(lambda: K.o_proj_residual(Hf, O, w, err=err), iters)
+    K.raise_device_error(err)
+    return _report("o_proj", ms, D * qd * 2 + BN * (qd + 2 * D) * 2, 2 * BN * D * qd,
+                   {"rows": BN})
+
+
+def bench_ffn(dims, rows, iters, g):
+    D, I = dims.hidden, dims.inter
+    BN = 256
+    hp = torch.randn(BN, D, generator=g).to(torch.bfloat16).cuda()
+    ln = torch.ones(D, dtype=torch.bfloat16, device="cuda")
+    wg = (torch.randn(I, D, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    wu = (torch.randn(I, D, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    wd = (torch.randn(D, I, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    r = _rows(BN, rows, g)
+    cnt = torch.tensor([rows], dtype=torch.int32, device="cuda")
+    ffn = torch.zeros(BN + 1, D, dtype=torch.bfloat16, device="cuda")
+    err = K.error_word("cuda")
+    ms = _events(lambda: K.fused_ffn_scatter(hp, ln, wg, wu, wd, r, cnt, ffn, BN, 1e-6, err=err),
+                 iters)
+    K.raise_device_error(err)
+    return _report("ffn", ms, 3 * I * D * 2, 2 * rows * 3 * I * D, {"rows": rows})
+
+
+def bench_lm_head(dims, rows, iters, g):
+    D, V = dims.hidden, dims.vocab
+    B1, N = max(1, rows // 32), 32
+    h = torch.randn(B1 * N, D, generator=g).to(torch.bfloat16).cuda()
+    nw = torch.ones(D, dtype=torch.bfloat16, device="cuda")
+    w = (torch.randn(V, D, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    err = K.error_word("cuda")
+    ms = _events(lambda: K.final_norm_lm_head(h, nw, w, B1, N, 1e-6, 1, err=err), iters)
+    K.raise_device_error(err)
+    return _report("lm_head", ms, V * D * 2 + B1 * N * V * 2, 2 * B1 * N * V * D,
+                   {"rows": B1 * N})
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", required=True,
+                    choices=["qkv", "o_proj", "ffn", "lm_head", "all_gemm"])
+    ap.add_argument("--shape", default="qwen7b", choices=sorted(SHAPES))
+    ap.add_argument("--rows", type=int, default=122)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args()
+    _lib.check(_lib.load().sf_check_device(), "device")
+    dims = SHAPES[args.shape]
+    g = torch.Generator().manual_seed(args.seed)
+    todo = ["qkv", "o_proj", "ffn", "lm_head"] if args.kernel == "all_gemm" else [args.kernel]
+    for k in todo:
+        rows = 256 if k in ("o_proj", "lm_head") and args.kernel == "all_gemm" else args.rows
+        {"qkv": bench_qkv, "o_proj": bench_o_proj, "ffn": bench_ffn,
+         "lm_head": bench_lm_head}[k](dims, rows, args.iters, g)
+
+
+if __name__ == "__main__":
+    main()

@@ -33,8 +33,8 @@ def test_every_declared_symbol_is_exported_and_bound():
 def test_abi_version_and_workspace_sizes():
     lib = _lib.load()
     assert lib.sf_abi_version() == 1
-    small = lib.sf_verify_workspace_bytes(1, 8, 32, 256, 4, 2, 64, 384, 128)
-    big = lib.sf_verify_workspace_bytes(1, 8, 32, 3584, 28, 4, 128, 18944, 152064)
+    small = lib.sf_verify_workspace_bytes(1, 8, 32, 256, 4, 2, 64, 384, 128, 64)
+    big = lib.sf_verify_workspace_bytes(1, 8, 32, 3584, 28, 4, 128, 18944, 152064, 1024)
     assert 0 < small < big < (1 << 30)
 
 
