@@ -201,6 +201,9 @@ typedef struct sf_verify_args {
   int bucket;                  /* compaction capacity (<= B1*N) */
   float delta, eps, scale;     /* recompute threshold, RMSNorm eps, attention scale */
   int shift_logits;            /* 1 for Fast-dLLM, 0 for NLD */
+  int weights_tiled;           /* bf16 only: w_qkv, w_o, w_gate (gate+up), w_down and lm_w
+                                  are in the tile layout of sf_pack_weight_tiles (w_up is
+                                  then unused) */
   const sf_layer* layers;      /* HOST array of L layers */
   const void* final_norm_w;    /* [D] */
   const void* lm_w;            /* [V, D] */
@@ -231,6 +234,16 @@ int sf_profile_end(void);
 int sf_profile_kinds(void);
 const char* sf_profile_name(int kind);
 int sf_profile_kind(int kind, double* total_ms, int* calls);
+
+/* Weight tile layout for the tensor-core projections (bf16): [n_tiles][K/64][128][64],
+ * i.e. every 128-row x 64-column block of W stored contiguously, so one pipeline stage
+ * is one 16 KB read.  mode 0: W [n_out, K]; mode 1 (SwiGLU): each 128-row block holds
+ * 64 rows of W (gate) then the same 64 rows of W2 (up), n_out = 2*inter.  Packing is a
+ * one-time copy per model (the reference packs [Wq;Wk;Wv] and [Wg;Wu] likewise,
+ * fastdllm_v2_folded.py:77-87).                                                      */
+size_t sf_weight_tiles_bytes(int n_out, int K, int mode, int inter);
+int sf_pack_weight_tiles(const void* W, const void* W2, int n_out, int K, int mode, int inter,
+                         void* dst, void* stream);
 
 size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
                                  int V, int P);

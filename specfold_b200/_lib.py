@@ -34,6 +34,7 @@ class SfVerifyArgs(C.Structure):
         ("Hkv", c_int), ("hd", c_int), ("I", c_int), ("V", c_int), ("L", c_int), ("P", c_int),
         ("kv_head_stride", c_int64), ("bucket", c_int),
         ("delta", c_float), ("eps", c_float), ("scale", c_float), ("shift_logits", c_int),
+        ("weights_tiled", c_int),
         ("layers", C.POINTER(SfLayer)), ("final_norm_w", c_void_p), ("lm_w", c_void_p),
         ("par_idx", c_void_p), ("hidden_in", c_void_p), ("cos", c_void_p), ("sin", c_void_p),
         ("q_scale", c_void_p), ("logits", c_void_p), ("count_slab", c_void_p),
@@ -83,6 +84,9 @@ _SIGS = {
                                       c_size_t, c_void_p, c_void_p]),
     "sf_kv_append": (c_int, [c_int, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
                              c_int, c_int, c_int, c_int, c_void_p]),
+    "sf_weight_tiles_bytes": (c_size_t, [c_int] * 4),
+    "sf_pack_weight_tiles": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                     c_void_p]),
     "sf_launch_count": (C.c_longlong, []),
     "sf_profile_begin": (c_int, [c_int]),
     "sf_profile_end": (c_int, []),

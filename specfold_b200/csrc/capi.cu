@@ -122,6 +122,7 @@ struct FwdBufs {
   float *M, *Z, *rstd, *rstd2;
   int64_t *f, *src, *seg, *rows;
   int8_t* rec;
+  int32_t* frows;
   size_t gemm_ws_bytes, attn_ws_bytes, total;
 };
 
@@ -148,6 +149,7 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   b.seg = static_cast<int64_t*>(c.take(static_cast<size_t>(BN) * 8));
   b.rows = static_cast<int64_t*>(c.take(static_cast<size_t>(bucket) * 8));
   b.rec = static_cast<int8_t*>(c.take(static_cast<size_t>(BN)));
+  b.frows = static_cast<int32_t*>(c.take(static_cast<size_t>(BN) * 4));
   size_t g = 0;
   g = std::max(g, ws_gemm(dtype, bucket, qd + 2 * kvd, D, EPI_QKV, 0));
   g = std::max(g, ws_gemm(dtype, BN, D, qd, EPI_RESID, 0));
@@ -572,7 +574,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
 
   for (int li = 0; li < L; ++li) {
     const sf_layer& ly = a->layers[li];
-    if (!ly.w_qkv || !ly.ln1_w || !ly.w_o || !ly.ln2_w || !ly.w_gate || !ly.w_up || !ly.w_down ||
+    if (!ly.w_qkv || !ly.ln1_w || !ly.w_o || !ly.ln2_w || !ly.w_gate ||
+        (!ly.w_up && !a->weights_tiled) || !ly.w_down ||
         (a->P > 0 && (!ly.prefix_k || !ly.prefix_v)))
       return fail(SF_ERR_ARG, "layer %d: null weight", li);
     const void* Hf = li == 0 ? a->hidden_in : b.hbuf;
@@ -610,6 +613,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     c.rstd = b.rstd;
     c.ln_w = ly.ln1_w;
     c.xn = b.xn;
+    c.frows = b.frows;
     c.B1 = B1;
     c.N = N;
     c.D = D;
@@ -622,6 +626,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     q.dtype = dtype;
     q.X = b.xn;
     q.W = ly.w_qkv;
+    q.w_tiled = a->weights_tiled;
     q.n_out = qd + 2 * kvd;
     q.K = D;
     q.rows_cap = bucket;
@@ -680,6 +685,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     m.rec = rec;
     m.seg = b.seg;
     m.segcnt = segcnt;
+    m.frows = b.frows;
+    m.count = count;
     m.O = b.O;
     m.M = b.M;
     m.Z = b.Z;
@@ -697,6 +704,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     o.dtype = dtype;
     o.X = b.O;
     o.W = ly.w_o;
+    o.w_tiled = a->weights_tiled;
     o.n_out = D;
     o.K = qd;
     o.rows_cap = BN;
@@ -728,6 +736,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     gu.dtype = dtype;
     gu.X = b.xn;
     gu.W = ly.w_gate;
+    gu.w_tiled = a->weights_tiled;
     gu.W2 = ly.w_up;
     gu.n_out = 2 * I;
     gu.K = D;
@@ -745,6 +754,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     dn.dtype = dtype;
     dn.X = b.act;
     dn.W = ly.w_down;
+    dn.w_tiled = a->weights_tiled;
     dn.n_out = D;
     dn.K = I;
     dn.rows_cap = bucket;
@@ -779,6 +789,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   lm.dtype = dtype;
   lm.X = b.xn;
   lm.W = a->lm_w;
+  lm.w_tiled = a->weights_tiled;
   lm.n_out = V;
   lm.K = D;
   lm.rows_cap = BN;
@@ -791,6 +802,19 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   lm.ws_bytes = b.gemm_ws_bytes;
   lm.err = a->err;
   return timed(K_LM_HEAD, st, [&] { return run_gemm(lm, a->stream, "lm_head"); });
+}
+
+size_t sf_weight_tiles_bytes(int n_out, int K, int mode, int inter) {
+  return weight_tiles_bytes(n_out, K, mode, inter);
+}
+
+int sf_pack_weight_tiles(const void* W, const void* W2, int n_out, int K, int mode, int inter,
+                         void* dst, void* stream) {
+  if (!W || !dst || K <= 0 || K % 8 || (mode != 0 && mode != 1) || (mode == 1 && (!W2 || inter <= 0)) ||
+      (mode == 0 && n_out <= 0) || !aligned16(W) || !aligned16(dst) || (W2 && !aligned16(W2)))
+    return fail(SF_ERR_ARG, "bad weight tiling arguments");
+  return cuda_status(pack_weight_tiles(W, W2, n_out, K, mode, inter, dst, S(stream)),
+                     "pack weight tiles");
 }
 
 long long sf_launch_count(void) { return sf::g_launches.load(); }

@@ -11,41 +11,34 @@
 //                        final norm (triton_kernels.py:90-99, fastdllm_v2_folded.py:365)
 //   combine_kernel     : hidden = hp + ffn[src*N + n] (fastdllm_v2_folded.py:361)
 //
-// All kernels are HBM/latency bound; rows are read with 16-byte vector loads.
+// All are latency/HBM bound.  Rows are walked in chunks of kChunkVec 16-byte vectors per
+// lane whose loads are all issued before any is used, so a row costs a couple of memory
+// round trips instead of one per vector.
 #include "sf_kernels.cuh"
 
 namespace sf {
 
-// Squared norm of a row of D elements, warp-cooperative, 16-byte vectors.
-template <typename T>
-__device__ __forceinline__ float row_sumsq(const T* x, int D, int lane) {
-  constexpr int V = Elt<T>::kVec;
-  float acc = 0.f;
-  for (int d = lane * V; d < D; d += 32 * V) {
-    float v[V];
-    load_vec<T>(x + d, v);
-#pragma unroll
-    for (int i = 0; i < V; ++i) acc = fmaf(v[i], v[i], acc);
-  }
-  return warp_sum(acc);
-}
+constexpr int kChunkVec = 8;   // 16-byte vectors per lane in flight per chunk
 
 // One CTA per block position n; warp b handles branch b's row r = b*N + n.
 // With hp != nullptr the row is first rebuilt as hidden = T(hp + ffn[src*N+n]) and
 // written to `hidden` (the previous layer's combine); otherwise `hidden` is read.
+constexpr int kGateWarps = 8;   // warps per gate CTA; warp w takes branches w, w+8, ...
+
 template <typename T>
-__global__ void __launch_bounds__(32 * kMaxBranches) gate_rows_kernel(GateRowsParams p) {
+__global__ void __launch_bounds__(32 * kGateWarps) gate_rows_kernel(GateRowsParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* rows_s = reinterpret_cast<T*>(smem_raw);  // [B1][D]
   constexpr int V = Elt<T>::kVec;
+  constexpr int STEP = 32 * V * kChunkVec;
   const int n = blockIdx.x;
-  const int b = threadIdx.x >> 5;
+  const int wid = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int D = p.D, N = p.N, B1 = p.B1;
-  if (b >= B1) return;
+  T* hidden = reinterpret_cast<T*>(p.hidden);
+  for (int b = wid; b < B1; b += kGateWarps) {
   const int64_t r = static_cast<int64_t>(b) * N + n;
   T* mine = rows_s + static_cast<size_t>(b) * D;
-  T* hidden = reinterpret_cast<T*>(p.hidden);
 
   float ss = 0.f;
   if (p.hp != nullptr) {
@@ -53,33 +46,59 @@ __global__ void __launch_bounds__(32 * kMaxBranches) gate_rows_kernel(GateRowsPa
     int64_t s = p.src[r];
     if (s < 0 || s >= B1) { flag_error(p.err, SF_DEV_ERR_INDEX); s = b; }
     const T* ff = reinterpret_cast<const T*>(p.ffn) + (s * N + n) * D;
-    for (int d = lane * V; d < D; d += 32 * V) {
-      float a[V], c[V];
-      load_vec<T>(hp + d, a);
-      load_vec<T>(ff + d, c);
+    for (int base = 0; base < D; base += STEP) {
+      float a[kChunkVec][V], c[kChunkVec][V];
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        a[i] = Elt<T>::rnd(a[i] + c[i]);
-        ss = fmaf(a[i], a[i], ss);
+      for (int i = 0; i < kChunkVec; ++i) {
+        const int d = base + (lane + 32 * i) * V;
+        if (d < D) {
+          load_vec<T>(hp + d, a[i]);
+          load_vec<T>(ff + d, c[i]);
+        }
       }
-      store_vec<T>(hidden + r * D + d, a);
-      store_vec<T>(mine + d, a);
+#pragma unroll
+      for (int i = 0; i < kChunkVec; ++i) {
+        const int d = base + (lane + 32 * i) * V;
+        if (d < D) {
+#pragma unroll
+          for (int k = 0; k < V; ++k) {
+            a[i][k] = Elt<T>::rnd(a[i][k] + c[i][k]);
+            ss = fmaf(a[i][k], a[i][k], ss);
+          }
+          store_vec<T>(hidden + r * D + d, a[i]);
+          store_vec<T>(mine + d, a[i]);
+        }
+      }
     }
   } else {
     const T* x = hidden + r * D;
-    for (int d = lane * V; d < D; d += 32 * V) {
-      float a[V];
-      load_vec<T>(x + d, a);
+    for (int base = 0; base < D; base += STEP) {
+      float a[kChunkVec][V];
 #pragma unroll
-      for (int i = 0; i < V; ++i) ss = fmaf(a[i], a[i], ss);
-      store_vec<T>(mine + d, a);
+      for (int i = 0; i < kChunkVec; ++i) {
+        const int d = base + (lane + 32 * i) * V;
+        if (d < D) load_vec<T>(x + d, a[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < kChunkVec; ++i) {
+        const int d = base + (lane + 32 * i) * V;
+        if (d < D) {
+#pragma unroll
+          for (int k = 0; k < V; ++k) ss = fmaf(a[i][k], a[i][k], ss);
+          store_vec<T>(mine + d, a[i]);
+        }
+      }
     }
   }
   ss = warp_sum(ss);
   if (p.rstd && lane == 0) p.rstd[r] = 1.0f / sqrtf(ss / static_cast<float>(D) + p.eps);
+  }
   if (p.rec == nullptr) return;   // combine-only use
   __syncthreads();
 
+  for (int b = wid; b < B1; b += kGateWarps) {
+  const int64_t r = static_cast<int64_t>(b) * N + n;
+  const T* mine = rows_s + static_cast<size_t>(b) * D;
   int recompute = 1;
   int64_t par = 0;
   if (b > 0) {
@@ -110,6 +129,59 @@ __global__ void __launch_bounds__(32 * kMaxBranches) gate_rows_kernel(GateRowsPa
     p.rec[r] = static_cast<int8_t>(recompute);
     p.f[r] = recompute ? b : par;
   }
+  }
+}
+
+// out = T(w * T(x * rs)) for one row, chunked (x may alias nothing written here).
+template <typename T>
+__device__ __forceinline__ void norm_row_write(const T* x, const T* lw, T* out, int D, int lane,
+                                               float rs) {
+  constexpr int V = Elt<T>::kVec;
+  constexpr int STEP = 32 * V * kChunkVec;
+  for (int base = 0; base < D; base += STEP) {
+    float a[kChunkVec][V], g[kChunkVec][V];
+#pragma unroll
+    for (int i = 0; i < kChunkVec; ++i) {
+      const int d = base + (lane + 32 * i) * V;
+      if (d < D) {
+        load_vec<T>(x + d, a[i]);
+        load_vec<T>(lw + d, g[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kChunkVec; ++i) {
+      const int d = base + (lane + 32 * i) * V;
+      if (d < D) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) a[i][k] = g[i][k] * Elt<T>::rnd(a[i][k] * rs);
+        store_vec<T>(out + d, a[i]);
+      }
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float row_sumsq_chunked(const T* x, int D, int lane) {
+  constexpr int V = Elt<T>::kVec;
+  constexpr int STEP = 32 * V * kChunkVec;
+  float acc = 0.f;
+  for (int base = 0; base < D; base += STEP) {
+    float a[kChunkVec][V];
+#pragma unroll
+    for (int i = 0; i < kChunkVec; ++i) {
+      const int d = base + (lane + 32 * i) * V;
+      if (d < D) load_vec<T>(x + d, a[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kChunkVec; ++i) {
+      const int d = base + (lane + 32 * i) * V;
+      if (d < D) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc = fmaf(a[i][k], a[i][k], acc);
+      }
+    }
+  }
+  return warp_sum(acc);
 }
 
 // Block-wide exclusive scan of 0/1 flags (BN <= kMaxRows) -> slot per row.
@@ -117,6 +189,7 @@ __global__ void __launch_bounds__(32 * kMaxBranches) gate_rows_kernel(GateRowsPa
 template <typename T>
 __global__ void __launch_bounds__(256) compact_kernel(CompactParams p) {
   __shared__ int s_slot[kMaxRows];
+  __shared__ int8_t s_f[kMaxRows];   // parent-or-self branch per flat row
   __shared__ int s_warp[8];
   const int BN = p.B1 * p.N;
   const int tid = threadIdx.x;
@@ -150,7 +223,17 @@ __global__ void __launch_bounds__(256) compact_kernel(CompactParams p) {
   for (int i = 0; i < kPer; ++i) {
     const int r = tid * kPer + i;
     if (r < kMaxRows) s_slot[r] = flags[i] ? run : -1;
+    // folded rows are listed in order too: slot = r - (recomputed rows before r)
+    if (blockIdx.x == 0 && p.frows != nullptr && r < BN && !flags[i]) p.frows[r - run] = r;
     run += flags[i];
+  }
+
+  if (blockIdx.x == 0) {
+    for (int r = tid; r < BN; r += blockDim.x) {
+      int64_t fv = p.f[r];
+      if (fv < 0 || fv >= p.B1) { flag_error(p.err, SF_DEV_ERR_INDEX); fv = 0; }
+      s_f[r] = static_cast<int8_t>(fv);
+    }
   }
   __syncthreads();
 
@@ -161,11 +244,10 @@ __global__ void __launch_bounds__(256) compact_kernel(CompactParams p) {
       if (s >= 0 && s < p.bucket) p.rows[s] = r;
       // src: follow f (branch indices) to the recomputing ancestor
       const int n = r % p.N;
-      int64_t c = p.f[r];
+      int c = s_f[r];
       int hops = 0;
       while (hops <= p.B1) {
-        if (c < 0 || c >= p.B1) { flag_error(p.err, SF_DEV_ERR_INDEX); c = 0; break; }
-        const int64_t nx = p.f[c * p.N + n];
+        const int nx = s_f[c * p.N + n];
         if (nx == c) break;
         c = nx;
         ++hops;
@@ -186,23 +268,14 @@ __global__ void __launch_bounds__(256) compact_kernel(CompactParams p) {
 
   // normalised A operand of the QKV projection: xn[slot] = T(w * T(x * rstd))
   if (p.xn == nullptr) return;
-  constexpr int V = Elt<T>::kVec;
   const int warps_total = gridDim.x * (blockDim.x >> 5);
   for (int r = blockIdx.x * (blockDim.x >> 5) + w; r < BN; r += warps_total) {
     const int s = s_slot[r];
     if (s < 0 || s >= p.bucket) continue;
-    const T* x = reinterpret_cast<const T*>(p.hidden) + static_cast<int64_t>(r) * p.D;
-    const T* lw = reinterpret_cast<const T*>(p.ln_w);
-    T* out = reinterpret_cast<T*>(p.xn) + static_cast<int64_t>(s) * p.D;
-    const float rs = p.rstd[r];
-    for (int d = lane * V; d < p.D; d += 32 * V) {
-      float a[V], g[V];
-      load_vec<T>(x + d, a);
-      load_vec<T>(lw + d, g);
-#pragma unroll
-      for (int i = 0; i < V; ++i) a[i] = g[i] * Elt<T>::rnd(a[i] * rs);
-      store_vec<T>(out + d, a);
-    }
+    norm_row_write<T>(reinterpret_cast<const T*>(p.hidden) + static_cast<int64_t>(r) * p.D,
+                      reinterpret_cast<const T*>(p.ln_w),
+                      reinterpret_cast<T*>(p.xn) + static_cast<int64_t>(s) * p.D, p.D, lane,
+                      p.rstd[r]);
   }
 }
 
@@ -227,7 +300,6 @@ __global__ void src_resolve_kernel(const int64_t* f, int64_t* src, int B1, int N
 // out[i] = T(w * T(x[row(i)] * rstd)), row(i) = rows ? rows[i] : i, for i < min(*count, n).
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(RmsRowsParams p) {
-  constexpr int V = Elt<T>::kVec;
   const int lane = threadIdx.x & 31;
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int n = p.n;
@@ -236,19 +308,11 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(RmsRowsParams p) {
   int64_t row = p.rows ? p.rows[w] : w;
   if (row < 0 || row >= p.n_src) { flag_error(p.err, SF_DEV_ERR_INDEX); return; }
   const T* x = reinterpret_cast<const T*>(p.x) + row * p.D;
-  const T* lw = reinterpret_cast<const T*>(p.w);
-  T* out = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(w) * p.D;
-  const float ss = row_sumsq<T>(x, p.D, lane);
+  const float ss = row_sumsq_chunked<T>(x, p.D, lane);
   const float rs = 1.0f / sqrtf(ss / static_cast<float>(p.D) + p.eps);
   if (p.rstd && lane == 0) p.rstd[w] = rs;
-  for (int d = lane * V; d < p.D; d += 32 * V) {
-    float a[V], g[V];
-    load_vec<T>(x + d, a);
-    load_vec<T>(lw + d, g);
-#pragma unroll
-    for (int i = 0; i < V; ++i) a[i] = g[i] * Elt<T>::rnd(a[i] * rs);
-    store_vec<T>(out + d, a);
-  }
+  norm_row_write<T>(x, reinterpret_cast<const T*>(p.w),
+                    reinterpret_cast<T*>(p.out) + static_cast<int64_t>(w) * p.D, p.D, lane, rs);
 }
 
 // hidden[r] = T(hp[r] + ffn[src[r]*N + n]); one warp per row.
@@ -257,6 +321,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* hp, const T* ffn,
                                                      const int64_t* src, T* hidden, int B1,
                                                      int N, int D, int* err) {
   constexpr int V = Elt<T>::kVec;
+  constexpr int STEP = 32 * V * kChunkVec;
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= B1 * N) return;
@@ -266,13 +331,25 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* hp, const T* ffn,
   const T* a = hp + static_cast<int64_t>(r) * D;
   const T* c = ffn + (s * N + n) * D;
   T* o = hidden + static_cast<int64_t>(r) * D;
-  for (int d = lane * V; d < D; d += 32 * V) {
-    float x[V], y[V];
-    load_vec<T>(a + d, x);
-    load_vec<T>(c + d, y);
+  for (int base = 0; base < D; base += STEP) {
+    float x[kChunkVec][V], y[kChunkVec][V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) x[i] = x[i] + y[i];
-    store_vec<T>(o + d, x);
+    for (int i = 0; i < kChunkVec; ++i) {
+      const int d = base + (lane + 32 * i) * V;
+      if (d < D) {
+        load_vec<T>(a + d, x[i]);
+        load_vec<T>(c + d, y[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kChunkVec; ++i) {
+      const int d = base + (lane + 32 * i) * V;
+      if (d < D) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) x[i][k] = x[i][k] + y[i][k];
+        store_vec<T>(o + d, x[i]);
+      }
+    }
   }
 }
 
@@ -286,7 +363,7 @@ static cudaError_t launch_gate_rows_t(const GateRowsParams& p, cudaStream_t st) 
                          kMaxGateSmem);
     configured = true;
   }
-  gate_rows_kernel<T><<<p.N, 32 * p.B1, smem, st>>>(p);
+  gate_rows_kernel<T><<<p.N, 32 * std::min(p.B1, kGateWarps), smem, st>>>(p);
   return launched();
 }
 cudaError_t launch_gate_rows(int dtype, const GateRowsParams& p, cudaStream_t st) {

@@ -1,0 +1,716 @@
+// Tensor-core (tcgen05) weight-streaming GEMM of the folded verify forward, bf16.
+//
+// acc[j][f] = sum_k X[j][k] * W[f][k] for the few activation rows j (recomputed rows,
+// <= B1*N) against a large weight matrix W [n_out, K].  At the model shapes this is
+// HBM-bound on the weight stream, so the kernel is built around it:
+//   * "swap-AB": 128 weight rows are the MMA's M operand, the activation rows its N
+//     operand (N = rows rounded up to 16), fp32 accumulators in TMEM;
+//   * a CTA streams `sub` (1 or 2) 128-row weight tiles per pipeline stage against one
+//     shared activation stage, so the activations (re-read from L2 by every CTA) cost
+//     half as much per weight byte when sub = 2;
+//   * weights optionally pre-arranged in 128x64 blocks (weight_tiles_bytes), making a
+//     stage's 16 KB of each tile one contiguous read;
+//   * TMA loads (128-byte swizzle, no multicast), stage count sized in the kernel from
+//     the actual row count;
+//   * persistent CTAs over units (tile group, K split); with several units per CTA the
+//     accumulators are double-buffered so one unit's epilogue overlaps the next mainloop;
+//   * few tile groups (QKV, o_proj, down) split K across co-resident CTAs (cooperative
+//     launch): each publishes fp32 partials, waits (bounded) for its group's other
+//     splits, and reduces its own slice of rows in split order -- deterministic.
+// Warp 0 issues TMA, warp 1 owns TMEM and issues MMAs, warps 2-5 run the epilogue.
+//
+// Epilogues reproduce the rounding points of the PyTorch folded forward:
+//   QKV     F.linear + bias rounded to the model dtype, then q*c + rot(q)*s with every
+//           op rounded (fastdllm_v2_folded.py:153-157; triton_kernels.py:65-87); also
+//           writes the query copy the tensor-core attention reads
+//   RESID   x + T(O @ Wo^T) (fastdllm_v2_folded.py:207-208, :351)
+//   SWIGLU  T(silu(T(g))) * T(u) (fastdllm_v2_folded.py:216; triton_kernels.py:133)
+//   SCATTER ffn_buf[rows[j]] = T(acc) (triton_kernels.py:171-173)
+//   LOGITS  lm_head with the Fast-dLLM shift (fastdllm_v2_generation.py:121-126)
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <mutex>
+
+#include "sf_kernels.cuh"
+
+namespace sf {
+
+constexpr int kTcThreads = 192;
+constexpr int kTileF = 128;                      // weight rows per tile (MMA M)
+constexpr int kBK = 64;                          // K per stage: one 128-byte swizzle row
+constexpr int kMaxPassRows = 256;                // MMA N limit
+constexpr int kWBytes = kTileF * kBK * 2;        // 16 KB per tile per stage
+constexpr int kXBoxRows = 64;
+constexpr int kXBoxBytes = kXBoxRows * kBK * 2;  // 8 KB
+constexpr int kChunk = 32;                       // rows per epilogue chunk
+constexpr int kTileLd = kTileF + 4;              // padded fp32 row of the transposed chunk
+constexpr int kTileTBytes = kChunk * kTileLd * 4;
+constexpr int kMaxStages = 8;
+constexpr int kSmemFixed = kTileTBytes + 1024 + 256;   // transposed chunk, alignment, barriers
+// split-K counters (arrivals, departures) per tile group at offset 0 of the workspace
+constexpr int kMaxCounterTiles = static_cast<int>(kGemmCounterBytes / 8);
+
+struct TcParams {
+  int n_out, K, rows_cap;
+  const int32_t* count;
+  int mode;            // 0: 128-row tiles of W; 1: SWIGLU, 64 gate + 64 up rows per tile
+  int inter;
+  int n_tiles;         // 128-row weight tiles
+  int sub;             // tiles per unit sharing one activation stage (1 or 2)
+  int n_groups;        // ceil(n_tiles / sub)
+  int splits, kb_total, kb_per_split, n_units;
+  int double_buf, acc_cols;
+  int w_tiled;         // weights in the [tile][kb][128][64] layout
+  int stage_budget;    // shared-memory bytes for the pipeline stages
+  float* partial;      // [splits][rows_cap][n_out] when splits > 1
+  int* counters;       // [2 * n_groups]
+  EpiParams epi;
+  int* err;
+};
+
+// natural feature index of tile-local weight row l, or -1 past the end
+__device__ __forceinline__ int tc_feature(const TcParams& p, int tile, int l) {
+  if (tile >= p.n_tiles) return -1;
+  if (p.mode == 1) {
+    const int g = tile * 64 + (l & 63);
+    if (g >= p.inter) return -1;
+    return l < 64 ? g : p.inter + g;
+  }
+  const int f = tile * kTileF + l;
+  return f < p.n_out ? f : -1;
+}
+
+template <typename T>
+__device__ __forceinline__ void ld8(const void* base, int64_t i, float* v) {
+  load_vec<T>(reinterpret_cast<const T*>(base) + i, v);
+  if (Elt<T>::kVec == 4) load_vec<T>(reinterpret_cast<const T*>(base) + i + 4, v + 4);
+}
+template <typename T>
+__device__ __forceinline__ void st8(void* base, int64_t i, const float* v) {
+  store_vec<T>(reinterpret_cast<T*>(base) + i, v);
+  if (Elt<T>::kVec == 4) store_vec<T>(reinterpret_cast<T*>(base) + i + 4, v + 4);
+}
+
+// Epilogue of 8 consecutive tile-local weight rows l0..l0+7 for activation row j:
+// v = their accumulators, vp = the partner rows' (RoPE pair / SwiGLU up half).
+__device__ __forceinline__ void epi_group8(const TcParams& p, int tile, int j, int l0,
+                                           const float* v, const float* vp) {
+  using T = __nv_bfloat16;
+  const EpiParams& e = p.epi;
+  const int f0 = tc_feature(p, tile, l0);
+  if (f0 < 0) return;
+  float o[8];
+  switch (e.kind) {
+    case EPI_RAW:
+      store_vec<float>(reinterpret_cast<float*>(e.out) + static_cast<int64_t>(j) * e.ld_out + f0, v);
+      store_vec<float>(reinterpret_cast<float*>(e.out) + static_cast<int64_t>(j) * e.ld_out + f0 + 4, v + 4);
+      return;
+    case EPI_QKV: {
+      const int64_t row = e.rows[j];
+      const int n = static_cast<int>(row % e.N);
+      const int fp0 = f0 ^ (e.hd >> 1);
+      float x[8], xp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { x[i] = v[i]; xp[i] = vp[i]; }
+      if (e.bias) {
+        float b[8], bp[8];
+        ld8<T>(e.bias, f0, b);
+        ld8<T>(e.bias, fp0, bp);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { x[i] = __fadd_rn(x[i], b[i]); xp[i] = __fadd_rn(xp[i], bp[i]); }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { o[i] = Elt<T>::rnd(x[i]); xp[i] = Elt<T>::rnd(xp[i]); }
+      if (f0 < e.q_dim + e.kv_dim) {
+        const int d0 = f0 % e.hd;
+        float c[8], s[8];
+        ld8<T>(e.cos, static_cast<int64_t>(n) * e.hd + d0, c);
+        ld8<T>(e.sin, static_cast<int64_t>(n) * e.hd + d0, s);
+        const bool first = d0 < (e.hd >> 1);
+        const float qs = (f0 < e.q_dim && e.q_scale) ? Elt<T>::rnd(e.q_scale[n]) : 1.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float rot = first ? -xp[i] : xp[i];
+          float r = Elt<T>::rnd(__fadd_rn(Elt<T>::rnd(__fmul_rn(o[i], c[i])),
+                                          Elt<T>::rnd(__fmul_rn(rot, s[i]))));
+          if (f0 < e.q_dim && e.q_scale) r = Elt<T>::rnd(__fmul_rn(r, qs));
+          o[i] = r;
+        }
+      }
+      if (f0 < e.q_dim) {
+        st8<T>(e.out, row * e.q_dim + f0, o);
+        if (e.q_comp) {   // query-major copy per kv head for the tensor-core attention
+          const int G = e.q_dim / e.kv_dim;
+          const int h = f0 / e.hd;
+          st8<T>(e.q_comp,
+                 ((static_cast<int64_t>(h / G) * e.q_comp_rows + static_cast<int64_t>(j) * G +
+                   h % G) * e.hd) + f0 % e.hd, o);
+        }
+      } else {
+        st8<T>(e.out2, row * (2 * e.kv_dim) + (f0 - e.q_dim), o);
+      }
+      return;
+    }
+    case EPI_RESID: {
+      const int64_t i0 = static_cast<int64_t>(j) * e.ld_out + f0;
+      float r[8];
+      ld8<T>(e.resid, i0, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(r[i], Elt<T>::rnd(v[i]));
+      st8<T>(e.out, i0, o);
+      return;
+    }
+    case EPI_SWIGLU: {
+      if (f0 >= e.inter) return;   // up half: consumed by its gate partner
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float g = Elt<T>::rnd(v[i]), u = Elt<T>::rnd(vp[i]);
+        o[i] = __fmul_rn(Elt<T>::rnd(g / (1.0f + expf(-g))), u);
+      }
+      st8<T>(e.out, static_cast<int64_t>(j) * e.inter + f0, o);
+      return;
+    }
+    case EPI_SCATTER:
+      st8<T>(e.out, e.rows[j] * e.ld_out + f0, v);
+      return;
+    case EPI_LOGITS: {
+      const int n = j % e.N;
+      const int64_t b = j / e.N;
+      if (e.shift) {
+        if (n + 1 < e.N) st8<T>(e.out, (b * e.N + n + 1) * e.ld_out + f0, v);
+        if (n == 0) st8<T>(e.out, (b * e.N) * e.ld_out + f0, v);
+      } else {
+        st8<T>(e.out, static_cast<int64_t>(j) * e.ld_out + f0, v);
+      }
+      return;
+    }
+    default:
+      return;
+  }
+}
+
+// tile-local partner of weight row l0 (first of a group of 8)
+__device__ __forceinline__ int tc_partner_l(const TcParams& p, int l0) {
+  if (p.epi.kind == EPI_QKV) return l0 ^ (p.epi.hd >> 1);
+  if (p.epi.kind == EPI_SWIGLU) return l0 ^ 64;
+  return l0;
+}
+
+// AND over the 128 epilogue threads (named barrier 1): keeps every branch that
+// guards a named barrier uniform, whatever each thread saw of the abort flag.
+__device__ __forceinline__ bool epi_vote_all(bool x) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(x))
+      : "memory");
+  return r != 0;
+}
+
+// First k-block of unit u's K range (nkb blocks).  CTAs start at different k-blocks so
+// that, at any moment, they read different activation blocks: every CTA reads the same
+// activations, and in lockstep all 148 SMs would request the same L2 lines at once.
+// The order is a fixed function of the unit, so results are deterministic.
+__device__ __forceinline__ int kb_rotation(int u, int nkb) {
+  return nkb > 1 ? static_cast<int>((static_cast<unsigned>(u) * 7919u) % static_cast<unsigned>(nkb)) : 0;
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmW2,
+                   const __grid_constant__ CUtensorMap tmX, TcParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int rows = p.rows_cap;
+  if (p.count) rows = min(rows, *p.count);
+  if (rows <= 0) return;                         // uniform over the grid
+  const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
+  // stage layout from the actual row count: sub weight tiles + the activation boxes
+  const int x_boxes = (min(rows, kMaxPassRows) + kXBoxRows - 1) / kXBoxRows;
+  const int w_bytes = p.sub * kWBytes;
+  const int stage_bytes = w_bytes + x_boxes * kXBoxBytes;
+  const int stages = min(kMaxStages, p.stage_budget / stage_bytes);
+  unsigned char* stage_base = smem;
+  float* tileT = reinterpret_cast<float*>(smem + p.stage_budget);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.stage_budget + kTileTBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMaxStages;
+  uint64_t* acc_full = bars + 2 * kMaxStages;    // [2]
+  uint64_t* acc_empty = acc_full + 2;            // [2]
+  uint64_t* drain = acc_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t tmem_cols = (p.double_buf ? 2u : 1u) * p.sub * p.acc_cols;
+  const uint32_t buf_cols = p.sub * p.acc_cols;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+    if (p.mode == 1 && !p.w_tiled) tma_prefetch_desc(&tmW2);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int it = 0;
+      for (int u = blockIdx.x; u < p.n_units && !*abort_flag; u += gridDim.x) {
+        const int grp = u / p.splits, split = u % p.splits;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        for (int pass = 0; pass < n_pass && !*abort_flag; ++pass) {
+          const int prow0 = pass * kMaxPassRows;
+          const int prows = min(kMaxPassRows, rows - prow0);
+          const int nbox = (prows + kXBoxRows - 1) / kXBoxRows;
+          const uint32_t bytes = w_bytes + nbox * kXBoxBytes;
+          const int nkb = kb1 - kb0, rot = kb_rotation(u, nkb);
+          for (int i = 0; i < nkb; ++i, ++it) {
+            const int kb = kb0 + (i + rot) % nkb;
+            const int s = it % stages;
+            const uint32_t ph = (it / stages) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, p.err)) { *abort_flag = 1; break; }
+            unsigned char* st = stage_base + s * stage_bytes;
+            mbar_arrive_expect_tx(&full[s], bytes);
+            const int kx = kb * kBK;
+            for (int t = 0; t < p.sub; ++t) {
+              const int tile = grp * p.sub + t;
+              unsigned char* wdst = st + t * kWBytes;
+              if (p.w_tiled) {
+                tma_load_2d(wdst, &tmW, &full[s], 0, (tile * p.kb_total + kb) * kTileF, pol_w);
+              } else if (p.mode == 1) {
+                tma_load_2d(wdst, &tmW, &full[s], kx, tile * 64, pol_w);
+                tma_load_2d(wdst + kWBytes / 2, &tmW2, &full[s], kx, tile * 64, pol_w);
+              } else {
+                tma_load_2d(wdst, &tmW, &full[s], kx, tile * kTileF, pol_w);
+              }
+            }
+            for (int b = 0; b < nbox; ++b)
+              tma_load_2d(st + w_bytes + b * kXBoxBytes, &tmX, &full[s], kx,
+                          prow0 + b * kXBoxRows, pol_x);
+          }
+        }
+      }
+      // no copy into this CTA's shared memory may still be in flight at exit
+      for (int i = max(0, it - stages); i < it; ++i)
+        mbar_wait(&full[i % stages], (i / stages) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int it = 0, acc_it = 0;
+      for (int u = blockIdx.x; u < p.n_units && !*abort_flag; u += gridDim.x) {
+        const int split = u % p.splits;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        for (int pass = 0; pass < n_pass; ++pass, ++acc_it) {
+          const int prows = min(kMaxPassRows, rows - pass * kMaxPassRows);
+          const int n_mma = ((prows + 15) / 16) * 16;
+          const uint32_t idesc = idesc_bf16(128, n_mma);
+          const int buf = p.double_buf ? (acc_it & 1) : 0;
+          const uint32_t par = p.double_buf ? ((acc_it >> 1) & 1) : (acc_it & 1);
+          if (!mbar_wait(&acc_empty[buf], par ^ 1, p.err)) { *abort_flag = 1; break; }
+          tc_fence_after();
+          const uint32_t d0 = tmem + buf * buf_cols;
+          bool ok = true;
+          for (int i = 0; i < kb1 - kb0; ++i, ++it) {
+            const int s = it % stages;
+            const uint32_t ph = (it / stages) & 1;
+            if (*abort_flag || !mbar_wait(&full[s], ph, p.err)) { *abort_flag = 1; ok = false; break; }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(stage_base + s * stage_bytes);
+            const uint32_t b0 = a0 + w_bytes;
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t bd = sdesc_kmajor_sw128(b0 + k * 32);
+              for (int t = 0; t < p.sub; ++t)
+                umma_f16(d0 + t * p.acc_cols, sdesc_kmajor_sw128(a0 + t * kWBytes + k * 32), bd,
+                         idesc, (i > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&empty[s]);
+          }
+          if (!ok) break;
+          umma_commit(&acc_full[buf]);
+        }
+      }
+      umma_commit(drain);                 // every issued MMA done before TMEM is freed
+      mbar_wait(drain, 0, p.err);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;               // TMEM lane quarter of this warp
+    const int l = q * 32 + lane;          // tile-local weight row == TMEM lane
+    const int et = threadIdx.x - 64;      // 0..127 within the epilogue warps
+    int acc_it = 0;
+    for (int u = blockIdx.x; u < p.n_units; u += gridDim.x) {
+      const int grp = u / p.splits, split = u % p.splits;
+      for (int pass = 0; pass < n_pass; ++pass, ++acc_it) {
+        const int prow0 = pass * kMaxPassRows;
+        const int prows = min(kMaxPassRows, rows - prow0);
+        const int buf = p.double_buf ? (acc_it & 1) : 0;
+        const uint32_t par = p.double_buf ? ((acc_it >> 1) & 1) : (acc_it & 1);
+        const bool ready = epi_vote_all(!*abort_flag && mbar_wait(&acc_full[buf], par, p.err));
+        if (!ready) *abort_flag = 1;
+        tc_fence_after();
+        for (int t = 0; ready && t < p.sub; ++t) {
+          const int tile = grp * p.sub + t;
+          if (tile >= p.n_tiles) break;
+          const int f = tc_feature(p, tile, l);
+          for (int c0 = 0; c0 < prows; c0 += kChunk) {
+            float v[kChunk];
+            const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                                static_cast<uint32_t>(buf * buf_cols + t * p.acc_cols + c0);
+            tmem_ld16(ta, v);
+            tmem_ld16(ta + 16, v + 16);
+            tmem_ld_wait();
+            if (p.splits > 1) {
+              if (f >= 0) {
+                float* part = p.partial +
+                              (static_cast<int64_t>(split) * p.rows_cap + prow0 + c0) * p.n_out + f;
+#pragma unroll
+                for (int i = 0; i < kChunk; ++i)
+                  if (c0 + i < prows) part[static_cast<int64_t>(i) * p.n_out] = v[i];
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i) tileT[i * kTileLd + l] = v[i];
+              asm volatile("bar.sync 1, 128;" ::: "memory");
+              const int nr = min(kChunk, prows - c0);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int item = et + 128 * k;
+                const int r = item >> 4, l0 = (item & 15) * 8;
+                if (r < nr) {
+                  const float* a = tileT + r * kTileLd + l0;
+                  const float* b = tileT + r * kTileLd + tc_partner_l(p, l0);
+                  float va[8], vb[8];
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) { va[i] = a[i]; vb[i] = b[i]; }
+                  epi_group8(p, tile, prow0 + c0 + r, l0, va, vb);
+                }
+              }
+              asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
+          }
+        }
+        tc_fence_before();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      }
+      if (p.splits > 1) {
+        // every split of this tile group publishes, then each reduces its slice of rows
+        __threadfence();
+        bool go = epi_vote_all(!*abort_flag);
+        if (et == 0 && go) {
+          atomicAdd(&p.counters[2 * grp], 1);
+          const uint64_t t0 = globaltimer();
+          while (ld_acquire(&p.counters[2 * grp]) < p.splits) {
+            if (globaltimer() - t0 > kWaitNs) {
+              flag_error(p.err, SF_DEV_ERR_TIMEOUT);
+              *abort_flag = 1;
+              break;
+            }
+          }
+        }
+        go = epi_vote_all(!*abort_flag);
+        const int slice = (rows + p.splits - 1) / p.splits;
+        const int r0 = split * slice, r1 = min(rows, r0 + slice);
+        for (int t = 0; go && t < p.sub; ++t) {
+          const int tile = grp * p.sub + t;
+          if (tile >= p.n_tiles) break;
+          for (int c0 = r0; c0 < r1; c0 += kChunk) {
+            const int nr = min(kChunk, r1 - c0);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int item = et + 128 * k;
+              const int r = item >> 4, l0 = (item & 15) * 8;
+              if (r >= nr) continue;
+              const int fa = tc_feature(p, tile, l0);
+              if (fa < 0) continue;
+              const int fb = tc_feature(p, tile, tc_partner_l(p, l0));
+              float va[8] = {}, vb[8] = {};
+              for (int s = 0; s < p.splits; ++s) {
+                const float* row = p.partial + (static_cast<int64_t>(s) * p.rows_cap + c0 + r) * p.n_out;
+                const float4 a0 = __ldcg(reinterpret_cast<const float4*>(row + fa));
+                const float4 a1 = __ldcg(reinterpret_cast<const float4*>(row + fa + 4));
+                va[0] += a0.x; va[1] += a0.y; va[2] += a0.z; va[3] += a0.w;
+                va[4] += a1.x; va[5] += a1.y; va[6] += a1.z; va[7] += a1.w;
+                if (fb >= 0 && fb != fa) {
+                  const float4 b0 = __ldcg(reinterpret_cast<const float4*>(row + fb));
+                  const float4 b1 = __ldcg(reinterpret_cast<const float4*>(row + fb + 4));
+                  vb[0] += b0.x; vb[1] += b0.y; vb[2] += b0.z; vb[3] += b0.w;
+                  vb[4] += b1.x; vb[5] += b1.y; vb[6] += b1.z; vb[7] += b1.w;
+                }
+              }
+              epi_group8(p, tile, c0 + r, l0, va, fb == fa ? va : vb);
+            }
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (et == 0 && go) {
+          const int prev = atomicAdd(&p.counters[2 * grp + 1], 1);
+          if (prev == p.splits - 1) {      // everyone has passed the wait: reset
+            p.counters[2 * grp] = 0;
+            p.counters[2 * grp + 1] = 0;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, tmem_cols);
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// bf16 row-major [rows][cols], box [box_rows][64], 128-byte swizzle
+static bool make_tmap(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols,
+                      uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// Tuning, read once from the environment: SF_GEMM_SUB (1 or 2 weight tiles per CTA
+// stage) and SF_GEMM_SMEM_KB (shared memory per CTA; below ~113 two CTAs share an SM).
+struct TcTuning {
+  int sub = 1;
+  int smem_kb = 222;
+};
+static const TcTuning& tc_tuning() {
+  static TcTuning t;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    if (const char* v = getenv("SF_GEMM_SUB")) t.sub = std::max(1, std::min(2, atoi(v)));
+    if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(222, atoi(v)));
+  });
+  return t;
+}
+
+struct TcPlan {
+  int n_tiles, sub, n_groups, splits, kb_total, kb_per_split, acc_cols, double_buf, grid;
+  int stage_budget, ctas_per_sm;
+};
+static TcPlan tc_plan(int n_out, int K, int mode, int inter, int rows_cap) {
+  TcPlan pl{};
+  pl.n_tiles = mode == 1 ? (inter + 63) / 64 : (n_out + kTileF - 1) / kTileF;
+  pl.kb_total = (K + kBK - 1) / kBK;
+  const TcTuning& tune = tc_tuning();
+  pl.acc_cols = rows_cap <= 128 ? 128 : 256;
+  pl.sub = (tune.sub == 2 && pl.n_tiles >= 2) ? 2 : 1;
+  pl.stage_budget = tune.smem_kb * 1024 - kSmemFixed;
+  pl.ctas_per_sm = std::max(1, (227 * 1024) / (tune.smem_kb * 1024 + 1024));
+  pl.n_groups = (pl.n_tiles + pl.sub - 1) / pl.sub;
+  const int sms = num_sms();
+  int splits = 1;
+  // few tile groups: split K so that groups x splits fills the SMs (one pass of rows)
+  if (rows_cap <= kMaxPassRows && pl.n_groups < sms / 2 && pl.n_groups <= kMaxCounterTiles)
+    splits = std::max(1, std::min(sms / pl.n_groups, pl.kb_total / 4));
+  pl.kb_per_split = (pl.kb_total + splits - 1) / splits;
+  pl.splits = (pl.kb_total + pl.kb_per_split - 1) / pl.kb_per_split;  // no empty split
+  const int n_units = pl.n_groups * pl.splits;
+  pl.grid = pl.splits > 1 ? n_units : std::min(n_units, sms * pl.ctas_per_sm);
+  const bool want_double = n_units > pl.grid || rows_cap > kMaxPassRows;
+  // TMEM (512 columns per SM) is shared by the CTAs resident on an SM
+  pl.double_buf = (want_double && 2 * pl.sub * pl.acc_cols * pl.ctas_per_sm <= 512) ? 1 : 0;
+  return pl;
+}
+
+size_t gemm_tc_ws_need(int rows_cap, int n_out, int K, int kind, int inter) {
+  const int mode = kind == EPI_SWIGLU ? 1 : 0;
+  const TcPlan pl = tc_plan(n_out, K, mode, inter, rows_cap);
+  if (pl.splits <= 1) return 0;
+  return kGemmCounterBytes + static_cast<size_t>(pl.splits) * rows_cap * n_out * 4;
+}
+
+int gemm_path_is_tc(int dtype) { return dtype == BF16; }
+
+cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
+  const int mode = a.epi.kind == EPI_SWIGLU ? 1 : 0;
+  const int inter = a.epi.inter;
+  if (a.n_out % 8 != 0 || (mode == 1 && inter % 8 != 0)) return cudaErrorInvalidValue;
+  const TcPlan pl = tc_plan(a.n_out, a.K, mode, inter, a.rows_cap);
+  TcParams p{};
+  p.n_out = a.n_out;
+  p.K = a.K;
+  p.rows_cap = a.rows_cap;
+  p.count = a.count;
+  p.mode = mode;
+  p.inter = inter;
+  p.n_tiles = pl.n_tiles;
+  p.sub = pl.sub;
+  p.n_groups = pl.n_groups;
+  p.splits = pl.splits;
+  p.kb_total = pl.kb_total;
+  p.kb_per_split = pl.kb_per_split;
+  p.n_units = pl.n_groups * pl.splits;
+  p.double_buf = pl.double_buf;
+  p.acc_cols = pl.acc_cols;
+  p.w_tiled = a.w_tiled ? 1 : 0;
+  p.stage_budget = pl.stage_budget;
+  if (pl.splits > 1) {
+    const size_t need = kGemmCounterBytes + static_cast<size_t>(pl.splits) * a.rows_cap * a.n_out * 4;
+    if (a.ws == nullptr || a.ws_bytes < need) return cudaErrorInvalidValue;
+    p.counters = static_cast<int*>(a.ws);
+    p.partial = reinterpret_cast<float*>(static_cast<char*>(a.ws) + kGemmCounterBytes);
+  }
+  p.epi = a.epi;
+  p.err = a.err;
+
+  CUtensorMap tmW, tmW2, tmX;
+  if (p.w_tiled) {
+    const uint64_t blocks = static_cast<uint64_t>(pl.n_tiles) * pl.kb_total * kTileF;
+    if (!make_tmap(&tmW, a.W, blocks, kBK, kTileF)) return cudaErrorInvalidValue;
+    tmW2 = tmW;
+  } else {
+    const uint32_t wrows = mode == 1 ? 64 : kTileF;
+    const int w_rows_total = mode == 1 ? inter : a.n_out;
+    if (!make_tmap(&tmW, a.W, w_rows_total, a.K, wrows)) return cudaErrorInvalidValue;
+    if (!make_tmap(&tmW2, mode == 1 ? a.W2 : a.W, w_rows_total, a.K, wrows))
+      return cudaErrorInvalidValue;
+  }
+  if (!make_tmap(&tmX, a.X, a.rows_cap, a.K, kXBoxRows)) return cudaErrorInvalidValue;
+
+  const size_t smem = static_cast<size_t>(pl.stage_budget) + kSmemFixed;
+  static size_t configured = 0;
+  if (configured < smem) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (pl.splits > 1) {
+    // the split CTAs of a tile group wait for one another: all must be resident at once
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, tmW, tmW2, tmX, p);
+  if (e != cudaSuccess) return e;
+  return launched();
+}
+
+// ------------------------------------------------------------------ weight tiling
+// dst[(t*kb_total + kb)*128 + r][c] = W row (t, r) at column kb*64 + c (zero past the
+// matrix).  mode 1: r < 64 -> gate row t*64 + r, r >= 64 -> up row t*64 + r - 64.
+// One thread per 16-byte destination vector (K is a multiple of 8).
+__global__ void pack_tiles_kernel(const __nv_bfloat16* W, const __nv_bfloat16* W2, int n_out,
+                                  int K, int mode, int inter, int n_tiles, int kb_total,
+                                  __nv_bfloat16* dst) {
+  const int64_t total = static_cast<int64_t>(n_tiles) * kb_total * kTileF * (kBK / 8);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = static_cast<int>(i % (kBK / 8));
+    const int64_t row = i / (kBK / 8);
+    const int r = static_cast<int>(row % kTileF);
+    const int64_t tk = row / kTileF;
+    const int kb = static_cast<int>(tk % kb_total);
+    const int t = static_cast<int>(tk / kb_total);
+    const int col = kb * kBK + v * 8;
+    const __nv_bfloat16* src = nullptr;
+    if (mode == 1) {
+      const int g = t * 64 + (r & 63);
+      if (g < inter) src = (r < 64 ? W : W2) + static_cast<int64_t>(g) * K;
+    } else {
+      const int f = t * kTileF + r;
+      if (f < n_out) src = W + static_cast<int64_t>(f) * K;
+    }
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (src != nullptr && col < K) val = *reinterpret_cast<const uint4*>(src + col);
+    *reinterpret_cast<uint4*>(dst + row * kBK + v * 8) = val;
+  }
+}
+
+size_t weight_tiles_bytes(int n_out, int K, int mode, int inter) {
+  const int n_tiles = mode == 1 ? (inter + 63) / 64 : (n_out + kTileF - 1) / kTileF;
+  const int kb_total = (K + kBK - 1) / kBK;
+  return static_cast<size_t>(n_tiles) * kb_total * kTileF * kBK * 2;
+}
+
+cudaError_t pack_weight_tiles(const void* W, const void* W2, int n_out, int K, int mode,
+                              int inter, void* dst, cudaStream_t st) {
+  if (K % 8 != 0 || (mode == 1 && W2 == nullptr)) return cudaErrorInvalidValue;
+  const int n_tiles = mode == 1 ? (inter + 63) / 64 : (n_out + kTileF - 1) / kTileF;
+  const int kb_total = (K + kBK - 1) / kBK;
+  const int64_t total = static_cast<int64_t>(n_tiles) * kb_total * kTileF * (kBK / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  pack_tiles_kernel<<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(W),
+                                            static_cast<const __nv_bfloat16*>(W2), n_out, K,
+                                            mode, inter, n_tiles, kb_total,
+                                            static_cast<__nv_bfloat16*>(dst));
+  return launched();
+}
+
+}  // namespace sf

@@ -44,6 +44,7 @@ struct CompactParams {
   const float* rstd;       // [BN]
   const void* ln_w;        // [D]
   void* xn;                // [bucket, D] or nullptr
+  int32_t* frows;          // [BN] folded rows in ascending order, or nullptr
   int B1, N, D, bucket;
   int* err;
 };
@@ -112,9 +113,22 @@ struct GemmArgs {
   void* ws;
   size_t ws_bytes;
   int* err;
+  int w_tiled;             // W (and W2) already in the tile layout of pack_weight_tiles
 };
 
+// Weight tile layout for the tensor-core GEMM: [n_tiles][k_blocks][128 rows][64] so
+// that the 16 KB a pipeline stage needs is one contiguous read.  mode 1 (SwiGLU) puts
+// rows [64 gate | 64 up] of the same 64 output features in each 128-row block.
+size_t weight_tiles_bytes(int n_out, int K, int mode, int inter);
+cudaError_t pack_weight_tiles(const void* W, const void* W2, int n_out, int K, int mode,
+                              int inter, void* dst, cudaStream_t st);
+
+// GEMM scratch: kGemmCounterBytes of split-K tile counters at offset 0 (kept zero between
+// launches; nothing else ever lands there), then partial sums / the SIMT raw result.
+constexpr size_t kGemmCounterBytes = 16384;
 size_t gemm_ws_need(int dtype, int rows_cap, int n_out, int K, int kind, int inter);
+size_t gemm_tc_ws_need(int rows_cap, int n_out, int K, int kind, int inter);
+cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st);
 cudaError_t gemm_simt_bf16(const GemmArgs& a, cudaStream_t st);
 cudaError_t gemm(const GemmArgs& a, cudaStream_t st);
 int gemm_path_is_tc(int dtype);
@@ -154,6 +168,8 @@ struct MergeParams {
   const int8_t* rec;
   const int64_t* seg;
   const int32_t* segcnt;
+  const int32_t* frows;    // folded rows listed by the compaction, or nullptr (scan all)
+  const int32_t* count;    // recomputed rows (BN - count rows are folded), with frows
   void* O;
   float* M;
   float* Z;

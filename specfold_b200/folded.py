@@ -93,10 +93,29 @@ class FoldedVerifyB200:
         m = self.model_executor.model
         return m.diffusion_head if self.family == "nld" else m.lm_head
 
+    # bf16 models: store every projection in the tile layout of the tensor-core GEMM
+    # (one contiguous 16 KB read per pipeline stage); a one-time copy of the weights
+    tile_weights = True
+
+    @staticmethod
+    def _tiles(w: torch.Tensor, w2: Optional[torch.Tensor] = None) -> torch.Tensor:
+        lib = _lib.load()
+        mode = 0 if w2 is None else 1
+        n_out, K = w.shape
+        inter = n_out if mode == 1 else 0
+        out = torch.empty(lib.sf_weight_tiles_bytes(n_out * (2 if mode else 1), K, mode, inter)
+                          // 2, dtype=w.dtype, device=w.device)
+        _lib.check(lib.sf_pack_weight_tiles(w.data_ptr(), None if w2 is None else w2.data_ptr(),
+                                            n_out, K, mode, inter, out.data_ptr(),
+                                            torch.cuda.current_stream(w.device).cuda_stream),
+                   "pack weight tiles")
+        return out
+
     def _pack_layer_weights(self, layers) -> None:
         """Per layer: [Wq; Wk; Wv] and its bias packed once (one weight stream for the
-        QKV projection, fastdllm_v2_folded.py:77-87); gate and up stay separate tensors
-        (the kernel reads both per tile), so only the QKV packing copies weights."""
+        QKV projection, fastdllm_v2_folded.py:77-87).  For bf16 models every projection is
+        also laid out in 128x64 tiles for the tensor-core GEMM, gate and up interleaved
+        per tile (the reference's [Wg; Wu] packing, done tile by tile)."""
         packed = []
         for lyr in layers:
             a, mlp = lyr.self_attn, lyr.mlp
@@ -105,13 +124,22 @@ class FoldedVerifyB200:
                 b_qkv = torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0).contiguous()
             else:
                 b_qkv = None   # NLD: no bias (nld_folded.py:92-102 packs zeros)
-            ws = (w_qkv, b_qkv, lyr.input_layernorm.weight.contiguous(),
-                  a.o_proj.weight.contiguous(), lyr.post_attention_layernorm.weight.contiguous(),
-                  mlp.gate_proj.weight.contiguous(), mlp.up_proj.weight.contiguous(),
-                  mlp.down_proj.weight.contiguous())
+            w_o = a.o_proj.weight.contiguous()
+            w_g, w_u = mlp.gate_proj.weight.contiguous(), mlp.up_proj.weight.contiguous()
+            w_d = mlp.down_proj.weight.contiguous()
+            if self._use_tiles(w_qkv):
+                w_qkv, w_o, w_g, w_u, w_d = (self._tiles(w_qkv), self._tiles(w_o),
+                                             self._tiles(w_g, w_u), None, self._tiles(w_d))
+            ws = (w_qkv, b_qkv, lyr.input_layernorm.weight.contiguous(), w_o,
+                  lyr.post_attention_layernorm.weight.contiguous(), w_g, w_u, w_d)
             packed.append(ws)
         self._packed_weights = packed
-        self._layer_structs = None
+        head_w = self._head().weight.contiguous()
+        self._lm_w = self._tiles(head_w) if self._use_tiles(head_w) else head_w
+        self._tiled = self._use_tiles(head_w)
+
+    def _use_tiles(self, w: torch.Tensor) -> bool:
+        return bool(self.tile_weights) and w.dtype == torch.bfloat16 and w.is_cuda
 
     def _shift_logits(self, logits: torch.Tensor) -> torch.Tensor:
         return torch.cat([logits[:, :1, :], logits[:, :-1, :]], dim=1)
@@ -168,10 +196,9 @@ class FoldedVerifyB200:
         sin = sin[0].to(dtype).contiguous()
         q_scale = self._q_scale(cfg, P, N, dev)
         hidden = hidden.reshape(BN, D).contiguous()
-        I = self._packed_weights[0][5].shape[0]
-        head = self._head()
-        lm_w = head.weight.contiguous()
-        V = lm_w.shape[0]
+        I = layers[0].mlp.gate_proj.weight.shape[0]
+        V = self._head().weight.shape[0]
+        lm_w = self._lm_w
 
         # per-layer structs: weights cached, prefix pointers refreshed per call
         layer_arr = (_lib.SfLayer * L)()
@@ -183,7 +210,8 @@ class FoldedVerifyB200:
             st.w_qkv, st.ln1_w, st.w_o, st.ln2_w = (w[0].data_ptr(), w[2].data_ptr(),
                                                     w[3].data_ptr(), w[4].data_ptr())
             st.b_qkv = None if w[1] is None else w[1].data_ptr()
-            st.w_gate, st.w_up, st.w_down = w[5].data_ptr(), w[6].data_ptr(), w[7].data_ptr()
+            st.w_gate, st.w_down = w[5].data_ptr(), w[7].data_ptr()
+            st.w_up = None if w[6] is None else w[6].data_ptr()
             if P > 0:
                 k, v = past_key_values[li]
                 k0, v0 = self._prefix_view(k), self._prefix_view(v)
@@ -212,6 +240,7 @@ class FoldedVerifyB200:
         args.eps = float(getattr(cfg, "rms_norm_eps", 1e-6))
         args.scale = scale
         args.shift_logits = 1 if self.family == "fastdllm" else 0
+        args.weights_tiled = 1 if self._tiled else 0
         args.layers = layer_arr
         args.final_norm_w = base.norm.weight.data_ptr()
         args.lm_w = lm_w.data_ptr()

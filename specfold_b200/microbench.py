@@ -115,18 +115,57 @@ def bench_lm_head(dims, rows, iters, g):
                    {"rows": B1 * N})
 
 
+def bench_forward(dims, args):
+    """Whole verify forward (main + 7 drafts, configuration-0 noise, fold ~0.6) with
+    ``--layers`` decoder layers of the named shape; per-kernel times from the library's
+    event profiler."""
+    import dataclasses
+    from .folded import SpecFoldB200FastDLLMV2Generation
+    from . import synthetic as syn
+    if args.layers:
+        dims = dataclasses.replace(dims, layers=args.layers)
+    B1, N = args.branches, 32
+    model = syn.build_model(dims, family="fastdllm", dtype=torch.bfloat16, seed=0, device="cuda")
+    cache = syn.random_prefix_cache(dims, args.prefix, dtype=torch.bfloat16, seed=1, device="cuda")
+    syn.inject_hidden(model, syn.config0_hidden(dims, B1, N, dtype=torch.bfloat16,
+                                                frac_recompute=1.0 - args.fold).cuda())
+    gen = SpecFoldB200FastDLLMV2Generation(model_executor=syn.StandinExecutor(model), delta=0.1)
+    gen.tile_weights = not args.untiled
+    ids = torch.zeros(B1, N, dtype=torch.int64, device="cuda")
+    for _ in range(3):
+        gen._batched_block_forward(ids, cache)
+    torch.cuda.synchronize()
+    gen._fold_draft_positions = gen._fold_draft_recomputed = 0
+    _lib.profile_begin(args.iters * (dims.layers * 9 + 4))
+    ms = _events(lambda: gen._batched_block_forward(ids, cache), args.iters, warmup=0)
+    prof = _lib.profile_end()
+    out = {"kernel": "forward", "ms": round(ms, 4), "layers": dims.layers, "prefix": args.prefix,
+           "fold_ratio": round(gen.fold_ratio, 4),
+           "per_kernel_ms": {k: round(v[0] / args.iters, 4) for k, v in prof.items() if v[1]}}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
-                    choices=["qkv", "o_proj", "ffn", "lm_head", "all_gemm"])
+                    choices=["qkv", "o_proj", "ffn", "lm_head", "all_gemm", "forward"])
     ap.add_argument("--shape", default="qwen7b", choices=sorted(SHAPES))
     ap.add_argument("--rows", type=int, default=122)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=0, help="forward: layer count override")
+    ap.add_argument("--prefix", type=int, default=1024, help="forward: prefix length")
+    ap.add_argument("--fold", type=float, default=0.6, help="forward: draft fold fraction")
+    ap.add_argument("--branches", type=int, default=8, help="forward: B1 (main + drafts)")
+    ap.add_argument("--untiled", action="store_true",
+                    help="forward: plain row-major weights instead of the tile layout")
     args = ap.parse_args()
     _lib.check(_lib.load().sf_check_device(), "device")
     dims = SHAPES[args.shape]
     g = torch.Generator().manual_seed(args.seed)
+    if args.kernel == "forward":
+        bench_forward(dims, args)
+        return
     todo = ["qkv", "o_proj", "ffn", "lm_head"] if args.kernel == "all_gemm" else [args.kernel]
     for k in todo:
         rows = 256 if k in ("o_proj", "lm_head") and args.kernel == "all_gemm" else args.rows

@@ -120,6 +120,22 @@ def test_forward_split_k_shapes(name):
     _check_against_oracle(name, ref, cap, out, gen)
 
 
+def test_tiled_weights_bit_identical():
+    """The 128x64 weight-tile layout changes only where the bytes sit: the tensor-core
+    GEMMs run the same MMAs in the same order, so logits are bit-identical."""
+    family, dims, P, kind = EXTRA["mid_bf16_tree"]
+    model = build_model(dims, family=family, dtype=torch.bfloat16, seed=0, device="cuda")
+    cache = random_prefix_cache(dims, P, dtype=torch.bfloat16, seed=1, device="cuda")
+    ids = tree_block_input(dims.vocab, N=32, edits_per_level=3).cuda()
+    outs = []
+    for tiled in (True, False):
+        gen = SpecFoldB200FastDLLMV2Generation(model_executor=StandinExecutor(model), delta=0.1)
+        gen.tile_weights = tiled
+        outs.append(gen._batched_block_forward(ids, cache))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_forward_repeatable():
     _, _, a, _ = _run_both("tiny_bf16_chain")
     _, _, b, _ = _run_both("tiny_bf16_chain")
