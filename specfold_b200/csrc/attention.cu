@@ -177,6 +177,231 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, const floa
   }
 }
 
+// attn_rows_kernel: the attention output of EVERY row r = b*N + n of the block, recomputed
+// or folded, in one pass.  A row's query is that of its recomputing ancestor
+// src_row = src[r]*N + n (a folded row inherits the hidden state, hence q, of src_row;
+// specfold_chain_correction_gqa_kernel, triton_kernels.py:393-394); its keys are the
+// prefix plus branch b's own block keys kv_buf[src[b*N+j]*N + j].  The prefix part is
+// shared by every row with the same query, so on the tensor-core path it comes from
+// src_row's split partials (its retained softmax state over the prefix) and only the N
+// block keys are visited here; otherwise the prefix keys are visited too.  This rebuilds
+// a folded row from its partner's retained state directly, where the reference walks
+// the ancestor chain and telescopes old/new key contributions (:396-428): the same
+// softmax, with no cancellation.  M is the true row max (the reference keeps the
+// running max m_new of the telescoping for folded rows); M and Z are not read by the
+// rest of the forward.
+//
+// One CTA per (branch b, kv head, group of rpc positions); warp w owns tasks
+// (position, q head) w, w+8, ... (at most kRowTasks per CTA).  Keys are staged 32 at a
+// time in shared memory and shared by all the CTA's tasks.
+constexpr int kRowTasks = 32;
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const float* part_O,
+                                                        const float* part_ml, int splits,
+                                                        int q_rows, int rpc) {
+  constexpr int DPL = HD / 32;
+  constexpr int V = Elt<T>::kVec;
+  constexpr int VPR = HD / V;
+  constexpr int TILE_VEC = (kAttnKeys * VPR + 255) / 256;
+  constexpr int TPW = kRowTasks / 8;      // tasks per warp
+  extern __shared__ __align__(16) float sm_rows[];
+  float* qs = sm_rows;                                  // [kRowTasks][HD]
+  float* ks = qs + kRowTasks * HD;                      // [32][HD + 1]
+  float* vs = ks + kAttnKeys * (HD + 1);                // [32][HD + 1]
+  int* s_slot = reinterpret_cast<int*>(vs + kAttnKeys * (HD + 1));   // [BN] (partials only)
+  __shared__ int64_t krow[kAttnKeys];
+  __shared__ int64_t s_qrow[kRowTasks];
+  __shared__ int s_warp_tot[8];
+
+  const int b = blockIdx.x, kvh = blockIdx.y;
+  const int n0 = blockIdx.z * rpc;
+  const int nrows = min(rpc, p.N - n0);
+  if (nrows <= 0) return;
+  const int G = p.H / p.Hkv;
+  const int ntasks = nrows * G;
+  const int BN = p.B1 * p.N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qd = p.H * HD, kvd = 2 * p.Hkv * HD;
+  const T* qb = reinterpret_cast<const T*>(p.q_buf);
+  const T* kvb = reinterpret_cast<const T*>(p.kv_buf);
+  const T* pk = reinterpret_cast<const T*>(p.pk);
+  const T* pv = reinterpret_cast<const T*>(p.pv);
+
+  // query rows of this CTA's positions
+  if (threadIdx.x < nrows) {
+    const int n = n0 + threadIdx.x;
+    int64_t s = p.src[static_cast<int64_t>(b) * p.N + n];
+    if (s < 0 || s >= p.B1) { flag_error(p.err, SF_DEV_ERR_INDEX); s = b; }
+    s_qrow[threadIdx.x] = s * p.N + n;
+  }
+  // slot of every row in the compaction order (exclusive scan of rec), for the partials
+  if (part_O != nullptr) {
+    constexpr int kPer = kMaxRows / 256;
+    int fl[kPer], local = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int r = threadIdx.x * kPer + i;
+      fl[i] = r < BN ? (p.rec[r] != 0) : 0;
+      local += fl[i];
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp_tot[warp] = incl;
+    __syncthreads();
+    int run = incl - local;
+    for (int i = 0; i < warp; ++i) run += s_warp_tot[i];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int r = threadIdx.x * kPer + i;
+      if (r < BN) s_slot[r] = fl[i] ? run : -1;
+      run += fl[i];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ntasks * VPR; i += 256) {
+    const int t = i / VPR, d0 = (i % VPR) * V;
+    const int g = t % G;
+    float v[V];
+    load_vec<T>(qb + s_qrow[t / G] * qd + (kvh * G + g) * HD + d0, v);
+#pragma unroll
+    for (int k = 0; k < V; ++k) qs[t * HD + d0 + k] = v[k];
+  }
+
+  float m[TPW], l[TPW], acc[TPW][DPL];
+#pragma unroll
+  for (int i = 0; i < TPW; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int t = 0; t < DPL; ++t) acc[i][t] = 0.f;
+  }
+  if (part_O != nullptr) {
+#pragma unroll
+    for (int i = 0; i < TPW; ++i) {
+      const int t = warp + 8 * i;
+      if (t >= ntasks) break;
+      const int slot = s_slot[s_qrow[t / G]];
+      if (slot < 0 || slot >= p.bucket) {   // src row not recomputed, or past the bucket
+        if (slot < 0) flag_error(p.err, SF_DEV_ERR_INDEX);
+        continue;
+      }
+      const int64_t qi = static_cast<int64_t>(slot) * G + (t % G);
+      float ms = -INFINITY, ls = 0.f;
+      if (lane < splits) {
+        const int64_t base = (static_cast<int64_t>(lane) * p.Hkv + kvh) * q_rows + qi;
+        ms = part_ml[2 * base];
+        ls = part_ml[2 * base + 1];
+      }
+      const float mx = warp_max(ms);
+      const float w = (ms == -INFINITY) ? 0.f : expf(ms - mx);
+      m[i] = mx;
+      l[i] = warp_sum(ls * w);
+      for (int s = 0; s < splits; ++s) {
+        const float ws = __shfl_sync(0xffffffffu, w, s);
+        if (ws == 0.f) continue;
+        const int64_t base = (static_cast<int64_t>(s) * p.Hkv + kvh) * q_rows + qi;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d)
+          acc[i][d] = fmaf(__ldcg(part_O + base * HD + lane + 32 * d), ws, acc[i][d]);
+      }
+    }
+  }
+  const int key_begin = part_O != nullptr ? p.P : 0;
+  const int total = p.P + p.N;
+  for (int k0 = key_begin; k0 < total; k0 += kAttnKeys) {
+    __syncthreads();
+    if (threadIdx.x < kAttnKeys) {
+      const int key = k0 + threadIdx.x;
+      int64_t kr = -1;
+      if (key >= p.P && key < total) {
+        const int j = key - p.P;
+        int64_t s = p.src[static_cast<int64_t>(b) * p.N + j];
+        if (s < 0 || s >= p.B1) { flag_error(p.err, SF_DEV_ERR_INDEX); s = b; }
+        kr = s * p.N + j;
+      }
+      krow[threadIdx.x] = kr;
+    }
+    __syncthreads();
+    float kv[TILE_VEC][V], vv[TILE_VEC][V];
+#pragma unroll
+    for (int u = 0; u < TILE_VEC; ++u) {
+      const int idx = threadIdx.x + 256 * u;
+      const int t = idx / VPR, d0 = (idx % VPR) * V;
+      const int key = k0 + t;
+      if (t < kAttnKeys && key < p.P) {
+        const int64_t o = kvh * p.kv_head_stride + static_cast<int64_t>(key) * HD + d0;
+        load_vec<T>(pk + o, kv[u]);
+        load_vec<T>(pv + o, vv[u]);
+      } else if (t < kAttnKeys && key < total) {
+        const int64_t o = krow[t] * kvd;
+        load_vec<T>(kvb + o + kvh * HD + d0, kv[u]);
+        load_vec<T>(kvb + o + (p.Hkv + kvh) * HD + d0, vv[u]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < V; ++k) kv[u][k] = vv[u][k] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < TILE_VEC; ++u) {
+      const int idx = threadIdx.x + 256 * u;
+      const int t = idx / VPR, d0 = (idx % VPR) * V;
+      if (t < kAttnKeys) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          ks[t * (HD + 1) + d0 + k] = kv[u][k];
+          vs[t * (HD + 1) + d0 + k] = vv[u][k];
+        }
+      }
+    }
+    __syncthreads();
+    const bool valid = (k0 + lane) < total;
+#pragma unroll
+    for (int i = 0; i < TPW; ++i) {
+      const int t = warp + 8 * i;
+      if (t >= ntasks) break;
+      const float* q = qs + t * HD;
+      const float* kr = ks + lane * (HD + 1);
+      float s = 0.f;
+#pragma unroll 16
+      for (int d = 0; d < HD; ++d) s = fmaf(q[d], kr[d], s);
+      s = valid ? s * p.scale : -INFINITY;
+      const float mt = warp_max(s);
+      const float mn = fmaxf(m[i], mt);
+      const float alpha = m[i] == -INFINITY ? 0.f : expf(m[i] - mn);
+      const float e = valid ? expf(s - mn) : 0.f;
+      l[i] = l[i] * alpha + warp_sum(e);
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) acc[i][d] *= alpha;
+#pragma unroll 8
+      for (int jj = 0; jj < kAttnKeys; ++jj) {
+        const float pj = __shfl_sync(0xffffffffu, e, jj);
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(pj, vs[jj * (HD + 1) + lane + 32 * d], acc[i][d]);
+      }
+      m[i] = mn;
+    }
+  }
+  T* O = reinterpret_cast<T*>(p.O);
+#pragma unroll
+  for (int i = 0; i < TPW; ++i) {
+    const int t = warp + 8 * i;
+    if (t >= ntasks) break;
+    const int64_t r = static_cast<int64_t>(b) * p.N + n0 + t / G;
+    const int h = kvh * G + t % G;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) O[r * qd + h * HD + lane + 32 * d] = Elt<T>::from_f(acc[i][d] / l[i]);
+    if (lane == 0) {
+      p.M[r * p.H + h] = m[i];
+      p.Z[r * p.H + h] = l[i];
+    }
+  }
+}
+
 template <typename T>
 __global__ void kv_append_kernel(T* ck, T* cv, int64_t cs, const T* nk, const T* nv, int64_t ns,
                                  int Hkv, int hd, int P, int n) {
@@ -220,6 +445,43 @@ cudaError_t launch_attention_simt_partials(int dtype, const AttnParams& p, const
   if (p.H % p.Hkv != 0 || p.H / p.Hkv > kMaxGroup || splits > 32) return cudaErrorInvalidValue;
   return dtype == BF16 ? attn_t<__nv_bfloat16>(p, part_O, part_ml, splits, q_rows, st)
                        : attn_t<float>(p, part_O, part_ml, splits, q_rows, st);
+}
+
+template <typename T, int HD>
+static cudaError_t rows_t(const AttnParams& p, const float* part_O, const float* part_ml,
+                          int splits, int q_rows, cudaStream_t st) {
+  const int G = p.H / p.Hkv;
+  const int rpc = std::max(1, std::min(p.N, kRowTasks / G));
+  const dim3 grid(p.B1, p.Hkv, (p.N + rpc - 1) / rpc);
+  const size_t smem = (static_cast<size_t>(kRowTasks) * HD + 2 * kAttnKeys * (HD + 1)) * 4 +
+                      static_cast<size_t>(kMaxRows) * 4;
+  static size_t configured = 0;
+  if (configured < smem) {
+    cudaError_t e = cudaFuncSetAttribute(attn_rows_kernel<T, HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  attn_rows_kernel<T, HD><<<grid, 256, smem, st>>>(p, part_O, part_ml, splits, q_rows, rpc);
+  return launched();
+}
+
+cudaError_t launch_attention_rows_partials(int dtype, const AttnParams& p, const float* part_O,
+                                           const float* part_ml, int splits, int q_rows,
+                                           cudaStream_t st) {
+  const int G = p.Hkv > 0 ? p.H / p.Hkv : 0;
+  if (G <= 0 || p.H % p.Hkv != 0 || G > kRowTasks || splits > 32 ||
+      p.B1 * p.N > kMaxRows || (part_O != nullptr && p.rec == nullptr))
+    return cudaErrorInvalidValue;
+  if (dtype == BF16) {
+    if (p.hd == 128) return rows_t<__nv_bfloat16, 128>(p, part_O, part_ml, splits, q_rows, st);
+    if (p.hd == 64) return rows_t<__nv_bfloat16, 64>(p, part_O, part_ml, splits, q_rows, st);
+  } else {
+    if (p.hd == 128) return rows_t<float, 128>(p, part_O, part_ml, splits, q_rows, st);
+    if (p.hd == 64) return rows_t<float, 64>(p, part_O, part_ml, splits, q_rows, st);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, const void* nk,

@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int kvh = blockIdx.x, split = blockIdx.y, qt = blockIdx.z;
   const int count = min(*p.count, p.bucket);
   const int Mq = count * p.G;
   const int q0 = qt * kQT;
@@ -352,8 +352,15 @@ cudaError_t launch_attention_simt_partials(int dtype, const AttnParams& p, const
                                            const float* part_ml, int splits, int q_rows,
                                            cudaStream_t st);
 
+struct PrefixPartials {
+  const float* part_O;
+  const float* part_ml;
+  int splits, q_rows;
+};
+
+// prefix part of every recomputed row's attention: per-split partials in the scratch
 template <int HD>
-static cudaError_t prefix_tc(const AttnParams& a, cudaStream_t st) {
+static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixPartials* out) {
   const int G = a.H / a.Hkv;
   const int q_rows = a.bucket * G;
   const int S = kv_splits(a.P);
@@ -402,20 +409,43 @@ static cudaError_t prefix_tc(const AttnParams& a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured = static_cast<int>(smem);
   }
-  dim3 grid((q_rows + kQT - 1) / kQT, a.Hkv, S);
+  // (kv head, split) fastest: the CTAs of the live query tiles (count * G rows, known
+  // only on the device) come first in launch order and run in the first wave
+  dim3 grid(a.Hkv, S, (q_rows + kQT - 1) / kQT);
   attn_prefix_kernel<HD><<<grid, kAttThreads, smem, st>>>(tq, tk, tv, p);
   cudaError_t e = launched();
   if (e != cudaSuccess) return e;
-  return launch_attention_simt_partials(BF16, a, p.part_O, p.part_ml, S, q_rows, st);
+  out->part_O = p.part_O;
+  out->part_ml = p.part_ml;
+  out->splits = S;
+  out->q_rows = q_rows;
+  return cudaSuccess;
+}
+
+static bool prefix_on_tc(int dtype, const AttnParams& p) {
+  return dtype == BF16 && p.P > 0 && p.pk != nullptr;
+}
+
+static cudaError_t prefix_partials_hd(const AttnParams& p, cudaStream_t st, PrefixPartials* pp) {
+  if (p.hd == 128) return prefix_partials<128>(p, st, pp);
+  if (p.hd == 64) return prefix_partials<64>(p, st, pp);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st) {
-  if (dtype == BF16 && p.P > 0 && p.pk != nullptr) {
-    if (p.hd == 128) return prefix_tc<128>(p, st);
-    if (p.hd == 64) return prefix_tc<64>(p, st);
-    return cudaErrorInvalidValue;
-  }
-  return launch_attention_simt(dtype, p, st);
+  if (!prefix_on_tc(dtype, p)) return launch_attention_simt(dtype, p, st);
+  PrefixPartials pp{};
+  cudaError_t e = prefix_partials_hd(p, st, &pp);
+  if (e != cudaSuccess) return e;
+  return launch_attention_simt_partials(BF16, p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
+}
+
+cudaError_t launch_attention_rows(int dtype, const AttnParams& p, cudaStream_t st) {
+  if (!prefix_on_tc(dtype, p)) return launch_attention_rows_partials(dtype, p, nullptr, nullptr, 0, 0, st);
+  PrefixPartials pp{};
+  cudaError_t e = prefix_partials_hd(p, st, &pp);
+  if (e != cudaSuccess) return e;
+  return launch_attention_rows_partials(BF16, p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
 }
 
 }  // namespace sf

@@ -122,7 +122,6 @@ struct FwdBufs {
   float *M, *Z, *rstd, *rstd2;
   int64_t *f, *src, *seg, *rows;
   int8_t* rec;
-  int32_t* frows;
   size_t gemm_ws_bytes, attn_ws_bytes, total;
 };
 
@@ -149,7 +148,6 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   b.seg = static_cast<int64_t*>(c.take(static_cast<size_t>(BN) * 8));
   b.rows = static_cast<int64_t*>(c.take(static_cast<size_t>(bucket) * 8));
   b.rec = static_cast<int8_t*>(c.take(static_cast<size_t>(BN)));
-  b.frows = static_cast<int32_t*>(c.take(static_cast<size_t>(BN) * 4));
   size_t g = 0;
   g = std::max(g, ws_gemm(dtype, bucket, qd + 2 * kvd, D, EPI_QKV, 0));
   g = std::max(g, ws_gemm(dtype, BN, D, qd, EPI_RESID, 0));
@@ -613,7 +611,6 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     c.rstd = b.rstd;
     c.ln_w = ly.ln1_w;
     c.xn = b.xn;
-    c.frows = b.frows;
     c.B1 = B1;
     c.N = N;
     c.D = D;
@@ -674,30 +671,10 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     at.q_comp = b.q_comp;
     at.scratch = b.attn_ws;
     at.scratch_bytes = b.attn_ws_bytes;
-    if ((s = timed(K_ATTN, st, [&] { return cuda_status(launch_attention(dtype, at, st), "attention"); })))
-      return s;
-
-    MergeParams m{};
-    m.q_buf = b.q_buf;
-    m.kv_buf = b.kv_buf;
-    m.src = b.src;
-    m.par_idx = a->par_idx;
-    m.rec = rec;
-    m.seg = b.seg;
-    m.segcnt = segcnt;
-    m.frows = b.frows;
-    m.count = count;
-    m.O = b.O;
-    m.M = b.M;
-    m.Z = b.Z;
-    m.B1 = B1;
-    m.N = N;
-    m.H = H;
-    m.Hkv = Hkv;
-    m.hd = hd;
-    m.scale = a->scale;
-    m.err = a->err;
-    if ((s = timed(K_MERGE, st, [&] { return cuda_status(launch_merge(dtype, m, st), "merge"); })))
+    at.rec = rec;
+    // every row: recomputed rows attend with their own query, folded rows are rebuilt
+    // from their recomputing ancestor's query and retained prefix state
+    if ((s = timed(K_ATTN, st, [&] { return cuda_status(launch_attention_rows(dtype, at, st), "attention"); })))
       return s;
 
     GemmArgs o{};

@@ -5,9 +5,10 @@
 // HBM-bound on the weight stream, so the kernel is built around it:
 //   * "swap-AB": 128 weight rows are the MMA's M operand, the activation rows its N
 //     operand (N = rows rounded up to 16), fp32 accumulators in TMEM;
-//   * a CTA streams `sub` (1 or 2) 128-row weight tiles per pipeline stage against one
-//     shared activation stage, so the activations (re-read from L2 by every CTA) cost
-//     half as much per weight byte when sub = 2;
+//   * a CTA streams `sub` (1, 2 or 4) 128-row weight tiles per pipeline stage against
+//     one shared activation stage, so the activations (re-read from L2 by every CTA)
+//     cost 1/sub as much per weight byte -- the L2->SM traffic, not HBM, is what limits
+//     the weight stream when every stage carries as many activation bytes as weight;
 //   * weights optionally pre-arranged in 128x64 blocks (weight_tiles_bytes), making a
 //     stage's 16 KB of each tile one contiguous read;
 //   * TMA loads (128-byte swizzle, no multicast), stage count sized in the kernel from
@@ -17,7 +18,9 @@
 //   * few tile groups (QKV, o_proj, down) split K across co-resident CTAs (cooperative
 //     launch): each publishes fp32 partials, waits (bounded) for its group's other
 //     splits, and reduces its own slice of rows in split order -- deterministic.
-// Warp 0 issues TMA, warp 1 owns TMEM and issues MMAs, warps 2-5 run the epilogue.
+// Warp 0 issues TMA, warp 1 owns TMEM and issues MMAs, warps 2-9 run the epilogue (two
+// warps per TMEM lane quarter, alternating 16-row chunks: the epilogue is latency-bound,
+// and with one warp per SM sub-partition the last unit's epilogue dominated the tail).
 //
 // Epilogues reproduce the rounding points of the PyTorch folded forward:
 //   QKV     F.linear + bias rounded to the model dtype, then q*c + rot(q)*s with every
@@ -36,18 +39,27 @@
 
 namespace sf {
 
-constexpr int kTcThreads = 192;
+constexpr int kEpiWarps = 8;                     // two warps per TMEM lane quarter
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kTcThreads = 64 + kEpiThreads;
 constexpr int kTileF = 128;                      // weight rows per tile (MMA M)
 constexpr int kBK = 64;                          // K per stage: one 128-byte swizzle row
 constexpr int kMaxPassRows = 256;                // MMA N limit
 constexpr int kWBytes = kTileF * kBK * 2;        // 16 KB per tile per stage
-constexpr int kXBoxRows = 64;
-constexpr int kXBoxBytes = kXBoxRows * kBK * 2;  // 8 KB
-constexpr int kChunk = 32;                       // rows per epilogue chunk
+constexpr int kXRowBytes = kBK * 2;              // one activation row of a stage
+constexpr int kChunk = 16;                       // rows (TMEM columns) per epilogue chunk
 constexpr int kTileLd = kTileF + 4;              // padded fp32 row of the transposed chunk
-constexpr int kTileTBytes = kChunk * kTileLd * 4;
+constexpr int kTileTBytes = 2 * kChunk * kTileLd * 4;   // one transposed chunk per half
 constexpr int kMaxStages = 8;
-constexpr int kSmemFixed = kTileTBytes + 1024 + 256;   // transposed chunk, alignment, barriers
+constexpr int kSmemFixed = kTileTBytes + 1024 + 256;   // transposed chunks, alignment, barriers
+
+// activation rows one pass loads: 128-row boxes while more than 64 remain, then one
+// 64-row box (fewer, larger TMA requests than 64-row boxes alone)
+__host__ __device__ __forceinline__ int x_rows_loaded(int prows) {
+  const int n128 = prows > 64 ? (prows - 64 + 127) / 128 : 0;
+  const int rest = prows - n128 * 128;
+  return n128 * 128 + (rest > 0 ? 64 : 0);
+}
 // split-K counters (arrivals, departures) per tile group at offset 0 of the workspace
 constexpr int kMaxCounterTiles = static_cast<int>(kGemmCounterBytes / 8);
 
@@ -57,7 +69,7 @@ struct TcParams {
   int mode;            // 0: 128-row tiles of W; 1: SWIGLU, 64 gate + 64 up rows per tile
   int inter;
   int n_tiles;         // 128-row weight tiles
-  int sub;             // tiles per unit sharing one activation stage (1 or 2)
+  int sub;             // tiles per unit sharing one activation stage (1, 2 or 4)
   int n_groups;        // ceil(n_tiles / sub)
   int splits, kb_total, kb_per_split, n_units;
   int double_buf, acc_cols;
@@ -163,10 +175,12 @@ __device__ __forceinline__ void epi_group8(const TcParams& p, int tile, int j, i
     }
     case EPI_SWIGLU: {
       if (f0 >= e.inter) return;   // up half: consumed by its gate partner
+      // silu in fp32 with the hardware exp and divide intrinsics; their few-ulp fp32
+      // error sits far below the bf16 rounding that follows
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float g = Elt<T>::rnd(v[i]), u = Elt<T>::rnd(vp[i]);
-        o[i] = __fmul_rn(Elt<T>::rnd(g / (1.0f + expf(-g))), u);
+        o[i] = __fmul_rn(Elt<T>::rnd(__fdividef(g, 1.0f + __expf(-g))), u);
       }
       st8<T>(e.out, static_cast<int64_t>(j) * e.inter + f0, o);
       return;
@@ -197,17 +211,51 @@ __device__ __forceinline__ int tc_partner_l(const TcParams& p, int l0) {
   return l0;
 }
 
-// AND over the 128 epilogue threads (named barrier 1): keeps every branch that
+// AND over the 256 epilogue threads (named barrier 1): keeps every branch that
 // guards a named barrier uniform, whatever each thread saw of the abort flag.
 __device__ __forceinline__ bool epi_vote_all(bool x) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      "bar.red.and.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
       : "r"(static_cast<uint32_t>(x))
       : "memory");
   return r != 0;
+}
+__device__ __forceinline__ void epi_sync_all() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// the four warps of one epilogue half (named barriers 2 and 3)
+__device__ __forceinline__ void epi_sync_half(int h) {
+  asm volatile("bar.sync %0, 128;" ::"r"(2 + h) : "memory");
+}
+
+// Sum over splits s of partial[s][row][f..f+7], in split order (deterministic), four
+// splits' loads in flight at a time.
+__device__ __forceinline__ void sum_splits8(const float* partial, int splits, int64_t split_stride,
+                                            int64_t off, float* acc) {
+  int s = 0;
+  for (; s + 4 <= splits; s += 4) {
+    float4 a[8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float* q = partial + (s + u) * split_stride + off;
+      a[2 * u] = __ldcg(reinterpret_cast<const float4*>(q));
+      a[2 * u + 1] = __ldcg(reinterpret_cast<const float4*>(q + 4));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc[0] += a[2 * u].x; acc[1] += a[2 * u].y; acc[2] += a[2 * u].z; acc[3] += a[2 * u].w;
+      acc[4] += a[2 * u + 1].x; acc[5] += a[2 * u + 1].y;
+      acc[6] += a[2 * u + 1].z; acc[7] += a[2 * u + 1].w;
+    }
+  }
+  for (; s < splits; ++s) {
+    const float* q = partial + s * split_stride + off;
+    const float4 a0 = __ldcg(reinterpret_cast<const float4*>(q));
+    const float4 a1 = __ldcg(reinterpret_cast<const float4*>(q + 4));
+    acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w;
+    acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
+  }
 }
 
 // First k-block of unit u's K range (nkb blocks).  CTAs start at different k-blocks so
@@ -226,7 +274,8 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmW2,
-                   const __grid_constant__ CUtensorMap tmX, TcParams p) {
+                   const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX64,
+                   TcParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -237,12 +286,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (rows <= 0) return;                         // uniform over the grid
   const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
   // stage layout from the actual row count: sub weight tiles + the activation boxes
-  const int x_boxes = (min(rows, kMaxPassRows) + kXBoxRows - 1) / kXBoxRows;
   const int w_bytes = p.sub * kWBytes;
-  const int stage_bytes = w_bytes + x_boxes * kXBoxBytes;
+  const int stage_bytes = w_bytes + x_rows_loaded(min(rows, kMaxPassRows)) * kXRowBytes;
   const int stages = min(kMaxStages, p.stage_budget / stage_bytes);
   unsigned char* stage_base = smem;
-  float* tileT = reinterpret_cast<float*>(smem + p.stage_budget);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.stage_budget + kTileTBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
@@ -261,7 +308,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -274,6 +321,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmX64);
     if (p.mode == 1 && !p.w_tiled) tma_prefetch_desc(&tmW2);
   }
   tc_fence_before();
@@ -294,8 +342,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int pass = 0; pass < n_pass && !*abort_flag; ++pass) {
           const int prow0 = pass * kMaxPassRows;
           const int prows = min(kMaxPassRows, rows - prow0);
-          const int nbox = (prows + kXBoxRows - 1) / kXBoxRows;
-          const uint32_t bytes = w_bytes + nbox * kXBoxBytes;
+          const int x_rows = x_rows_loaded(prows);
+          const uint32_t bytes = w_bytes + x_rows * kXRowBytes;
           const int nkb = kb1 - kb0, rot = kb_rotation(u, nkb);
           for (int i = 0; i < nkb; ++i, ++it) {
             const int kb = kb0 + (i + rot) % nkb;
@@ -317,9 +365,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tma_load_2d(wdst, &tmW, &full[s], kx, tile * kTileF, pol_w);
               }
             }
-            for (int b = 0; b < nbox; ++b)
-              tma_load_2d(st + w_bytes + b * kXBoxBytes, &tmX, &full[s], kx,
-                          prow0 + b * kXBoxRows, pol_x);
+            for (int r = 0; r < x_rows; r += 128) {
+              const bool wide = x_rows - r > 64;
+              tma_load_2d(st + w_bytes + r * kXRowBytes, wide ? &tmX : &tmX64, &full[s], kx,
+                          prow0 + r, pol_x);
+            }
           }
         }
       }
@@ -370,9 +420,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue
+    // Two warps per TMEM lane quarter: half h takes the even (h = 0) or odd (h = 1)
+    // chunks of kChunk activation rows, so two chunks are in flight per SM sub-partition.
     const int q = warp & 3;               // TMEM lane quarter of this warp
     const int l = q * 32 + lane;          // tile-local weight row == TMEM lane
-    const int et = threadIdx.x - 64;      // 0..127 within the epilogue warps
+    const int et = threadIdx.x - 64;      // 0..255 within the epilogue warps
+    const int h = et >> 7;                // epilogue half
+    const int eh = et & 127;              // thread within the half
+    float* tileT = reinterpret_cast<float*>(smem + p.stage_budget) + h * kChunk * kTileLd;
     int acc_it = 0;
     for (int u = blockIdx.x; u < p.n_units; u += gridDim.x) {
       const int grp = u / p.splits, split = u % p.splits;
@@ -388,12 +443,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int tile = grp * p.sub + t;
           if (tile >= p.n_tiles) break;
           const int f = tc_feature(p, tile, l);
-          for (int c0 = 0; c0 < prows; c0 += kChunk) {
+          for (int c0 = h * kChunk; c0 < prows; c0 += 2 * kChunk) {
             float v[kChunk];
             const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                 static_cast<uint32_t>(buf * buf_cols + t * p.acc_cols + c0);
             tmem_ld16(ta, v);
-            tmem_ld16(ta + 16, v + 16);
             tmem_ld_wait();
             if (p.splits > 1) {
               if (f >= 0) {
@@ -406,11 +460,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             } else {
 #pragma unroll
               for (int i = 0; i < kChunk; ++i) tileT[i * kTileLd + l] = v[i];
-              asm volatile("bar.sync 1, 128;" ::: "memory");
+              epi_sync_half(h);
               const int nr = min(kChunk, prows - c0);
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const int item = et + 128 * k;
+              for (int k = 0; k < kChunk * 16 / 128; ++k) {
+                const int item = eh + 128 * k;
                 const int r = item >> 4, l0 = (item & 15) * 8;
                 if (r < nr) {
                   const float* a = tileT + r * kTileLd + l0;
@@ -421,7 +475,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                   epi_group8(p, tile, prow0 + c0 + r, l0, va, vb);
                 }
               }
-              asm volatile("bar.sync 1, 128;" ::: "memory");
+              epi_sync_half(h);
             }
           }
         }
@@ -446,38 +500,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         go = epi_vote_all(!*abort_flag);
         const int slice = (rows + p.splits - 1) / p.splits;
         const int r0 = split * slice, r1 = min(rows, r0 + slice);
-        for (int t = 0; go && t < p.sub; ++t) {
+        const int64_t split_stride = static_cast<int64_t>(p.rows_cap) * p.n_out;
+        // items: (tile t, row r, group of 8 weight rows l0), 16 groups per row
+        const int n_items = go ? p.sub * max(0, r1 - r0) * 16 : 0;
+        for (int item = et; item < n_items; item += kEpiThreads) {
+          const int t = item / ((r1 - r0) * 16);
+          const int rem = item - t * (r1 - r0) * 16;
+          const int r = r0 + (rem >> 4), l0 = (rem & 15) * 8;
           const int tile = grp * p.sub + t;
-          if (tile >= p.n_tiles) break;
-          for (int c0 = r0; c0 < r1; c0 += kChunk) {
-            const int nr = min(kChunk, r1 - c0);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int item = et + 128 * k;
-              const int r = item >> 4, l0 = (item & 15) * 8;
-              if (r >= nr) continue;
-              const int fa = tc_feature(p, tile, l0);
-              if (fa < 0) continue;
-              const int fb = tc_feature(p, tile, tc_partner_l(p, l0));
-              float va[8] = {}, vb[8] = {};
-              for (int s = 0; s < p.splits; ++s) {
-                const float* row = p.partial + (static_cast<int64_t>(s) * p.rows_cap + c0 + r) * p.n_out;
-                const float4 a0 = __ldcg(reinterpret_cast<const float4*>(row + fa));
-                const float4 a1 = __ldcg(reinterpret_cast<const float4*>(row + fa + 4));
-                va[0] += a0.x; va[1] += a0.y; va[2] += a0.z; va[3] += a0.w;
-                va[4] += a1.x; va[5] += a1.y; va[6] += a1.z; va[7] += a1.w;
-                if (fb >= 0 && fb != fa) {
-                  const float4 b0 = __ldcg(reinterpret_cast<const float4*>(row + fb));
-                  const float4 b1 = __ldcg(reinterpret_cast<const float4*>(row + fb + 4));
-                  vb[0] += b0.x; vb[1] += b0.y; vb[2] += b0.z; vb[3] += b0.w;
-                  vb[4] += b1.x; vb[5] += b1.y; vb[6] += b1.z; vb[7] += b1.w;
-                }
-              }
-              epi_group8(p, tile, c0 + r, l0, va, fb == fa ? va : vb);
-            }
-          }
+          if (tile >= p.n_tiles) continue;
+          const int fa = tc_feature(p, tile, l0);
+          if (fa < 0) continue;
+          const int fb = tc_feature(p, tile, tc_partner_l(p, l0));
+          float va[8] = {}, vb[8] = {};
+          const int64_t row_off = static_cast<int64_t>(r) * p.n_out;
+          sum_splits8(p.partial, p.splits, split_stride, row_off + fa, va);
+          if (fb >= 0 && fb != fa) sum_splits8(p.partial, p.splits, split_stride, row_off + fb, vb);
+          epi_group8(p, tile, r, l0, va, fb == fa ? va : vb);
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        epi_sync_all();
         if (et == 0 && go) {
           const int prev = atomicAdd(&p.counters[2 * grp + 1], 1);
           if (prev == p.splits - 1) {      // everyone has passed the wait: reset
@@ -535,18 +576,22 @@ static int num_sms() {
   return n;
 }
 
-// Tuning, read once from the environment: SF_GEMM_SUB (1 or 2 weight tiles per CTA
-// stage) and SF_GEMM_SMEM_KB (shared memory per CTA; below ~113 two CTAs share an SM).
+// Tuning, read once from the environment: SF_GEMM_SUB (weight tiles per CTA stage: 0 =
+// chosen per GEMM, or 1 / 2 / 4 wherever TMEM allows) and SF_GEMM_SMEM_KB (shared memory
+// per CTA; below ~113 two CTAs share an SM).
 struct TcTuning {
-  int sub = 1;
-  int smem_kb = 222;
+  int sub = 0;
+  int smem_kb = 226;
 };
 static const TcTuning& tc_tuning() {
   static TcTuning t;
   static std::once_flag once;
   std::call_once(once, [] {
-    if (const char* v = getenv("SF_GEMM_SUB")) t.sub = std::max(1, std::min(2, atoi(v)));
-    if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(222, atoi(v)));
+    if (const char* v = getenv("SF_GEMM_SUB")) {
+      const int s = atoi(v);
+      t.sub = (s == 1 || s == 2 || s == 4) ? s : 0;
+    }
+    if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(226, atoi(v)));
   });
   return t;
 }
@@ -561,11 +606,19 @@ static TcPlan tc_plan(int n_out, int K, int mode, int inter, int rows_cap) {
   pl.kb_total = (K + kBK - 1) / kBK;
   const TcTuning& tune = tc_tuning();
   pl.acc_cols = rows_cap <= 128 ? 128 : 256;
-  pl.sub = (tune.sub == 2 && pl.n_tiles >= 2) ? 2 : 1;
+  const int sms = num_sms();
+  // Weight tiles per stage: each CTA re-reads the activations from L2 for every stage, so
+  // `sub` tiles per stage cut that traffic per weight byte by `sub`.  Chosen where the
+  // tile groups still fill the SMs without splitting K (a wider unit under split-K
+  // multiplies the fp32 partials instead); TMEM holds sub x acc_cols columns.
+  if (tune.sub > 0)
+    pl.sub = tune.sub;
+  else
+    pl.sub = pl.n_tiles >= 2 * sms ? 2 : 1;
+  while (pl.sub > 1 && (pl.sub * pl.acc_cols > 512 || pl.n_tiles < pl.sub)) pl.sub >>= 1;
   pl.stage_budget = tune.smem_kb * 1024 - kSmemFixed;
   pl.ctas_per_sm = std::max(1, (227 * 1024) / (tune.smem_kb * 1024 + 1024));
   pl.n_groups = (pl.n_tiles + pl.sub - 1) / pl.sub;
-  const int sms = num_sms();
   int splits = 1;
   // few tile groups: split K so that groups x splits fills the SMs (one pass of rows)
   if (rows_cap <= kMaxPassRows && pl.n_groups < sms / 2 && pl.n_groups <= kMaxCounterTiles)
@@ -633,7 +686,9 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
     if (!make_tmap(&tmW2, mode == 1 ? a.W2 : a.W, w_rows_total, a.K, wrows))
       return cudaErrorInvalidValue;
   }
-  if (!make_tmap(&tmX, a.X, a.rows_cap, a.K, kXBoxRows)) return cudaErrorInvalidValue;
+  CUtensorMap tmX64;
+  if (!make_tmap(&tmX, a.X, a.rows_cap, a.K, 128) || !make_tmap(&tmX64, a.X, a.rows_cap, a.K, 64))
+    return cudaErrorInvalidValue;
 
   const size_t smem = static_cast<size_t>(pl.stage_budget) + kSmemFixed;
   static size_t configured = 0;
@@ -657,7 +712,7 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, tmW, tmW2, tmX, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, tmW, tmW2, tmX, tmX64, p);
   if (e != cudaSuccess) return e;
   return launched();
 }

@@ -143,6 +143,7 @@ struct AttnParams {
   const int64_t* src;      // [BN]
   const int64_t* rows;     // [bucket]
   const int32_t* count;
+  const int8_t* rec;       // [BN] recompute flags (launch_attention_rows: slot of a row)
   void* O;                 // [BN, H*hd]
   float* M;                // [BN, H]
   float* Z;
@@ -157,8 +158,15 @@ struct AttnParams {
 };
 size_t attn_scratch_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P,
                           bool need_q_comp);
+// recomputed rows only (the flash-attention operator)
 cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attention_simt(int dtype, const AttnParams& p, cudaStream_t st);
+// every row of the block, folded rows from their recomputing ancestor's query and prefix
+// state (the fused forward's attention + chain correction in one pass)
+cudaError_t launch_attention_rows(int dtype, const AttnParams& p, cudaStream_t st);
+cudaError_t launch_attention_rows_partials(int dtype, const AttnParams& p, const float* part_O,
+                                           const float* part_ml, int splits, int q_rows,
+                                           cudaStream_t st);
 
 struct MergeParams {
   const void* q_buf;
