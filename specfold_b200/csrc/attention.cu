@@ -196,20 +196,31 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, const floa
 // time in shared memory and shared by all the CTA's tasks.
 constexpr int kRowTasks = 32;
 
+template <int DPL>
+struct VecF;
+template <> struct VecF<4> { using type = float4; };
+template <> struct VecF<2> { using type = float2; };
+
+// DPL consecutive floats <-> array
+__device__ __forceinline__ void vec_get(const float4& v, float* o) { o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w; }
+__device__ __forceinline__ void vec_get(const float2& v, float* o) { o[0] = v.x; o[1] = v.y; }
+
 template <typename T, int HD>
 __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const float* part_O,
                                                         const float* part_ml, int splits,
                                                         int q_rows, int rpc) {
-  constexpr int DPL = HD / 32;
+  constexpr int DPL = HD / 32;            // consecutive dims per lane (4 or 2)
+  using VD = typename VecF<DPL>::type;
   constexpr int V = Elt<T>::kVec;
   constexpr int VPR = HD / V;
+  constexpr int KS = HD + 4;              // padded smem row: 16-byte aligned, conflict-free
   constexpr int TILE_VEC = (kAttnKeys * VPR + 255) / 256;
   constexpr int TPW = kRowTasks / 8;      // tasks per warp
   extern __shared__ __align__(16) float sm_rows[];
   float* qs = sm_rows;                                  // [kRowTasks][HD]
-  float* ks = qs + kRowTasks * HD;                      // [32][HD + 1]
-  float* vs = ks + kAttnKeys * (HD + 1);                // [32][HD + 1]
-  int* s_slot = reinterpret_cast<int*>(vs + kAttnKeys * (HD + 1));   // [BN] (partials only)
+  float* ks = qs + kRowTasks * HD;                      // [32][KS]
+  float* vs = ks + kAttnKeys * KS;                      // [32][KS]
+  int* s_slot = reinterpret_cast<int*>(vs + kAttnKeys * KS);   // [BN] (partials only)
   __shared__ int64_t krow[kAttnKeys];
   __shared__ int64_t s_qrow[kRowTasks];
   __shared__ int s_warp_tot[8];
@@ -263,11 +274,15 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < ntasks * VPR; i += 256) {
+  for (int i = threadIdx.x; i < kRowTasks * VPR; i += 256) {
     const int t = i / VPR, d0 = (i % VPR) * V;
-    const int g = t % G;
     float v[V];
-    load_vec<T>(qb + s_qrow[t / G] * qd + (kvh * G + g) * HD + d0, v);
+    if (t < ntasks) {
+      load_vec<T>(qb + s_qrow[t / G] * qd + (kvh * G + t % G) * HD + d0, v);
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k) v[k] = 0.f;
+    }
 #pragma unroll
     for (int k = 0; k < V; ++k) qs[t * HD + d0 + k] = v[k];
   }
@@ -278,7 +293,7 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
     m[i] = -INFINITY;
     l[i] = 0.f;
 #pragma unroll
-    for (int t = 0; t < DPL; ++t) acc[i][t] = 0.f;
+    for (int d = 0; d < DPL; ++d) acc[i][d] = 0.f;
   }
   if (part_O != nullptr) {
 #pragma unroll
@@ -305,9 +320,10 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
         const float ws = __shfl_sync(0xffffffffu, w, s);
         if (ws == 0.f) continue;
         const int64_t base = (static_cast<int64_t>(s) * p.Hkv + kvh) * q_rows + qi;
+        float o[DPL];
+        vec_get(__ldcg(reinterpret_cast<const VD*>(part_O + base * HD) + lane), o);
 #pragma unroll
-        for (int d = 0; d < DPL; ++d)
-          acc[i][d] = fmaf(__ldcg(part_O + base * HD + lane + 32 * d), ws, acc[i][d]);
+        for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(o[d], ws, acc[i][d]);
       }
     }
   }
@@ -352,38 +368,59 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
       const int t = idx / VPR, d0 = (idx % VPR) * V;
       if (t < kAttnKeys) {
 #pragma unroll
-        for (int k = 0; k < V; ++k) {
-          ks[t * (HD + 1) + d0 + k] = kv[u][k];
-          vs[t * (HD + 1) + d0 + k] = vv[u][k];
+        for (int k = 0; k < V; k += 4) {
+          *reinterpret_cast<float4*>(ks + t * KS + d0 + k) =
+              make_float4(kv[u][k], kv[u][k + 1], kv[u][k + 2], kv[u][k + 3]);
+          *reinterpret_cast<float4*>(vs + t * KS + d0 + k) =
+              make_float4(vv[u][k], vv[u][k + 1], vv[u][k + 2], vv[u][k + 3]);
         }
       }
     }
     __syncthreads();
     const bool valid = (k0 + lane) < total;
+    // scores: lane = key; each K row read once for all of the warp's tasks
+    float sc[TPW];
+#pragma unroll
+    for (int i = 0; i < TPW; ++i) sc[i] = 0.f;
+    const float4* kr4 = reinterpret_cast<const float4*>(ks + lane * KS);
+#pragma unroll 4
+    for (int d4 = 0; d4 < HD / 4; ++d4) {
+      const float4 kk = kr4[d4];
+#pragma unroll
+      for (int i = 0; i < TPW; ++i) {
+        const float4 qq = reinterpret_cast<const float4*>(qs + (warp + 8 * i) * HD)[d4];
+        sc[i] = fmaf(qq.x, kk.x, sc[i]);
+        sc[i] = fmaf(qq.y, kk.y, sc[i]);
+        sc[i] = fmaf(qq.z, kk.z, sc[i]);
+        sc[i] = fmaf(qq.w, kk.w, sc[i]);
+      }
+    }
+    float e[TPW];
 #pragma unroll
     for (int i = 0; i < TPW; ++i) {
-      const int t = warp + 8 * i;
-      if (t >= ntasks) break;
-      const float* q = qs + t * HD;
-      const float* kr = ks + lane * (HD + 1);
-      float s = 0.f;
-#pragma unroll 16
-      for (int d = 0; d < HD; ++d) s = fmaf(q[d], kr[d], s);
-      s = valid ? s * p.scale : -INFINITY;
+      e[i] = 0.f;
+      if (warp + 8 * i >= ntasks) continue;
+      const float s = valid ? sc[i] * p.scale : -INFINITY;
       const float mt = warp_max(s);
       const float mn = fmaxf(m[i], mt);
       const float alpha = m[i] == -INFINITY ? 0.f : expf(m[i] - mn);
-      const float e = valid ? expf(s - mn) : 0.f;
-      l[i] = l[i] * alpha + warp_sum(e);
+      e[i] = valid ? expf(s - mn) : 0.f;
+      l[i] = l[i] * alpha + warp_sum(e[i]);
 #pragma unroll
       for (int d = 0; d < DPL; ++d) acc[i][d] *= alpha;
-#pragma unroll 8
-      for (int jj = 0; jj < kAttnKeys; ++jj) {
-        const float pj = __shfl_sync(0xffffffffu, e, jj);
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(pj, vs[jj * (HD + 1) + lane + 32 * d], acc[i][d]);
-      }
       m[i] = mn;
+    }
+    // P V: lane owns DPL consecutive dims; each V row read once for all tasks
+#pragma unroll 4
+    for (int jj = 0; jj < kAttnKeys; ++jj) {
+      float vvv[DPL];
+      vec_get(*reinterpret_cast<const VD*>(vs + jj * KS + lane * DPL), vvv);
+#pragma unroll
+      for (int i = 0; i < TPW; ++i) {
+        const float pj = __shfl_sync(0xffffffffu, e[i], jj);
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(pj, vvv[d], acc[i][d]);
+      }
     }
   }
   T* O = reinterpret_cast<T*>(p.O);
@@ -394,7 +431,8 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
     const int64_t r = static_cast<int64_t>(b) * p.N + n0 + t / G;
     const int h = kvh * G + t % G;
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) O[r * qd + h * HD + lane + 32 * d] = Elt<T>::from_f(acc[i][d] / l[i]);
+    for (int d = 0; d < DPL; ++d)
+      O[r * qd + h * HD + lane * DPL + d] = Elt<T>::from_f(acc[i][d] / l[i]);
     if (lane == 0) {
       p.M[r * p.H + h] = m[i];
       p.Z[r * p.H + h] = l[i];
@@ -453,7 +491,7 @@ static cudaError_t rows_t(const AttnParams& p, const float* part_O, const float*
   const int G = p.H / p.Hkv;
   const int rpc = std::max(1, std::min(p.N, kRowTasks / G));
   const dim3 grid(p.B1, p.Hkv, (p.N + rpc - 1) / rpc);
-  const size_t smem = (static_cast<size_t>(kRowTasks) * HD + 2 * kAttnKeys * (HD + 1)) * 4 +
+  const size_t smem = (static_cast<size_t>(kRowTasks) * HD + 2 * kAttnKeys * (HD + 4)) * 4 +
                       static_cast<size_t>(kMaxRows) * 4;
   static size_t configured = 0;
   if (configured < smem) {

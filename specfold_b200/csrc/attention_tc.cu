@@ -22,7 +22,7 @@
 
 namespace sf {
 
-constexpr int kAttThreads = 192;
+constexpr int kAttThreads = 320;   // TMA warp, MMA warp, 8 softmax warps
 constexpr int kQT = 128;            // queries per tile (MMA M)
 constexpr int kKB = 128;            // keys per block
 constexpr int kMaxKvSplits = 16;
@@ -41,6 +41,19 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// AND over the 256 softmax threads (named barrier 1): keeps the softmax warps, which meet
+// at named barriers, on the same iteration whatever each saw of a failed wait.
+__device__ __forceinline__ bool softmax_vote(bool x) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(x))
+      : "memory");
+  return r != 0;
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kAttThreads, 1)
     attn_prefix_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -50,6 +63,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   constexpr int QBYTES = KCH * kBox;
   constexpr int KVBYTES = KCH * kBox;
   constexpr int PBYTES = 2 * kBox;             // 128 queries x 128 keys bf16
+  constexpr int HALF_KEYS = kKB / 2;           // keys (S columns) per softmax half
+  constexpr int HALF_DIMS = HD / 2;            // O columns per softmax half
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -57,15 +72,16 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   unsigned char* sK = sQ + QBYTES;             // [2][KVBYTES]
   unsigned char* sV = sK + 2 * KVBYTES;        // [2][KVBYTES]
   unsigned char* sP = sV + 2 * KVBYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + PBYTES);
+  float* s_red = reinterpret_cast<float*>(sP + PBYTES);     // [2][128] half-row max / sum
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_red + 2 * kQT);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;    // [2]
   uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* pv_done = bars + 7;
-  uint64_t* drain = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* s_full = bars + 5;     // [2] (S double-buffered in TMEM)
+  uint64_t* p_full = bars + 7;
+  uint64_t* pv_done = bars + 8;
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -83,23 +99,23 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tO = tmem + 2 * kKB;          // S buffers at columns 0 and 128
 
   if (warp == 0) {
     if (lane == 0 && nb > 0) {
@@ -128,32 +144,24 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     if (lane == 0 && nb > 0) {
       const uint32_t id_s = idesc_bf16(128, kKB);          // S = Q K^T, both K-major
       const uint32_t id_pv = idesc_bf16(128, HD, 0, 1);    // O += P V, V MN-major
-      bool ok = mbar_wait(q_full, 0, p.err) && mbar_wait(&kv_full[0], 0, p.err);
-      if (ok) {
+      const uint32_t q_s = smem_u32(sQ);
+      // S(i) = Q K(i)^T into TMEM buffer i & 1
+      auto issue_s = [&](int i) -> bool {
+        if (!mbar_wait(&kv_full[i & 1], (i >> 1) & 1, p.err)) return false;
         tc_fence_after();
-        const uint32_t q_s = smem_u32(sQ), k_s = smem_u32(sK);
+        const uint32_t k_s = smem_u32(sK + (i & 1) * KVBYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          umma_f16(tS, sdesc_kmajor_sw128(q_s + (kk >> 2) * kBox + (kk & 3) * 32),
+          umma_f16(tmem + (i & 1) * kKB, sdesc_kmajor_sw128(q_s + (kk >> 2) * kBox + (kk & 3) * 32),
                    sdesc_kmajor_sw128(k_s + (kk >> 2) * kBox + (kk & 3) * 32), id_s,
                    kk > 0 ? 1u : 0u);
-        umma_commit(s_full);
-      }
+        umma_commit(&s_full[i & 1]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, p.err) && issue_s(0) && (nb < 2 || issue_s(1));
       for (int i = 0; ok && i < nb; ++i) {
         if (!mbar_wait(p_full, i & 1, p.err)) { ok = false; break; }
         tc_fence_after();
-        if (i + 1 < nb) {
-          const int s1 = (i + 1) & 1;
-          if (!mbar_wait(&kv_full[s1], ((i + 1) >> 1) & 1, p.err)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t q_s = smem_u32(sQ), k_s = smem_u32(sK + s1 * KVBYTES);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk)
-            umma_f16(tS, sdesc_kmajor_sw128(q_s + (kk >> 2) * kBox + (kk & 3) * 32),
-                     sdesc_kmajor_sw128(k_s + (kk >> 2) * kBox + (kk & 3) * 32), id_s,
-                     kk > 0 ? 1u : 0u);
-          umma_commit(s_full);
-        }
         const uint32_t p_s = smem_u32(sP), v_s = smem_u32(sV + (i & 1) * KVBYTES);
 #pragma unroll
         for (int kk = 0; kk < kKB / 16; ++kk)
@@ -162,6 +170,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
                    (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(pv_done);
         umma_commit(&kv_empty[i & 1]);
+        // the softmax of block i has read S buffer i & 1 (p_full): block i + 2 may reuse it
+        if (i + 2 < nb && !issue_s(i + 2)) { ok = false; break; }
       }
       if (!ok) *abort_flag = 1;
       umma_commit(drain);
@@ -169,75 +179,71 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax warps
+    // Two warps per TMEM lane quarter: half hh takes keys [hh*64, hh*64+64) of S and
+    // dims [hh*HD/2, ...) of O for the 32 query rows of its quarter.
     const int q = warp & 3;
+    const int hh = (warp - 2) >> 2;
     const int r = q * 32 + lane;                          // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    float m = -INFINITY, l = 0.f;
+    const float sl2 = p.scale * 1.4426950408889634f;     // scores in log2 units
+    float m = -INFINITY, l = 0.f;                         // m: full row; l: this half's keys
     bool ok = true;
     for (int i = 0; i < nb; ++i) {
-      ok = ok && !*abort_flag && mbar_wait(s_full, i & 1, p.err);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = softmax_vote(ok && !*abort_flag && mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.err));
       if (!ok) break;
       tc_fence_after();
-      const int nv = min(kKB, k_end - (k_begin + i * kKB));
+      const uint32_t tS = tmem + (i & 1) * kKB + hh * HALF_KEYS;
+      const int nv = min(kKB, k_end - (k_begin + i * kKB)) - hh * HALF_KEYS;   // valid keys here
+      float v[HALF_KEYS];
+#pragma unroll
+      for (int c = 0; c < HALF_KEYS; c += 16) tmem_ld16(tS + lane_off + c, v + c);
+      tmem_ld_wait();
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kKB / 32; ++c) {
-        float v[32];
-        tmem_ld16(tS + lane_off + c * 32, v);
-        tmem_ld16(tS + lane_off + c * 32 + 16, v + 16);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c * 32 + j < nv) mx = fmaxf(mx, v[j] * p.scale);
-      }
-      const float mn = fmaxf(m, mx);
-      const float alpha = expf(m - mn);
+      for (int j = 0; j < HALF_KEYS; ++j)
+        if (j < nv) mx = fmaxf(mx, v[j] * sl2);
+      s_red[hh * kQT + r] = mx;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float mn = fmaxf(m, fmaxf(mx, s_red[(hh ^ 1) * kQT + r]));
+      const float alpha = exp2f(m - mn);
       if (i > 0) {
-        ok = mbar_wait(pv_done, (i - 1) & 1, p.err);
-        ok = __all_sync(0xffffffffu, ok);
+        // P V of the previous block must be done: it reads sP and accumulates into O
+        ok = softmax_vote(mbar_wait(pv_done, (i - 1) & 1, p.err));
         if (!ok) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
+          for (int c = 0; c < HALF_DIMS; c += 32) {
             float o[32];
-            tmem_ld16(tO + lane_off + c * 32, o);
-            tmem_ld16(tO + lane_off + c * 32 + 16, o + 16);
+            tmem_ld16(tO + lane_off + hh * HALF_DIMS + c, o);
+            tmem_ld16(tO + lane_off + hh * HALF_DIMS + c + 16, o + 16);
             tmem_ld_wait();
             uint32_t u[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(o[j] * alpha);
-            tmem_st16(tO + lane_off + c * 32, u);
-            tmem_st16(tO + lane_off + c * 32 + 16, u + 16);
+            tmem_st16(tO + lane_off + hh * HALF_DIMS + c, u);
+            tmem_st16(tO + lane_off + hh * HALF_DIMS + c + 16, u + 16);
           }
           tmem_st_wait();
         }
       }
+      // P = exp2(s*scale*log2e - m) in bf16, written in the 128-byte-swizzled K-major
+      // layout the P V MMA reads (keys hh*64.. form the second 64-key box)
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < kKB / 32; ++c) {
-        float v[32];
-        tmem_ld16(tS + lane_off + c * 32, v);
-        tmem_ld16(tS + lane_off + c * 32 + 16, v + 16);
-        tmem_ld_wait();
+      for (int g8 = 0; g8 < HALF_KEYS / 8; ++g8) {
+        uint32_t pk[4];
 #pragma unroll
-        for (int g8 = 0; g8 < 4; ++g8) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const int j0 = g8 * 8 + 2 * h;
-            const float e0 = (c * 32 + j0 < nv) ? expf(v[j0] * p.scale - mn) : 0.f;
-            const float e1 = (c * 32 + j0 + 1 < nv) ? expf(v[j0 + 1] * p.scale - mn) : 0.f;
-            sum += e0 + e1;
-            const __nv_bfloat162 b2 = __floats2bfloat162_rn(e0, e1);
-            pk[h] = *reinterpret_cast<const uint32_t*>(&b2);
-          }
-          const int key = c * 32 + g8 * 8;             // first key of this 16-byte chunk
-          const int half = key >> 6, chunk = (key & 63) >> 3;
-          unsigned char* dst = sP + half * kBox + r * 128 + ((chunk ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        for (int h2 = 0; h2 < 4; ++h2) {
+          const int j0 = g8 * 8 + 2 * h2;
+          const float e0 = j0 < nv ? exp2f(fmaf(v[j0], sl2, -mn)) : 0.f;
+          const float e1 = j0 + 1 < nv ? exp2f(fmaf(v[j0 + 1], sl2, -mn)) : 0.f;
+          sum += e0 + e1;
+          const __nv_bfloat162 b2 = __floats2bfloat162_rn(e0, e1);
+          pk[h2] = *reinterpret_cast<const uint32_t*>(&b2);
         }
+        unsigned char* dst = sP + hh * kBox + r * 128 + ((g8 ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l = l * alpha + sum;
       m = mn;
@@ -245,22 +251,23 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && nb > 0) {
-      ok = mbar_wait(pv_done, (nb - 1) & 1, p.err);
-      ok = __all_sync(0xffffffffu, ok);
-    }
+    if (ok && nb > 0) ok = softmax_vote(mbar_wait(pv_done, (nb - 1) & 1, p.err));
+    // full-row sum: the two halves' partial sums
+    s_red[hh * kQT + r] = l;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float l_row = l + s_red[(hh ^ 1) * kQT + r];
     const int qi = q0 + r;
     const int64_t base = (static_cast<int64_t>(split) * p.Hkv + kvh) * p.q_rows + qi;
     if (ok && nb > 0) {
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HALF_DIMS; c += 32) {
         float o[32];
-        tmem_ld16(tO + lane_off + c * 32, o);
-        tmem_ld16(tO + lane_off + c * 32 + 16, o + 16);
+        tmem_ld16(tO + lane_off + hh * HALF_DIMS + c, o);
+        tmem_ld16(tO + lane_off + hh * HALF_DIMS + c + 16, o + 16);
         tmem_ld_wait();
         if (qi < Mq) {
-          float4* dst = reinterpret_cast<float4*>(p.part_O + base * HD + c * 32);
+          float4* dst = reinterpret_cast<float4*>(p.part_O + base * HD + hh * HALF_DIMS + c);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             dst[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
@@ -268,18 +275,18 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       }
     } else if (qi < Mq) {
       m = -INFINITY;
-      l = 0.f;
-      for (int d = 0; d < HD; ++d) p.part_O[base * HD + d] = 0.f;
+      for (int d = 0; d < HALF_DIMS; ++d) p.part_O[base * HD + hh * HALF_DIMS + d] = 0.f;
     }
-    if (qi < Mq) {
-      p.part_ml[2 * base] = m;
-      p.part_ml[2 * base + 1] = l;
+    if (qi < Mq && hh == 0) {
+      // m in natural-log units for the consumers
+      p.part_ml[2 * base] = (ok && nb > 0) ? m * 0.6931471805599453f : -INFINITY;
+      p.part_ml[2 * base + 1] = (ok && nb > 0) ? l_row : 0.f;
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 256);
+  if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // q_comp[kvh][slot*G + g][:] = q_buf[rows[slot]][(kvh*G + g)*hd : ...]
@@ -400,7 +407,7 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
       !att_tmap(&tv, a.pv, static_cast<uint64_t>(a.Hkv) * p.kv_rows, HD))
     return cudaErrorInvalidValue;
   constexpr int kBox = 128 * 64 * 2;
-  const size_t smem = 1024 + (HD / 64) * kBox * 5 + 2 * kBox + 256;
+  const size_t smem = 1024 + (HD / 64) * kBox * 5 + 2 * kBox + 2 * kQT * 4 + 256;
   static int configured = 0;
   if (configured < static_cast<int>(smem)) {
     cudaError_t e = cudaFuncSetAttribute(attn_prefix_kernel<HD>,

@@ -105,7 +105,10 @@ __device__ __forceinline__ void st8(void* base, int64_t i, const float* v) {
 }
 
 // Epilogue of 8 consecutive tile-local weight rows l0..l0+7 for activation row j:
-// v = their accumulators, vp = the partner rows' (RoPE pair / SwiGLU up half).
+// v = their accumulators, vp = the partner rows' (RoPE pair / SwiGLU up half).  The kind
+// is a template parameter: one kernel per epilogue keeps each kernel's code small (the
+// epilogue loop of an all-kinds kernel missed in the instruction cache).
+template <int KIND>
 __device__ __forceinline__ void epi_group8(const TcParams& p, int tile, int j, int l0,
                                            const float* v, const float* vp) {
   using T = __nv_bfloat16;
@@ -113,7 +116,7 @@ __device__ __forceinline__ void epi_group8(const TcParams& p, int tile, int j, i
   const int f0 = tc_feature(p, tile, l0);
   if (f0 < 0) return;
   float o[8];
-  switch (e.kind) {
+  switch (KIND) {
     case EPI_RAW:
       store_vec<float>(reinterpret_cast<float*>(e.out) + static_cast<int64_t>(j) * e.ld_out + f0, v);
       store_vec<float>(reinterpret_cast<float*>(e.out) + static_cast<int64_t>(j) * e.ld_out + f0 + 4, v + 4);
@@ -205,9 +208,19 @@ __device__ __forceinline__ void epi_group8(const TcParams& p, int tile, int j, i
 }
 
 // tile-local partner of weight row l0 (first of a group of 8)
+// groups of 8 tile rows per activation row that produce output (SwiGLU: the gate half;
+// its up partner rides along)
+template <int KIND>
+constexpr int kGroupsOut = KIND == EPI_SWIGLU ? 8 : 16;
+
+__device__ __forceinline__ void vec_get(const float4& v, float* o) {
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+
+template <int KIND>
 __device__ __forceinline__ int tc_partner_l(const TcParams& p, int l0) {
-  if (p.epi.kind == EPI_QKV) return l0 ^ (p.epi.hd >> 1);
-  if (p.epi.kind == EPI_SWIGLU) return l0 ^ 64;
+  if (KIND == EPI_QKV) return l0 ^ (p.epi.hd >> 1);
+  if (KIND == EPI_SWIGLU) return l0 ^ 64;
   return l0;
 }
 
@@ -272,6 +285,7 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   return v;
 }
 
+template <int KIND>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmW2,
                    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX64,
@@ -442,37 +456,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int t = 0; ready && t < p.sub; ++t) {
           const int tile = grp * p.sub + t;
           if (tile >= p.n_tiles) break;
-          const int f = tc_feature(p, tile, l);
           for (int c0 = h * kChunk; c0 < prows; c0 += 2 * kChunk) {
             float v[kChunk];
             const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                 static_cast<uint32_t>(buf * buf_cols + t * p.acc_cols + c0);
             tmem_ld16(ta, v);
             tmem_ld_wait();
-            if (p.splits > 1) {
-              if (f >= 0) {
-                float* part = p.partial +
-                              (static_cast<int64_t>(split) * p.rows_cap + prow0 + c0) * p.n_out + f;
 #pragma unroll
-                for (int i = 0; i < kChunk; ++i)
-                  if (c0 + i < prows) part[static_cast<int64_t>(i) * p.n_out] = v[i];
+            for (int i = 0; i < kChunk; ++i) tileT[i * kTileLd + l] = v[i];
+            epi_sync_half(h);
+            const int nr = min(kChunk, prows - c0);
+            if (p.splits > 1) {
+              // fp32 partial of this split, row-major, 16-byte stores
+              float* part = p.partial + (static_cast<int64_t>(split) * p.rows_cap + prow0 + c0) * p.n_out;
+#pragma unroll
+              for (int k = 0; k < kChunk * 32 / 128; ++k) {
+                const int item = eh + 128 * k;
+                const int r = item >> 5, l0 = (item & 31) * 4;
+                const int f0 = tc_feature(p, tile, l0);
+                if (r < nr && f0 >= 0)
+                  *reinterpret_cast<float4*>(part + static_cast<int64_t>(r) * p.n_out + f0) =
+                      *reinterpret_cast<const float4*>(tileT + r * kTileLd + l0);
               }
+              epi_sync_half(h);
             } else {
 #pragma unroll
-              for (int i = 0; i < kChunk; ++i) tileT[i * kTileLd + l] = v[i];
-              epi_sync_half(h);
-              const int nr = min(kChunk, prows - c0);
-#pragma unroll
-              for (int k = 0; k < kChunk * 16 / 128; ++k) {
+              for (int k = 0; k < kChunk * kGroupsOut<KIND> / 128; ++k) {
                 const int item = eh + 128 * k;
-                const int r = item >> 4, l0 = (item & 15) * 8;
+                const int r = item / kGroupsOut<KIND>, l0 = (item % kGroupsOut<KIND>) * 8;
                 if (r < nr) {
-                  const float* a = tileT + r * kTileLd + l0;
-                  const float* b = tileT + r * kTileLd + tc_partner_l(p, l0);
+                  const float4* a = reinterpret_cast<const float4*>(tileT + r * kTileLd + l0);
+                  const float4* b =
+                      reinterpret_cast<const float4*>(tileT + r * kTileLd + tc_partner_l<KIND>(p, l0));
                   float va[8], vb[8];
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) { va[i] = a[i]; vb[i] = b[i]; }
-                  epi_group8(p, tile, prow0 + c0 + r, l0, va, vb);
+                  vec_get(a[0], va); vec_get(a[1], va + 4);
+                  vec_get(b[0], vb); vec_get(b[1], vb + 4);
+                  epi_group8<KIND>(p, tile, prow0 + c0 + r, l0, va, vb);
                 }
               }
               epi_sync_half(h);
@@ -501,22 +520,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int slice = (rows + p.splits - 1) / p.splits;
         const int r0 = split * slice, r1 = min(rows, r0 + slice);
         const int64_t split_stride = static_cast<int64_t>(p.rows_cap) * p.n_out;
-        // items: (tile t, row r, group of 8 weight rows l0), 16 groups per row
-        const int n_items = go ? p.sub * max(0, r1 - r0) * 16 : 0;
+        // items: (tile t, row r, group of 8 weight rows l0 that emits output)
+        constexpr int GPR = kGroupsOut<KIND>;
+        const int n_items = go ? p.sub * max(0, r1 - r0) * GPR : 0;
         for (int item = et; item < n_items; item += kEpiThreads) {
-          const int t = item / ((r1 - r0) * 16);
-          const int rem = item - t * (r1 - r0) * 16;
-          const int r = r0 + (rem >> 4), l0 = (rem & 15) * 8;
+          const int t = item / ((r1 - r0) * GPR);
+          const int rem = item - t * (r1 - r0) * GPR;
+          const int r = r0 + rem / GPR, l0 = (rem % GPR) * 8;
           const int tile = grp * p.sub + t;
           if (tile >= p.n_tiles) continue;
           const int fa = tc_feature(p, tile, l0);
           if (fa < 0) continue;
-          const int fb = tc_feature(p, tile, tc_partner_l(p, l0));
+          const int fb = tc_feature(p, tile, tc_partner_l<KIND>(p, l0));
           float va[8] = {}, vb[8] = {};
           const int64_t row_off = static_cast<int64_t>(r) * p.n_out;
           sum_splits8(p.partial, p.splits, split_stride, row_off + fa, va);
           if (fb >= 0 && fb != fa) sum_splits8(p.partial, p.splits, split_stride, row_off + fb, vb);
-          epi_group8(p, tile, r, l0, va, fb == fa ? va : vb);
+          epi_group8<KIND>(p, tile, r, l0, va, fb == fa ? va : vb);
         }
         epi_sync_all();
         if (et == 0 && go) {
@@ -611,10 +631,18 @@ static TcPlan tc_plan(int n_out, int K, int mode, int inter, int rows_cap) {
   // `sub` tiles per stage cut that traffic per weight byte by `sub`.  Chosen where the
   // tile groups still fill the SMs without splitting K (a wider unit under split-K
   // multiplies the fp32 partials instead); TMEM holds sub x acc_cols columns.
-  if (tune.sub > 0)
+  if (tune.sub > 0) {
     pl.sub = tune.sub;
-  else
-    pl.sub = pl.n_tiles >= 2 * sms ? 2 : 1;
+  } else if (pl.n_tiles >= 2 * sms) {
+    pl.sub = 2;
+  } else {
+    // split-K regime: two tiles per stage when each split still streams >= 16 k-blocks
+    // (the doubled partials are a fixed cost per CTA; the halved activation re-reads pay
+    // over a long K range, e.g. the down projection)
+    const int g2 = (pl.n_tiles + 1) / 2;
+    const int s2 = std::max(1, std::min(sms / g2, pl.kb_total / 4));
+    pl.sub = (pl.n_tiles >= 2 && pl.kb_total / s2 >= 16) ? 2 : 1;
+  }
   while (pl.sub > 1 && (pl.sub * pl.acc_cols > 512 || pl.n_tiles < pl.sub)) pl.sub >>= 1;
   pl.stage_budget = tune.smem_kb * 1024 - kSmemFixed;
   pl.ctas_per_sm = std::max(1, (227 * 1024) / (tune.smem_kb * 1024 + 1024));
@@ -691,13 +719,23 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
     return cudaErrorInvalidValue;
 
   const size_t smem = static_cast<size_t>(pl.stage_budget) + kSmemFixed;
-  static size_t configured = 0;
-  if (configured < smem) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, TcParams);
+  KernelFn kern = nullptr;
+  switch (a.epi.kind) {
+    case EPI_RAW: kern = tc_gemm_kernel<EPI_RAW>; break;
+    case EPI_QKV: kern = tc_gemm_kernel<EPI_QKV>; break;
+    case EPI_RESID: kern = tc_gemm_kernel<EPI_RESID>; break;
+    case EPI_SWIGLU: kern = tc_gemm_kernel<EPI_SWIGLU>; break;
+    case EPI_SCATTER: kern = tc_gemm_kernel<EPI_SCATTER>; break;
+    case EPI_LOGITS: kern = tc_gemm_kernel<EPI_LOGITS>; break;
+    default: return cudaErrorInvalidValue;
+  }
+  static size_t configured[EPI_LOGITS + 1] = {};
+  if (configured[a.epi.kind] < smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured = smem;
+    configured[a.epi.kind] = smem;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
@@ -712,7 +750,7 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel, tmW, tmW2, tmX, tmX64, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmW, tmW2, tmX, tmX64, p);
   if (e != cudaSuccess) return e;
   return launched();
 }
