@@ -122,6 +122,8 @@ struct FwdBufs {
   float *M, *Z, *rstd, *rstd2;
   int64_t *f, *src, *seg, *rows;
   int8_t* rec;
+  float* gate_red;        // gate partial sums [BN][S][4]
+  unsigned* sync;         // grid barrier counter (zeroed per forward)
   size_t gemm_ws_bytes, attn_ws_bytes, total;
 };
 
@@ -148,6 +150,9 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   b.seg = static_cast<int64_t*>(c.take(static_cast<size_t>(BN) * 8));
   b.rows = static_cast<int64_t*>(c.take(static_cast<size_t>(bucket) * 8));
   b.rec = static_cast<int8_t*>(c.take(static_cast<size_t>(BN)));
+  b.gate_red = static_cast<float*>(
+      c.take(static_cast<size_t>(BN) * gate_compact_slices(N, D) * 4 * sizeof(float)));
+  b.sync = static_cast<unsigned*>(c.take(256));
   size_t g = 0;
   g = std::max(g, ws_gemm(dtype, bucket, qd + 2 * kvd, D, EPI_QKV, 0));
   g = std::max(g, ws_gemm(dtype, BN, D, qd, EPI_RESID, 0));
@@ -569,6 +574,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   }
   s = cuda_status(cudaMemsetAsync(a->count_slab, 0, sizeof(int32_t) * L, st), "memset");
   if (s) return s;
+  s = cuda_status(cudaMemsetAsync(b.sync, 0, 256, st), "memset");
+  if (s) return s;
 
   for (int li = 0; li < L; ++li) {
     const sf_layer& ly = a->layers[li];
@@ -581,42 +588,33 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     int32_t* count = a->count_slab + li;
     int32_t* segcnt = a->segcnt_slab + static_cast<int64_t>(li) * B1;
 
-    GateRowsParams g{};
+    // previous layer's combine + delta gate + compaction + normalised QKV input
+    GateCompactParams g{};
     g.hp = li == 0 ? nullptr : b.hp;
     g.ffn = b.ffn;
-    g.src = b.src;
+    g.src_prev = b.src;
     g.hidden = const_cast<void*>(Hf);
     g.par_idx = a->par_idx;
-    g.rstd = b.rstd;
+    g.ln_w = ly.ln1_w;
     g.rec = rec;
     g.f = b.f;
+    g.rows = b.rows;
+    g.count = count;
+    g.seg = b.seg;
+    g.segcnt = segcnt;
+    g.src = b.src;
+    g.xn = b.xn;
+    g.red = b.gate_red;
+    g.bar = b.sync;
+    g.bar_target = static_cast<unsigned>(li + 1) * static_cast<unsigned>(N * gate_compact_slices(N, D));
     g.delta = a->delta;
     g.eps = a->eps;
     g.B1 = B1;
     g.N = N;
     g.D = D;
+    g.bucket = bucket;
     g.err = a->err;
-    if ((s = timed(K_GATE, st, [&] { return cuda_status(launch_gate_rows(dtype, g, st), "gate"); })))
-      return s;
-
-    CompactParams c{};
-    c.rec = rec;
-    c.f = b.f;
-    c.rows = b.rows;
-    c.count = count;
-    c.seg = b.seg;
-    c.segcnt = segcnt;
-    c.src = b.src;
-    c.hidden = Hf;
-    c.rstd = b.rstd;
-    c.ln_w = ly.ln1_w;
-    c.xn = b.xn;
-    c.B1 = B1;
-    c.N = N;
-    c.D = D;
-    c.bucket = bucket;
-    c.err = a->err;
-    if ((s = timed(K_COMPACT, st, [&] { return cuda_status(launch_compact(dtype, c, st), "compact"); })))
+    if ((s = timed(K_GATE, st, [&] { return cuda_status(launch_gate_compact(dtype, g, st), "gate"); })))
       return s;
 
     GemmArgs q{};

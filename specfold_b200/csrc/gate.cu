@@ -315,6 +315,62 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(RmsRowsParams p) {
                     reinterpret_cast<T*>(p.out) + static_cast<int64_t>(w) * p.D, p.D, lane, rs);
 }
 
+// Same output, one CTA per row: every element of the row is loaded once into registers
+// (one memory round trip), the sum of squares is a block reduction, and the row is
+// normalised from the registers (D <= 256 * kVec * MAXV).
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) rmsnorm_cta_kernel(RmsRowsParams p) {
+  constexpr int V = Elt<T>::kVec;
+  __shared__ float s_part[8];
+  const int i = blockIdx.x;
+  int n = p.n;
+  if (p.count) n = min(n, *p.count);
+  if (i >= n) return;
+  const int64_t row = p.rows ? p.rows[i] : i;
+  if (row < 0 || row >= p.n_src) {
+    if (threadIdx.x == 0) flag_error(p.err, SF_DEV_ERR_INDEX);
+    return;
+  }
+  const T* x = reinterpret_cast<const T*>(p.x) + row * p.D;
+  const T* w = reinterpret_cast<const T*>(p.w);
+  float a[MAXV][V], g[MAXV][V];
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < MAXV; ++u) {
+    const int d = (threadIdx.x + 256 * u) * V;
+    if (d < p.D) {
+      load_vec<T>(x + d, a[u]);
+      load_vec<T>(w + d, g[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < MAXV; ++u) {
+    const int d = (threadIdx.x + 256 * u) * V;
+    if (d < p.D) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) ss = fmaf(a[u][k], a[u][k], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) tot += s_part[k];
+  const float rs = 1.0f / sqrtf(tot / static_cast<float>(p.D) + p.eps);
+  if (p.rstd && threadIdx.x == 0) p.rstd[i] = rs;
+  T* out = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(i) * p.D;
+#pragma unroll
+  for (int u = 0; u < MAXV; ++u) {
+    const int d = (threadIdx.x + 256 * u) * V;
+    if (d < p.D) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) a[u][k] = g[u][k] * Elt<T>::rnd(a[u][k] * rs);
+      store_vec<T>(out + d, a[u]);
+    }
+  }
+}
+
 // hidden[r] = T(hp[r] + ffn[src[r]*N + n]); one warp per row.
 template <typename T>
 __global__ void __launch_bounds__(256) combine_kernel(const T* hp, const T* ffn,
@@ -353,7 +409,286 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* hp, const T* ffn,
   }
 }
 
+// ------------------------------------------------------------------------ fused gate
+// gate_compact_kernel: the previous layer's combine, the delta gate, the compaction and
+// the normalised QKV input of one layer in a single cooperative launch.
+//   phase 1  CTA (n, s) owns position n and D-slice s of every branch row r = b*N + n:
+//            hidden = T(hp + ffn[src*N+n]) (or the input rows at layer 0) into shared
+//            memory, and its slice of sum(x^2), sum(T(x - x_par)^2), sum(x_par^2);
+//   barrier  every CTA's partial sums are published (bounded spin on a counter);
+//   phase 2  every CTA adds the S slices of every row in slice order (deterministic) and
+//            takes the gate decisions (residual_delta_gate_kernel, triton_kernels.py:
+//            199-241), the slot scan and, in CTA 0, rows / count / src / segments;
+//   phase 3  each CTA writes xn[slot] = T(w * T(x * rstd)) for its own slice of the
+//            recomputed rows straight from shared memory (triton_kernels.py:30-87 input).
+// The slices keep ~N*S CTAs busy on the loads where one CTA per position left most SMs
+// idle, and the two launches of gate + compaction become one.
+template <typename T>
+__global__ void __launch_bounds__(256) gate_compact_kernel(GateCompactParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* rows_s = reinterpret_cast<T*>(smem_raw);   // [B1][slice]
+  __shared__ int s_slot[kMaxRows];
+  __shared__ int8_t s_rec[kMaxRows];
+  __shared__ int8_t s_f[kMaxRows];
+  __shared__ float s_rstd[kMaxBranches];
+  __shared__ int s_warp[8];
+  constexpr int V = Elt<T>::kVec;
+  constexpr int CV = 4;                          // vectors per lane in flight
+  const int n = blockIdx.x / p.S, sl = blockIdx.x % p.S;
+  const int d0 = sl * p.slice;
+  const int len = min(p.D, d0 + p.slice) - d0;   // a multiple of V
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B1 = p.B1, N = p.N, D = p.D, BN = B1 * N;
+  T* hidden = reinterpret_cast<T*>(p.hidden);
+
+  // ---- phase 1: rows of position n, slice [d0, d0 + len)
+  for (int b = warp; b < B1; b += 8) {
+    const int64_t r = static_cast<int64_t>(b) * N + n;
+    T* mine = rows_s + static_cast<size_t>(b) * p.slice;
+    float ss = 0.f;
+    const T* hpr = nullptr;
+    const T* ffr = nullptr;
+    if (p.hp != nullptr) {
+      int64_t s = p.src_prev[r];
+      if (s < 0 || s >= B1) { flag_error(p.err, SF_DEV_ERR_INDEX); s = b; }
+      hpr = reinterpret_cast<const T*>(p.hp) + r * D + d0;
+      ffr = reinterpret_cast<const T*>(p.ffn) + (s * N + n) * D + d0;
+    }
+    for (int base = 0; base < len; base += 32 * V * CV) {
+      float a[CV][V], c[CV][V];
+#pragma unroll
+      for (int i = 0; i < CV; ++i) {
+        const int d = base + (lane + 32 * i) * V;
+        if (d < len) {
+          if (hpr != nullptr) {
+            load_vec<T>(hpr + d, a[i]);
+            load_vec<T>(ffr + d, c[i]);
+          } else {
+            load_vec<T>(hidden + r * D + d0 + d, a[i]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < CV; ++i) {
+        const int d = base + (lane + 32 * i) * V;
+        if (d < len) {
+          if (hpr != nullptr) {
+#pragma unroll
+            for (int k = 0; k < V; ++k) a[i][k] = Elt<T>::rnd(a[i][k] + c[i][k]);
+            store_vec<T>(hidden + r * D + d0 + d, a[i]);
+          }
+#pragma unroll
+          for (int k = 0; k < V; ++k) ss = fmaf(a[i][k], a[i][k], ss);
+          store_vec<T>(mine + d, a[i]);
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) p.red[(r * p.S + sl) * 4] = ss;
+  }
+  __syncthreads();
+  for (int b = warp; b < B1; b += 8) {
+    const int64_t r = static_cast<int64_t>(b) * N + n;
+    float dd = 0.f, pp = 0.f;
+    if (b > 0) {
+      int64_t par = p.par_idx[b];
+      if (par < 0 || par >= B1 || par == b) { flag_error(p.err, SF_DEV_ERR_INDEX); par = 0; }
+      const T* mine = rows_s + static_cast<size_t>(b) * p.slice;
+      const T* pr = rows_s + static_cast<size_t>(par) * p.slice;
+      for (int d = lane * V; d < len; d += 32 * V) {
+        float a[V], c[V];
+        load_vec<T>(mine + d, a);
+        load_vec<T>(pr + d, c);
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          const float diff = Elt<T>::rnd(a[k] - c[k]);   // x - x_par in the model dtype
+          dd = fmaf(diff, diff, dd);
+          pp = fmaf(c[k], c[k], pp);
+        }
+      }
+      dd = warp_sum(dd);
+      pp = warp_sum(pp);
+    }
+    if (lane == 0) {
+      p.red[(r * p.S + sl) * 4 + 1] = dd;
+      p.red[(r * p.S + sl) * 4 + 2] = pp;
+    }
+  }
+
+  // ---- grid barrier: every CTA's partial sums are visible
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    atomicAdd(p.bar, 1u);
+    const uint64_t t0 = globaltimer();
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.bar) : "memory");
+      if (static_cast<int>(v - p.bar_target) >= 0) break;
+      if (globaltimer() - t0 > kWaitNs) { flag_error(p.err, SF_DEV_ERR_TIMEOUT); break; }
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 2: decisions of every row (slice sums in slice order), then the scan
+  for (int r = tid; r < BN; r += 256) {
+    const int b = r / N;
+    float ss = 0.f, dd = 0.f, pp = 0.f;
+    for (int s = 0; s < p.S; ++s) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(p.red + (static_cast<int64_t>(r) * p.S + s) * 4));
+      ss += v.x;
+      dd += v.y;
+      pp += v.z;
+    }
+    int recompute = 1;
+    int fv = b;
+    if (b > 0) {
+      // norms returned in the model dtype, threshold delta * ||x_par|| rounded likewise
+      const float dn = Elt<T>::rnd(sqrtf(dd));
+      const float pn = Elt<T>::rnd(sqrtf(pp));
+      const float thr = Elt<T>::rnd(pn * p.delta);
+      recompute = dn > thr ? 1 : 0;
+      if (!recompute) {
+        int64_t par = p.par_idx[b];
+        if (par < 0 || par >= B1) par = 0;
+        fv = static_cast<int>(par);
+      }
+    }
+    s_rec[r] = static_cast<int8_t>(recompute);
+    s_f[r] = static_cast<int8_t>(fv);
+    if (r % N == n) s_rstd[b] = 1.0f / sqrtf(ss / static_cast<float>(D) + p.eps);
+  }
+  __syncthreads();
+  constexpr int kPer = kMaxRows / 256;
+  int flags[kPer];
+  int local = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int r = tid * kPer + i;
+    flags[i] = r < BN ? s_rec[r] : 0;
+    local += flags[i];
+  }
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int run = incl - local, total = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i < warp) run += s_warp[i];
+    total += s_warp[i];
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int r = tid * kPer + i;
+    if (r < kMaxRows) s_slot[r] = flags[i] ? run : -1;
+    run += flags[i];
+  }
+  __syncthreads();
+
+  if (blockIdx.x == 0) {
+    if (tid == 0) *p.count = total;
+    for (int r = tid; r < BN; r += 256) {
+      p.rec[r] = s_rec[r];
+      p.f[r] = s_f[r];
+      const int s = s_slot[r];
+      if (s >= 0 && s < p.bucket) p.rows[s] = r;
+      // src: follow f (branch indices) to the recomputing ancestor
+      const int nn = r % N;
+      int c = s_f[r];
+      int hops = 0;
+      while (hops <= B1) {
+        const int nx = s_f[c * N + nn];
+        if (nx == c) break;
+        c = nx;
+        ++hops;
+      }
+      if (hops > B1) flag_error(p.err, SF_DEV_ERR_DEPTH);
+      p.src[r] = c;
+    }
+    for (int b = tid; b < B1; b += 256) {
+      int k = 0;
+      for (int nn = 0; nn < N; ++nn) {
+        const int r = b * N + nn;
+        if (s_slot[r] >= 0) p.seg[static_cast<int64_t>(b) * N + (k++)] = r;
+      }
+      p.segcnt[b] = k;
+    }
+  }
+
+  // ---- phase 3: normalised QKV input of this CTA's recomputed rows
+  const T* lw = reinterpret_cast<const T*>(p.ln_w) + d0;
+  for (int b = warp; b < B1; b += 8) {
+    const int r = b * N + n;
+    const int s = s_slot[r];
+    if (s < 0 || s >= p.bucket) continue;
+    const T* mine = rows_s + static_cast<size_t>(b) * p.slice;
+    T* out = reinterpret_cast<T*>(p.xn) + static_cast<int64_t>(s) * D + d0;
+    const float rs = s_rstd[b];
+    for (int d = lane * V; d < len; d += 32 * V) {
+      float a[V], g[V];
+      load_vec<T>(mine + d, a);
+      load_vec<T>(lw + d, g);
+#pragma unroll
+      for (int k = 0; k < V; ++k) a[k] = g[k] * Elt<T>::rnd(a[k] * rs);
+      store_vec<T>(out + d, a);
+    }
+  }
+}
+
+// D-slices per position: about one CTA per SM in all, at least 64 elements per slice;
+// the slice is a multiple of 8 elements (16-byte vectors)
+static int gate_slice(int N, int D) {
+  int S = std::max(1, 148 / std::max(1, N));
+  S = std::min(S, std::max(1, D / 64));
+  return ((D + S - 1) / S + 7) / 8 * 8;
+}
+int gate_compact_slices(int N, int D) {
+  const int slice = gate_slice(N, D);
+  return (D + slice - 1) / slice;
+}
+
 // ------------------------------------------------------------------------ launchers
+template <typename T>
+static cudaError_t launch_gate_compact_t(GateCompactParams p, cudaStream_t st) {
+  p.slice = gate_slice(p.N, p.D);
+  p.S = gate_compact_slices(p.N, p.D);
+  const size_t smem = static_cast<size_t>(p.B1) * p.slice * sizeof(T);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gate_compact_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  if (smem > 160 * 1024) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.N * p.S);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  // the CTAs meet at a grid barrier: all must be resident at once
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gate_compact_kernel<T>, p);
+  if (e != cudaSuccess) return e;
+  return launched();
+}
+
+cudaError_t launch_gate_compact(int dtype, const GateCompactParams& p, cudaStream_t st) {
+  if (p.B1 > kMaxBranches || p.B1 * p.N > kMaxRows || p.D % 8 != 0) return cudaErrorInvalidValue;
+  return dtype == BF16 ? launch_gate_compact_t<__nv_bfloat16>(p, st)
+                       : launch_gate_compact_t<float>(p, st);
+}
+
+
 template <typename T>
 static cudaError_t launch_gate_rows_t(const GateRowsParams& p, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(p.B1) * p.D * sizeof(T);
@@ -386,8 +721,14 @@ cudaError_t launch_src_resolve(const int64_t* f, int64_t* src, int B1, int N, in
 }
 
 cudaError_t launch_rmsnorm_rows(int dtype, const RmsRowsParams& p, cudaStream_t st) {
+  if (p.n <= 0) return cudaSuccess;
+  const int vec = dtype == BF16 ? 8 : 4;
+  if (p.D % vec == 0 && p.D <= 256 * vec * 4) {
+    if (dtype == BF16) rmsnorm_cta_kernel<__nv_bfloat16, 4><<<p.n, 256, 0, st>>>(p);
+    else rmsnorm_cta_kernel<float, 4><<<p.n, 256, 0, st>>>(p);
+    return launched();
+  }
   const int grid = (p.n + 7) / 8;
-  if (grid == 0) return cudaSuccess;
   if (dtype == BF16) rmsnorm_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
   else rmsnorm_rows_kernel<float><<<grid, 256, 0, st>>>(p);
   return launched();

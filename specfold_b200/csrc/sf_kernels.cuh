@@ -63,6 +63,32 @@ struct RmsRowsParams {
   int* err;
 };
 
+struct GateCompactParams {
+  const void* hp;          // previous layer's o_proj output (nullptr at layer 0)
+  const void* ffn;         // [BN+1, D] previous layer's FFN rows
+  const int64_t* src_prev; // previous layer's src (read before the grid barrier)
+  void* hidden;            // [BN, D] read (layer 0) or written by the combine
+  const int64_t* par_idx;  // [B1]
+  const void* ln_w;        // [D] input RMSNorm weight
+  int8_t* rec;             // [BN]
+  int64_t* f;              // [BN]
+  int64_t* rows;           // [bucket]
+  int32_t* count;          // [1]
+  int64_t* seg;            // [BN]
+  int32_t* segcnt;         // [B1]
+  int64_t* src;            // [BN] (written after the barrier; may alias src_prev)
+  void* xn;                // [bucket, D]
+  float* red;              // [BN][S][4] partial sums
+  unsigned* bar;           // grid barrier counter (zero at the start of the forward)
+  unsigned bar_target;     // counter value to wait for (cumulative over layers)
+  float delta, eps;
+  int B1, N, D, bucket;
+  int S, slice;            // set by the launcher
+  int* err;
+};
+int gate_compact_slices(int N, int D);
+cudaError_t launch_gate_compact(int dtype, const GateCompactParams& p, cudaStream_t st);
+
 cudaError_t launch_gate_rows(int dtype, const GateRowsParams& p, cudaStream_t st);
 cudaError_t launch_compact(int dtype, const CompactParams& p, cudaStream_t st);
 cudaError_t launch_src_resolve(const int64_t* f, int64_t* src, int B1, int N, int* err,
