@@ -214,13 +214,21 @@ typedef struct sf_verify_args {
   const float* q_scale;        /* [N] or NULL */
   void* logits;                /* [B1, N, V] */
   int32_t* count_slab;         /* [L] recomputed rows per layer (zeroed by the call) */
-  int32_t* segcnt_slab;        /* [L*B1] recomputed rows per layer and branch */
+  int32_t* segcnt_slab;        /* [L*B1] recomputed rows per layer and branch (zeroed by
+                                  the call) */
   int8_t* rec_slab;            /* [L*B1*N] fold masks per layer, or NULL */
   void* ws;                    /* sf_verify_workspace_bytes(...) bytes */
   size_t ws_bytes;
-  int* err;                    /* device error word (SF_DEV_*), accumulated */
+  int* err;                    /* device error word (SF_DEV_*), zeroed by the call */
   void* stream;
 } sf_verify_args;
+
+/* The parent map of a verify block on the device: par_idx[i] = the first branch whose
+ * set of positions differing from the main branch (row 0 of ids) is a subset of
+ * branch i's with one element fewer, else 0 (SpecFold*Generation._build_parent_map,
+ * fastdllm_v2_folded.py:55-75; the reference computes it on the host after a sync).
+ * ids [B1, N] int64 on the device. */
+int sf_parent_map(const int64_t* ids, int B1, int N, int64_t* par_idx, void* stream);
 
 /* ------------------------------------------------------------------ measurement ----
  * Kernels launched by this library so far (all host threads).                       */
@@ -247,6 +255,11 @@ int sf_pack_weight_tiles(const void* W, const void* W2, int n_out, int K, int mo
 
 size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
                                  int V, int P);
+/* Runs the forward on args->stream.  The launches of one argument set (every field but
+ * `stream`, and the contents of the layer table) are captured into a CUDA graph on the
+ * second call with that set and replayed afterwards: keep buffers at fixed addresses
+ * across steps to benefit; the data behind the pointers may change freely.  SF_GRAPH=0
+ * in the environment launches directly every time. */
 int sf_folded_verify_forward(const sf_verify_args* args);
 
 #ifdef __cplusplus

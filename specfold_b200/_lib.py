@@ -85,6 +85,7 @@ _SIGS = {
     "sf_kv_append": (c_int, [c_int, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
                              c_int, c_int, c_int, c_int, c_void_p]),
     "sf_weight_tiles_bytes": (c_size_t, [c_int] * 4),
+    "sf_parent_map": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "sf_pack_weight_tiles": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                      c_void_p]),
     "sf_launch_count": (C.c_longlong, []),

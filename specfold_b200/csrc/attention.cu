@@ -225,6 +225,8 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
   __shared__ int64_t s_qrow[kRowTasks];
   __shared__ int s_warp_tot[8];
 
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int n0 = blockIdx.z * rpc;
   const int nrows = min(rpc, p.N - n0);
@@ -501,7 +503,9 @@ static cudaError_t rows_t(const AttnParams& p, const float* part_O, const float*
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  attn_rows_kernel<T, HD><<<grid, 256, smem, st>>>(p, part_O, part_ml, splits, q_rows, rpc);
+  const cudaError_t e = launch_ex(attn_rows_kernel<T, HD>, grid, dim3(256), smem, st, false, p,
+                                 part_O, part_ml, splits, q_rows, rpc);
+  if (e != cudaSuccess) return e;
   return launched();
 }
 

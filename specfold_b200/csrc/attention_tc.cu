@@ -85,6 +85,13 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  pdl_trigger();
+  pdl_wait();
   const int kvh = blockIdx.x, split = blockIdx.y, qt = blockIdx.z;
   const int count = min(*p.count, p.bucket);
   const int Mq = count * p.G;
@@ -419,8 +426,9 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
   // (kv head, split) fastest: the CTAs of the live query tiles (count * G rows, known
   // only on the device) come first in launch order and run in the first wave
   dim3 grid(a.Hkv, S, (q_rows + kQT - 1) / kQT);
-  attn_prefix_kernel<HD><<<grid, kAttThreads, smem, st>>>(tq, tk, tv, p);
-  cudaError_t e = launched();
+  cudaError_t e = launch_ex(attn_prefix_kernel<HD>, grid, dim3(kAttThreads), smem, st, false, tq,
+                            tk, tv, p);
+  if (e == cudaSuccess) e = launched();
   if (e != cudaSuccess) return e;
   out->part_O = p.part_O;
   out->part_ml = p.part_ml;

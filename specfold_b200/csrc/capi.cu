@@ -3,6 +3,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <atomic>
+#include <mutex>
+#include <unordered_set>
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -14,6 +17,15 @@ using namespace sf;
 namespace sf {
 static std::atomic<long long> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+// Programmatic dependent launch is off unless SF_PDL=1: measured on the verify forward
+// (captured as a CUDA graph) it did not shorten the step.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SF_PDL");
+    return v != nullptr && atoi(v) != 0;
+  }();
+  return on;
+}
 }  // namespace sf
 
 namespace {
@@ -542,6 +554,16 @@ size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv
   return carve_forward(nullptr, dtype, B1, N, D, H, Hkv, hd, I, V, B1 * N, P).total + 256;
 }
 
+static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStream_t st);
+static int forward_graph(const sf_verify_args* a, const FwdBufs& b);
+static bool graphs_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SF_GRAPH");
+    return v == nullptr || atoi(v) != 0;
+  }();
+  return on;
+}
+
 int sf_folded_verify_forward(const sf_verify_args* a) {
   if (!a) return fail(SF_ERR_ARG, "null args");
   const int dtype = a->dtype;
@@ -564,7 +586,25 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket, a->P);
   if (b.total > a->ws_bytes)
     return fail(SF_ERR_WORKSPACE, "workspace %zu < %zu bytes", a->ws_bytes, b.total);
-  cudaStream_t st = S(a->stream);
+  for (int li = 0; li < L; ++li) {
+    const sf_layer& ly = a->layers[li];
+    if (!ly.w_qkv || !ly.ln1_w || !ly.w_o || !ly.ln2_w || !ly.w_gate ||
+        (!ly.w_up && !a->weights_tiled) || !ly.w_down ||
+        (a->P > 0 && (!ly.prefix_k || !ly.prefix_v)))
+      return fail(SF_ERR_ARG, "layer %d: null weight", li);
+  }
+  if (g_prof.on || !graphs_enabled()) return forward_launches(a, b, S(a->stream));
+  return forward_graph(a, b);
+}
+
+// The launches of one verify forward on stream st (validated arguments).
+static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStream_t st) {
+  const int dtype = a->dtype;
+  const int B1 = a->B1, N = a->N, D = a->D, H = a->H, Hkv = a->Hkv, hd = a->hd, I = a->I,
+            V = a->V, L = a->L;
+  const int BN = B1 * N;
+  const int bucket = a->bucket;
+  int s = 0;
   const int qd = H * hd, kvd = Hkv * hd;
   // split-K tile counters (first 16 KB of the GEMM scratch) start at zero
   if (b.gemm_ws_bytes > 0) {
@@ -576,13 +616,15 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   if (s) return s;
   s = cuda_status(cudaMemsetAsync(b.sync, 0, 256, st), "memset");
   if (s) return s;
+  s = cuda_status(cudaMemsetAsync(a->segcnt_slab, 0, sizeof(int32_t) * L * B1, st), "memset");
+  if (s) return s;
+  if (a->err) {
+    s = cuda_status(cudaMemsetAsync(a->err, 0, sizeof(int32_t), st), "memset");
+    if (s) return s;
+  }
 
   for (int li = 0; li < L; ++li) {
     const sf_layer& ly = a->layers[li];
-    if (!ly.w_qkv || !ly.ln1_w || !ly.w_o || !ly.ln2_w || !ly.w_gate ||
-        (!ly.w_up && !a->weights_tiled) || !ly.w_down ||
-        (a->P > 0 && (!ly.prefix_k || !ly.prefix_v)))
-      return fail(SF_ERR_ARG, "layer %d: null weight", li);
     const void* Hf = li == 0 ? a->hidden_in : b.hbuf;
     int8_t* rec = a->rec_slab ? a->rec_slab + static_cast<int64_t>(li) * BN : b.rec;
     int32_t* count = a->count_slab + li;
@@ -643,7 +685,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     q.ws = b.gemm_ws;
     q.ws_bytes = b.gemm_ws_bytes;
     q.err = a->err;
-    if ((s = timed(K_QKV, st, [&] { return run_gemm(q, a->stream, "qkv"); }))) return s;
+    if ((s = timed(K_QKV, st, [&] { return run_gemm(q, st, "qkv"); }))) return s;
 
     AttnParams at{};
     at.q_buf = b.q_buf;
@@ -690,7 +732,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     o.ws = b.gemm_ws;
     o.ws_bytes = b.gemm_ws_bytes;
     o.err = a->err;
-    if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, a->stream, "o_proj"); }))) return s;
+    if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, st, "o_proj"); }))) return s;
 
     RmsRowsParams r{};
     r.x = b.hp;
@@ -723,7 +765,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     gu.ws = b.gemm_ws;
     gu.ws_bytes = b.gemm_ws_bytes;
     gu.err = a->err;
-    if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, a->stream, "gate/up"); }))) return s;
+    if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, st, "gate/up"); }))) return s;
 
     GemmArgs dn{};
     dn.dtype = dtype;
@@ -741,7 +783,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     dn.ws = b.gemm_ws;
     dn.ws_bytes = b.gemm_ws_bytes;
     dn.err = a->err;
-    if ((s = timed(K_DOWN, st, [&] { return run_gemm(dn, a->stream, "down"); }))) return s;
+    if ((s = timed(K_DOWN, st, [&] { return run_gemm(dn, st, "down"); }))) return s;
   }
   // last layer's combine, final norm, lm_head
   if ((s = timed(K_COMBINE, st, [&] {
@@ -776,7 +818,120 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   lm.ws = b.gemm_ws;
   lm.ws_bytes = b.gemm_ws_bytes;
   lm.err = a->err;
-  return timed(K_LM_HEAD, st, [&] { return run_gemm(lm, a->stream, "lm_head"); });
+  return timed(K_LM_HEAD, st, [&] { return run_gemm(lm, st, "lm_head"); });
+}
+
+// ------------------------------------------------------------------ CUDA graphs
+// A verify step is ~230 kernel launches whose host cost (tensor-map encoding, launch
+// calls) exceeds the GPU time of the small kernels.  The launches of one argument set
+// are captured once, on a private stream, into a CUDA graph; a call with byte-identical
+// arguments (same pointers, shapes, scalars, layer table) replays it with one launch on
+// the caller's stream.  Data behind the pointers may change freely between calls.
+namespace {
+
+struct GraphEntry {
+  int device;
+  std::string key;
+  cudaGraphExec_t exec;
+  long long launches;   // kernels in the graph (the library's launch counter advances by it)
+  unsigned long long last_use;
+};
+std::mutex g_graph_mu;
+std::vector<GraphEntry> g_graphs;
+std::unordered_set<std::string> g_seen;
+unsigned long long g_graph_clock = 0;
+constexpr size_t kMaxGraphs = 16;
+
+std::string graph_key(const sf_verify_args* a) {
+  sf_verify_args c = *a;
+  c.stream = nullptr;
+  c.layers = nullptr;
+  std::string k(reinterpret_cast<const char*>(&c), sizeof(c));
+  k.append(reinterpret_cast<const char*>(a->layers), sizeof(sf_layer) * a->L);
+  return k;
+}
+
+cudaStream_t capture_stream(int device) {
+  static std::mutex mu;
+  static std::vector<cudaStream_t> streams;
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(streams.size()) <= device) streams.resize(device + 1, nullptr);
+  if (!streams[device]) cudaStreamCreateWithFlags(&streams[device], cudaStreamNonBlocking);
+  return streams[device];
+}
+
+}  // namespace
+
+static int forward_graph(const sf_verify_args* a, const FwdBufs& b) {
+  int dev = 0;
+  int s = cuda_status(cudaGetDevice(&dev), "get device");
+  if (s) return s;
+  const std::string key = graph_key(a);
+  cudaStream_t st = S(a->stream);
+  {
+    std::lock_guard<std::mutex> lock(g_graph_mu);
+    for (auto& e : g_graphs) {
+      if (e.device == dev && e.key == key) {
+        e.last_use = ++g_graph_clock;
+        s = cuda_status(cudaGraphLaunch(e.exec, st), "graph launch");
+        if (!s) count_launch(static_cast<int>(e.launches));
+        return s;
+      }
+    }
+  }
+  {
+    // the first call of an argument set runs directly (it also performs the one-time
+    // per-kernel setup); the second is captured
+    std::lock_guard<std::mutex> lock(g_graph_mu);
+    const std::string skey = std::to_string(dev) + ":" + key;
+    if (g_seen.insert(skey).second) {
+      if (g_seen.size() > 4 * kMaxGraphs) g_seen.clear();
+      return forward_launches(a, b, st);
+    }
+  }
+  cudaStream_t cs = capture_stream(dev);
+  if (!cs) return fail(SF_ERR_CUDA, "could not create the capture stream");
+  const long long before = g_launches.load();
+  s = cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
+  if (s) return s;
+  const int rs = forward_launches(a, b, cs);
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+  if (rs) {
+    if (g) cudaGraphDestroy(g);
+    return rs;
+  }
+  if (ce != cudaSuccess || !g) {
+    if (g) cudaGraphDestroy(g);
+    return cuda_status(ce != cudaSuccess ? ce : cudaErrorUnknown, "end capture");
+  }
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return cuda_status(ie, "graph instantiate");
+  const long long n = g_launches.load() - before;
+  g_launches.fetch_sub(n);            // counted when the graph runs, not when captured
+  {
+    std::lock_guard<std::mutex> lock(g_graph_mu);
+    if (g_graphs.size() >= kMaxGraphs) {
+      auto lru = g_graphs.begin();
+      for (auto it = g_graphs.begin(); it != g_graphs.end(); ++it)
+        if (it->last_use < lru->last_use) lru = it;
+      cudaGraphExecDestroy(lru->exec);
+      g_graphs.erase(lru);
+    }
+    g_graphs.push_back({dev, key, exec, n, ++g_graph_clock});
+  }
+  s = cuda_status(cudaGraphLaunch(exec, st), "graph launch");
+  if (!s) count_launch(static_cast<int>(n));
+  return s;
+}
+
+int sf_parent_map(const int64_t* ids, int B1, int N, int64_t* par_idx, void* stream) {
+  if (!ids || !par_idx) return fail(SF_ERR_ARG, "null pointer");
+  if (B1 < 1 || B1 > kMaxBranches || N < 1 || B1 * N > kMaxRows)
+    return fail(SF_ERR_ARG, "parent map shape B1=%d N=%d unsupported", B1, N);
+  return cuda_status(launch_parent_map(ids, B1, N, par_idx, S(stream)), "parent map");
 }
 
 size_t sf_weight_tiles_bytes(int n_out, int K, int mode, int inter) {

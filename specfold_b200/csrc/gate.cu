@@ -322,6 +322,8 @@ template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) rmsnorm_cta_kernel(RmsRowsParams p) {
   constexpr int V = Elt<T>::kVec;
   __shared__ float s_part[8];
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   int n = p.n;
   if (p.count) n = min(n, *p.count);
@@ -378,6 +380,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* hp, const T* ffn,
                                                      int N, int D, int* err) {
   constexpr int V = Elt<T>::kVec;
   constexpr int STEP = 32 * V * kChunkVec;
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= B1 * N) return;
@@ -409,6 +413,52 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* hp, const T* ffn,
   }
 }
 
+// ------------------------------------------------------------------------ parent map
+// par_idx[i] for the B1 branches of a verify block (fastdllm_v2_folded.py:55-75): the
+// first branch j whose set of positions differing from the main branch (row 0) is a
+// subset of branch i's with exactly one element fewer; 0 (the main branch) otherwise.
+// One CTA; runs on the device so the forward needs no host round trip before launch.
+__global__ void __launch_bounds__(256) parent_map_kernel(const int64_t* ids, int B1, int N,
+                                                         int64_t* par_idx) {
+  __shared__ uint8_t diff[kMaxRows];
+  __shared__ int cnt[kMaxBranches];
+  __shared__ uint8_t esc[kMaxBranches * kMaxBranches];   // esc[i][j]: j differs where i does not
+  const int BN = B1 * N;
+  for (int r = threadIdx.x; r < BN; r += blockDim.x) diff[r] = ids[r] != ids[r % N] ? 1 : 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < B1; i += blockDim.x) {
+    int c = 0;
+    for (int n = 0; n < N; ++n) c += diff[i * N + n];
+    cnt[i] = c;
+  }
+  for (int q = threadIdx.x; q < B1 * B1; q += blockDim.x) {
+    const int i = q / B1, j = q % B1;
+    uint8_t e = 0;
+    for (int n = 0; n < N && !e; ++n) e = diff[j * N + n] && !diff[i * N + n];
+    esc[q] = e;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < B1; i += blockDim.x) {
+    int par = 0;
+    if (i > 0) {
+      for (int j = 0; j < B1; ++j) {
+        if (j != i && cnt[j] == cnt[i] - 1 && !esc[i * B1 + j]) {
+          par = j;
+          break;
+        }
+      }
+    }
+    par_idx[i] = par;
+  }
+}
+
+cudaError_t launch_parent_map(const int64_t* ids, int B1, int N, int64_t* par_idx,
+                              cudaStream_t st) {
+  if (B1 < 1 || B1 > kMaxBranches || N < 1 || B1 * N > kMaxRows) return cudaErrorInvalidValue;
+  parent_map_kernel<<<1, 256, 0, st>>>(ids, B1, N, par_idx);
+  return launched();
+}
+
 // ------------------------------------------------------------------------ fused gate
 // gate_compact_kernel: the previous layer's combine, the delta gate, the compaction and
 // the normalised QKV input of one layer in a single cooperative launch.
@@ -434,6 +484,8 @@ __global__ void __launch_bounds__(256) gate_compact_kernel(GateCompactParams p) 
   __shared__ int s_warp[8];
   constexpr int V = Elt<T>::kVec;
   constexpr int CV = 4;                          // vectors per lane in flight
+  pdl_trigger();
+  pdl_wait();
   const int n = blockIdx.x / p.S, sl = blockIdx.x % p.S;
   const int d0 = sl * p.slice;
   const int len = min(p.D, d0 + p.slice) - d0;   // a multiple of V
@@ -666,18 +718,8 @@ static cudaError_t launch_gate_compact_t(GateCompactParams p, cudaStream_t st) {
     configured = true;
   }
   if (smem > 160 * 1024) return cudaErrorInvalidValue;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.N * p.S);
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
   // the CTAs meet at a grid barrier: all must be resident at once
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gate_compact_kernel<T>, p);
+  cudaError_t e = launch_ex(gate_compact_kernel<T>, dim3(p.N * p.S), dim3(256), smem, st, true, p);
   if (e != cudaSuccess) return e;
   return launched();
 }
@@ -724,8 +766,10 @@ cudaError_t launch_rmsnorm_rows(int dtype, const RmsRowsParams& p, cudaStream_t 
   if (p.n <= 0) return cudaSuccess;
   const int vec = dtype == BF16 ? 8 : 4;
   if (p.D % vec == 0 && p.D <= 256 * vec * 4) {
-    if (dtype == BF16) rmsnorm_cta_kernel<__nv_bfloat16, 4><<<p.n, 256, 0, st>>>(p);
-    else rmsnorm_cta_kernel<float, 4><<<p.n, 256, 0, st>>>(p);
+    const cudaError_t e =
+        dtype == BF16 ? launch_ex(rmsnorm_cta_kernel<__nv_bfloat16, 4>, dim3(p.n), dim3(256), 0, st, false, p)
+                      : launch_ex(rmsnorm_cta_kernel<float, 4>, dim3(p.n), dim3(256), 0, st, false, p);
+    if (e != cudaSuccess) return e;
     return launched();
   }
   const int grid = (p.n + 7) / 8;
@@ -737,14 +781,16 @@ cudaError_t launch_rmsnorm_rows(int dtype, const RmsRowsParams& p, cudaStream_t 
 cudaError_t launch_combine(int dtype, const void* hp, const void* ffn, const int64_t* src,
                            void* hidden, int B1, int N, int D, int* err, cudaStream_t st) {
   const int grid = (B1 * N + 7) / 8;
+  cudaError_t e;
   if (dtype == BF16)
-    combine_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(hp), static_cast<const __nv_bfloat16*>(ffn), src,
-        static_cast<__nv_bfloat16*>(hidden), B1, N, D, err);
+    e = launch_ex(combine_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, false,
+                  static_cast<const __nv_bfloat16*>(hp), static_cast<const __nv_bfloat16*>(ffn), src,
+                  static_cast<__nv_bfloat16*>(hidden), B1, N, D, err);
   else
-    combine_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(hp),
-                                                static_cast<const float*>(ffn), src,
-                                                static_cast<float*>(hidden), B1, N, D, err);
+    e = launch_ex(combine_kernel<float>, dim3(grid), dim3(256), 0, st, false,
+                  static_cast<const float*>(hp), static_cast<const float*>(ffn), src,
+                  static_cast<float*>(hidden), B1, N, D, err);
+  if (e != cudaSuccess) return e;
   return launched();
 }
 

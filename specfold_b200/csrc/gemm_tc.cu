@@ -75,6 +75,8 @@ struct TcParams {
   int double_buf, acc_cols;
   int w_tiled;         // weights in the [tile][kb][128][64] layout
   int stage_budget;    // shared-memory bytes for the pipeline stages
+  const void* w_pf;    // tiled weights to prefetch into L2 before the dependency wait
+  int pf_kb;           // k-blocks per tile of the first unit to prefetch
   float* partial;      // [splits][rows_cap][n_out] when splits > 1
   int* counters;       // [2 * n_groups]
   EpiParams epi;
@@ -295,6 +297,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmX64);
+    if (p.mode == 1 && !p.w_tiled) tma_prefetch_desc(&tmW2);
+    // The weights are constant: while the previous kernel still runs, pull the first
+    // unit's first k-blocks into L2 in the order the producer will read them.
+    if (p.w_pf != nullptr && blockIdx.x < p.n_units) {
+      const int u = blockIdx.x, grp = u / p.splits, split = u % p.splits;
+      const int kb0 = split * p.kb_per_split;
+      const int nkb = min(p.kb_total, kb0 + p.kb_per_split) - kb0;
+      const int rot = kb_rotation(u, nkb);
+      const int npf = min(nkb, p.pf_kb);
+      for (int t = 0; t < p.sub; ++t) {
+        const int tile = grp * p.sub + t;
+        if (tile >= p.n_tiles) break;
+        for (int i = 0; i < npf; ++i) {
+          const int kb = kb0 + (i + rot) % nkb;
+          prefetch_l2_bulk(static_cast<const char*>(p.w_pf) +
+                               (static_cast<int64_t>(tile) * p.kb_total + kb) * kWBytes,
+                           kWBytes);
+        }
+      }
+    }
+  }
+  pdl_trigger();
+  pdl_wait();
   int rows = p.rows_cap;
   if (p.count) rows = min(rows, *p.count);
   if (rows <= 0) return;                         // uniform over the grid
@@ -331,12 +360,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmW);
-    tma_prefetch_desc(&tmX);
-    tma_prefetch_desc(&tmX64);
-    if (p.mode == 1 && !p.w_tiled) tma_prefetch_desc(&tmW2);
   }
   tc_fence_before();
   __syncthreads();
@@ -601,7 +624,9 @@ static int num_sms() {
 // per CTA; below ~113 two CTAs share an SM).
 struct TcTuning {
   int sub = 0;
-  int smem_kb = 226;
+  int smem_kb = 170;
+  int pf_mb = 0;       // SF_GEMM_PF_MB: L2 prefetch of the first units' weights, whole grid
+                       // (off: it competed with the running kernel for HBM)
 };
 static const TcTuning& tc_tuning() {
   static TcTuning t;
@@ -612,6 +637,7 @@ static const TcTuning& tc_tuning() {
       t.sub = (s == 1 || s == 2 || s == 4) ? s : 0;
     }
     if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(226, atoi(v)));
+    if (const char* v = getenv("SF_GEMM_PF_MB")) t.pf_mb = std::max(0, std::min(96, atoi(v)));
   });
   return t;
 }
@@ -693,6 +719,15 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
   p.acc_cols = pl.acc_cols;
   p.w_tiled = a.w_tiled ? 1 : 0;
   p.stage_budget = pl.stage_budget;
+  // L2 prefetch of each CTA's first k-blocks, capped so the prefetched lines (every CTA's
+  // share together) stay well inside L2 until the producer reads them
+  {
+    const int64_t per_kb = static_cast<int64_t>(std::min(pl.grid, p.n_units)) * pl.sub * kWBytes;
+    const int64_t cap = static_cast<int64_t>(tc_tuning().pf_mb) << 20;
+    const int pf = static_cast<int>(std::min<int64_t>(pl.kb_per_split, per_kb > 0 ? cap / per_kb : 0));
+    p.w_pf = (a.w_tiled && pf > 0) ? a.W : nullptr;
+    p.pf_kb = pf;
+  }
   if (pl.splits > 1) {
     const size_t need = kGemmCounterBytes + static_cast<size_t>(pl.splits) * a.rows_cap * a.n_out * 4;
     if (a.ws == nullptr || a.ws_bytes < need) return cudaErrorInvalidValue;
@@ -737,20 +772,9 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured[a.epi.kind] = smem;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.grid);
-  cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  if (pl.splits > 1) {
-    // the split CTAs of a tile group wait for one another: all must be resident at once
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmW, tmW2, tmX, tmX64, p);
+  // split K: the split CTAs of a tile group wait for one another, all must be resident
+  cudaError_t e = launch_ex(kern, dim3(pl.grid), dim3(kTcThreads), smem, st, pl.splits > 1, tmW,
+                            tmW2, tmX, tmX64, p);
   if (e != cudaSuccess) return e;
   return launched();
 }

@@ -164,6 +164,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
+// bytes (a multiple of 16, 16-byte aligned address) from global memory into L2
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Programmatic dependent launch.  Every kernel of the forward is launched with
+// programmatic stream serialization: it may start while the previous kernel still
+// runs.  pdl_trigger() lets the next kernel launch; pdl_wait() returns once the
+// previous kernel has completed and its memory is visible (and, transitively, every
+// earlier one).  Before pdl_wait() a kernel reads only data that no kernel of the
+// forward writes (weights, the prefix cache, RoPE tables) and writes nothing global.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t* bar, int c0,
                                             int c1, uint64_t policy) {
   asm volatile(

@@ -1,6 +1,8 @@
 // Internal launcher interface shared by the .cu files of the library.
 #pragma once
 
+#include <utility>
+
 #include "sf_common.cuh"
 
 namespace sf {
@@ -8,6 +10,43 @@ namespace sf {
 constexpr int kMaxBranches = 32;         // B1 limit (one warp per branch in the gate)
 constexpr int kMaxRows = 1024;           // B1*N limit of the compaction scan
 constexpr int kMaxGateSmem = 227 * 1024;
+
+// Launch with programmatic stream serialization (the kernel may begin while the previous
+// one finishes; it calls pdl_wait() before touching what that kernel produces), plus the
+// cooperative attribute when the kernel's CTAs wait on one another.  If the driver
+// refuses the combination, the launch is repeated without the programmatic attribute.
+// The programmatic attribute is set only with SF_PDL=1 in the environment (read once).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, bool cooperative, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  ++na;
+  if (cooperative) {
+    attr[na].id = cudaLaunchAttributeCooperative;
+    attr[na].val.cooperative = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e == cudaErrorInvalidValue || e == cudaErrorNotSupported) {
+    (void)cudaGetLastError();
+    cfg.attrs = attr + 1;
+    cfg.numAttrs = na - 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  }
+  return e;
+}
 
 // number of kernels this library has launched (all threads, all devices)
 void count_launch(int n = 1);
@@ -87,6 +126,8 @@ struct GateCompactParams {
   int* err;
 };
 int gate_compact_slices(int N, int D);
+cudaError_t launch_parent_map(const int64_t* ids, int B1, int N, int64_t* par_idx,
+                              cudaStream_t st);
 cudaError_t launch_gate_compact(int dtype, const GateCompactParams& p, cudaStream_t st);
 
 cudaError_t launch_gate_rows(int dtype, const GateRowsParams& p, cudaStream_t st);

@@ -173,65 +173,111 @@ class FoldedVerifyB200:
         dev = batched_input.device
         if dev.type != "cuda":
             raise ValueError("the B200 folded forward runs on CUDA tensors only")
-        layers = base.layers
-        L = len(layers)
-        H, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
-        hd = layers[0].self_attn.head_dim
-        scale = float(layers[0].self_attn.scaling)
         B1, N = batched_input.shape
         BN = B1 * N
         if self._packed_weights is None:
-            self._pack_layer_weights(layers)
+            self._pack_layer_weights(base.layers)
         P = int(past_key_values.get_seq_length()) if past_key_values is not None else 0
-
-        parent, counts = self._build_parent_map(batched_input)
-        par_idx = torch.tensor([0] + [parent[i] for i in range(1, B1)], dtype=torch.int64,
-                               device=dev)
+        stream = torch.cuda.current_stream(dev)
         hidden = base.embed_tokens(batched_input)
-        dtype = hidden.dtype
-        D = hidden.shape[-1]
-        pos = torch.arange(P, P + N, device=dev).unsqueeze(0)
-        cos, sin = base.rotary_emb(hidden, pos)
-        cos = cos[0].to(dtype).contiguous()
-        sin = sin[0].to(dtype).contiguous()
-        q_scale = self._q_scale(cfg, P, N, dev)
-        hidden = hidden.reshape(BN, D).contiguous()
-        I = layers[0].mlp.gate_proj.weight.shape[0]
-        V = self._head().weight.shape[0]
-        lm_w = self._lm_w
+        st = self._static_state(batched_input, past_key_values, hidden.dtype, P, bucket)
+        L = st["L"]
 
-        # per-layer structs: weights cached, prefix pointers refreshed per call
-        layer_arr = (_lib.SfLayer * L)()
-        kv_stride = 0
-        keep = []
-        for li in range(L):
-            w = self._packed_weights[li]
-            st = layer_arr[li]
-            st.w_qkv, st.ln1_w, st.w_o, st.ln2_w = (w[0].data_ptr(), w[2].data_ptr(),
-                                                    w[3].data_ptr(), w[4].data_ptr())
-            st.b_qkv = None if w[1] is None else w[1].data_ptr()
-            st.w_gate, st.w_down = w[5].data_ptr(), w[7].data_ptr()
-            st.w_up = None if w[6] is None else w[6].data_ptr()
-            if P > 0:
+        # per call: parent map on the device (the reference's :263-265 host round trip),
+        # embeddings into the fixed input buffer, then the forward (a CUDA graph replay
+        # once the argument set has been seen)
+        ids = batched_input if batched_input.dtype == torch.int64 else batched_input.to(torch.int64)
+        ids = ids.contiguous()
+        _lib.check(lib.sf_parent_map(ids.data_ptr(), B1, N, st["par"].data_ptr(),
+                                     stream.cuda_stream), "parent map")
+        st["hidden"].copy_(hidden.reshape(BN, -1))
+        st["args"].stream = stream.cuda_stream
+        _lib.check(lib.sf_folded_verify_forward(st["args"]), "folded verify forward")
+        logits = st["logits"].clone()
+        rec = st["rec"].clone() if st["rec"] is not None else None
+
+        # one sync for the fold counters and the device error word (the reference's :363)
+        host = st["host_slab"]
+        host.copy_(st["slab"], non_blocking=True)
+        stream.synchronize()
+        counts = host[:L].tolist()
+        bits = int(host[-1])
+        if bits:
+            raise _lib.SpecFoldError("folded verify forward: " + _lib.describe_device_error(bits))
+        mx, sm = max(counts), sum(counts)
+        if count_stats:
+            self._fold_draft_positions = getattr(self, "_fold_draft_positions", 0) + (B1 - 1) * N * L
+            self._fold_draft_recomputed = getattr(self, "_fold_draft_recomputed", 0) + int(sm) - L * N
+        if rec is not None:
+            self.last_rec_masks = rec.view(L, B1, N)
+        return logits, {"max_count": int(mx), "sum_count": int(sm)}
+
+    def _static_state(self, batched_input, past_key_values, dtype, P, bucket) -> dict:
+        """Buffers and the C argument struct of one configuration (shape, prefix cache
+        tensors, bucket), kept at fixed addresses across calls so that the library
+        replays its CUDA graph of the forward.  RoPE tables and the query scale depend
+        only on the prefix length and are filled once here."""
+        lib = _lib.load()
+        base = self._base()
+        cfg = self.model_executor.model.config
+        dev = batched_input.device
+        layers = base.layers
+        L = len(layers)
+        B1, N = batched_input.shape
+        BN = B1 * N
+        H, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        hd = layers[0].self_attn.head_dim
+        kv, keep, kv_stride = [], [], 0
+        if P > 0:
+            for li in range(L):
                 k, v = past_key_values[li]
                 k0, v0 = self._prefix_view(k), self._prefix_view(v)
-                keep += [k0, v0]
                 if kv_stride == 0:
                     kv_stride = k0.stride(0)
                 if k0.stride(0) != kv_stride or v0.stride(0) != kv_stride:
-                    k0, v0 = k0.contiguous(), v0.contiguous()
                     raise ValueError("prefix cache layers must share one head stride")
-                st.prefix_k, st.prefix_v = k0.data_ptr(), v0.data_ptr()
+                keep += [k0, v0]
+                kv.append((k0.data_ptr(), v0.data_ptr()))
+        key = (dev.index, dtype, B1, N, P, bucket, bool(self.record_masks), kv_stride, tuple(kv))
+        statics = self.__dict__.setdefault("_statics", {})
+        st = statics.get(key)
+        if st is not None:
+            return st
 
-        need = lib.sf_verify_workspace_bytes(dtype_code(hidden), B1, N, D, H, Hkv, hd, I, V, P)
-        ws = self._workspace((dev.index, dtype), need, dev)
-        logits = torch.empty(B1, N, V, dtype=dtype, device=dev)
-        slab = torch.zeros(L + L * B1 + 1, dtype=torch.int32, device=dev)
-        count_slab, segcnt_slab, err = slab[:L], slab[L:L + L * B1], slab[L + L * B1:]
-        rec_slab = torch.zeros(L * BN, dtype=torch.int8, device=dev) if self.record_masks else None
+        D = layers[0].self_attn.q_proj.weight.shape[1]
+        I = layers[0].mlp.gate_proj.weight.shape[0]
+        V = self._head().weight.shape[0]
+        scale = float(layers[0].self_attn.scaling)
+        probe = torch.zeros(1, N, D, dtype=dtype, device=dev)
+        pos = torch.arange(P, P + N, device=dev).unsqueeze(0)
+        cos, sin = base.rotary_emb(probe, pos)
+        st = {"L": L, "keep": keep}
+        st["cos"] = cos[0].to(dtype).contiguous()
+        st["sin"] = sin[0].to(dtype).contiguous()
+        st["q_scale"] = self._q_scale(cfg, P, N, dev)
+        st["hidden"] = torch.empty(BN, D, dtype=dtype, device=dev)
+        st["par"] = torch.zeros(B1, dtype=torch.int64, device=dev)
+        st["logits"] = torch.empty(B1, N, V, dtype=dtype, device=dev)
+        st["slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32, device=dev)
+        st["host_slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32).pin_memory()
+        st["rec"] = torch.zeros(L * BN, dtype=torch.int8, device=dev) if self.record_masks else None
+        need = lib.sf_verify_workspace_bytes(dtype_code(st["hidden"]), B1, N, D, H, Hkv, hd, I, V, P)
+        st["ws"] = torch.empty(need, dtype=torch.uint8, device=dev)
 
+        layer_arr = (_lib.SfLayer * L)()
+        for li in range(L):
+            w = self._packed_weights[li]
+            sl = layer_arr[li]
+            sl.w_qkv, sl.ln1_w, sl.w_o, sl.ln2_w = (w[0].data_ptr(), w[2].data_ptr(),
+                                                    w[3].data_ptr(), w[4].data_ptr())
+            sl.b_qkv = None if w[1] is None else w[1].data_ptr()
+            sl.w_gate, sl.w_down = w[5].data_ptr(), w[7].data_ptr()
+            sl.w_up = None if w[6] is None else w[6].data_ptr()
+            if P > 0:
+                sl.prefix_k, sl.prefix_v = kv[li]
+        slab = st["slab"]
         args = _lib.SfVerifyArgs()
-        args.dtype = dtype_code(hidden)
+        args.dtype = dtype_code(st["hidden"])
         args.B1, args.N, args.D, args.H, args.Hkv, args.hd = B1, N, D, H, Hkv, hd
         args.I, args.V, args.L, args.P = I, V, L, P
         args.kv_head_stride = kv_stride
@@ -243,32 +289,24 @@ class FoldedVerifyB200:
         args.weights_tiled = 1 if self._tiled else 0
         args.layers = layer_arr
         args.final_norm_w = base.norm.weight.data_ptr()
-        args.lm_w = lm_w.data_ptr()
-        args.par_idx = par_idx.data_ptr()
-        args.hidden_in = hidden.data_ptr()
-        args.cos, args.sin = cos.data_ptr(), sin.data_ptr()
-        args.q_scale = None if q_scale is None else q_scale.data_ptr()
-        args.logits = logits.data_ptr()
-        args.count_slab = count_slab.data_ptr()
-        args.segcnt_slab = segcnt_slab.data_ptr()
-        args.rec_slab = None if rec_slab is None else rec_slab.data_ptr()
-        args.ws = ws.data_ptr()
-        args.ws_bytes = ws.numel()
-        args.err = err.data_ptr()
-        args.stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check(lib.sf_folded_verify_forward(args), "folded verify forward")
-
-        # one sync for the fold counters and the device error word (the reference's :363)
-        mx, sm, bits = torch.stack([count_slab.max(), count_slab.sum(), err[0]]).tolist()
-        if bits:
-            raise _lib.SpecFoldError("folded verify forward: " + _lib.describe_device_error(bits))
-        if count_stats:
-            self._fold_draft_positions = getattr(self, "_fold_draft_positions", 0) + (B1 - 1) * N * L
-            self._fold_draft_recomputed = getattr(self, "_fold_draft_recomputed", 0) + int(sm) - L * N
-        if rec_slab is not None:
-            self.last_rec_masks = rec_slab.view(L, B1, N)
-        del keep
-        return logits, {"max_count": int(mx), "sum_count": int(sm)}
+        args.lm_w = self._lm_w.data_ptr()
+        args.par_idx = st["par"].data_ptr()
+        args.hidden_in = st["hidden"].data_ptr()
+        args.cos, args.sin = st["cos"].data_ptr(), st["sin"].data_ptr()
+        args.q_scale = None if st["q_scale"] is None else st["q_scale"].data_ptr()
+        args.logits = st["logits"].data_ptr()
+        args.count_slab = slab[:L].data_ptr()
+        args.segcnt_slab = slab[L:L + L * B1].data_ptr()
+        args.rec_slab = None if st["rec"] is None else st["rec"].data_ptr()
+        args.ws = st["ws"].data_ptr()
+        args.ws_bytes = st["ws"].numel()
+        args.err = slab[L + L * B1:].data_ptr()
+        st["layer_arr"] = layer_arr
+        st["args"] = args
+        if len(statics) >= 4:
+            statics.pop(next(iter(statics)))
+        statics[key] = st
+        return st
 
     @staticmethod
     def _prefix_view(t: torch.Tensor) -> torch.Tensor:
