@@ -208,7 +208,7 @@ __device__ __forceinline__ void vec_get(const float2& v, float* o) { o[0] = v.x;
 template <typename T, int HD>
 __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const float* part_O,
                                                         const float* part_ml, int splits,
-                                                        int q_rows, int rpc) {
+                                                        int part_rows, int rpc) {
   constexpr int DPL = HD / 32;            // consecutive dims per lane (4 or 2)
   using VD = typename VecF<DPL>::type;
   constexpr int V = Elt<T>::kVec;
@@ -220,10 +220,7 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
   float* qs = sm_rows;                                  // [kRowTasks][HD]
   float* ks = qs + kRowTasks * HD;                      // [32][KS]
   float* vs = ks + kAttnKeys * KS;                      // [32][KS]
-  int* s_slot = reinterpret_cast<int*>(vs + kAttnKeys * KS);   // [BN] (partials only)
-  __shared__ int64_t krow[kAttnKeys];
-  __shared__ int64_t s_qrow[kRowTasks];
-  __shared__ int s_warp_tot[8];
+  __shared__ int s_src[kMaxRows];                       // branch b's src per position
 
   pdl_trigger();
   pdl_wait();
@@ -233,7 +230,6 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
   if (nrows <= 0) return;
   const int G = p.H / p.Hkv;
   const int ntasks = nrows * G;
-  const int BN = p.B1 * p.N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qd = p.H * HD, kvd = 2 * p.Hkv * HD;
   const T* qb = reinterpret_cast<const T*>(p.q_buf);
@@ -241,46 +237,50 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
   const T* pk = reinterpret_cast<const T*>(p.pk);
   const T* pv = reinterpret_cast<const T*>(p.pv);
 
-  // query rows of this CTA's positions
-  if (threadIdx.x < nrows) {
-    const int n = n0 + threadIdx.x;
-    int64_t s = p.src[static_cast<int64_t>(b) * p.N + n];
+  // recomputing ancestor of every position of branch b: query rows of this CTA's
+  // positions and rows of the branch's block keys
+  for (int j = threadIdx.x; j < p.N; j += 256) {
+    int64_t s = p.src[static_cast<int64_t>(b) * p.N + j];
     if (s < 0 || s >= p.B1) { flag_error(p.err, SF_DEV_ERR_INDEX); s = b; }
-    s_qrow[threadIdx.x] = s * p.N + n;
-  }
-  // slot of every row in the compaction order (exclusive scan of rec), for the partials
-  if (part_O != nullptr) {
-    constexpr int kPer = kMaxRows / 256;
-    int fl[kPer], local = 0;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int r = threadIdx.x * kPer + i;
-      fl[i] = r < BN ? (p.rec[r] != 0) : 0;
-      local += fl[i];
-    }
-    int incl = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    if (lane == 31) s_warp_tot[warp] = incl;
-    __syncthreads();
-    int run = incl - local;
-    for (int i = 0; i < warp; ++i) run += s_warp_tot[i];
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int r = threadIdx.x * kPer + i;
-      if (r < BN) s_slot[r] = fl[i] ? run : -1;
-      run += fl[i];
-    }
+    s_src[j] = static_cast<int>(s);
   }
   __syncthreads();
+
+  const int key_begin = part_O != nullptr ? p.P : 0;
+  const int total = p.P + p.N;
+  float kv[TILE_VEC][V], vv[TILE_VEC][V];
+  // keys [k0, k0 + 32) into registers: prefix cache, then branch b's block keys
+  auto load_tile = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < TILE_VEC; ++u) {
+      const int idx = threadIdx.x + 256 * u;
+      const int t = idx / VPR, d0 = (idx % VPR) * V;
+      const int key = k0 + t;
+      if (t < kAttnKeys && key < p.P) {
+        const int64_t o = kvh * p.kv_head_stride + static_cast<int64_t>(key) * HD + d0;
+        load_vec<T>(pk + o, kv[u]);
+        load_vec<T>(pv + o, vv[u]);
+      } else if (t < kAttnKeys && key < total) {
+        const int j = key - p.P;
+        const int64_t o = (static_cast<int64_t>(s_src[j]) * p.N + j) * kvd;
+        load_vec<T>(kvb + o + kvh * HD + d0, kv[u]);
+        load_vec<T>(kvb + o + (p.Hkv + kvh) * HD + d0, vv[u]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < V; ++k) kv[u][k] = vv[u][k] = 0.f;
+      }
+    }
+  };
+  if (key_begin < total) load_tile(key_begin);
+
+  // queries (every task's q row) into shared memory as fp32
   for (int i = threadIdx.x; i < kRowTasks * VPR; i += 256) {
     const int t = i / VPR, d0 = (i % VPR) * V;
     float v[V];
     if (t < ntasks) {
-      load_vec<T>(qb + s_qrow[t / G] * qd + (kvh * G + t % G) * HD + d0, v);
+      const int n = n0 + t / G;
+      const int64_t qrow = static_cast<int64_t>(s_src[n]) * p.N + n;
+      load_vec<T>(qb + qrow * qd + (kvh * G + t % G) * HD + d0, v);
     } else {
 #pragma unroll
       for (int k = 0; k < V; ++k) v[k] = 0.f;
@@ -298,72 +298,53 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
     for (int d = 0; d < DPL; ++d) acc[i][d] = 0.f;
   }
   if (part_O != nullptr) {
+    // the ancestor row's prefix state: merge of its split partials (lane s: split s's m, l)
+    float pm[TPW], pl[TPW];
+#pragma unroll
+    for (int i = 0; i < TPW; ++i) {
+      pm[i] = -INFINITY;
+      pl[i] = 0.f;
+      const int t = warp + 8 * i;
+      if (t < ntasks && lane < splits) {
+        const int n = n0 + t / G;
+        const int64_t qi = (static_cast<int64_t>(s_src[n]) * p.N + n) * G + t % G;
+        const int64_t base = (static_cast<int64_t>(lane) * p.Hkv + kvh) * part_rows + qi;
+        pm[i] = part_ml[2 * base];
+        pl[i] = part_ml[2 * base + 1];
+      }
+    }
 #pragma unroll
     for (int i = 0; i < TPW; ++i) {
       const int t = warp + 8 * i;
       if (t >= ntasks) break;
-      const int slot = s_slot[s_qrow[t / G]];
-      if (slot < 0 || slot >= p.bucket) {   // src row not recomputed, or past the bucket
-        if (slot < 0) flag_error(p.err, SF_DEV_ERR_INDEX);
-        continue;
-      }
-      const int64_t qi = static_cast<int64_t>(slot) * G + (t % G);
-      float ms = -INFINITY, ls = 0.f;
-      if (lane < splits) {
-        const int64_t base = (static_cast<int64_t>(lane) * p.Hkv + kvh) * q_rows + qi;
-        ms = part_ml[2 * base];
-        ls = part_ml[2 * base + 1];
-      }
-      const float mx = warp_max(ms);
-      const float w = (ms == -INFINITY) ? 0.f : expf(ms - mx);
+      const int n = n0 + t / G;
+      const int64_t qi = (static_cast<int64_t>(s_src[n]) * p.N + n) * G + t % G;
+      const float mx = warp_max(pm[i]);
+      const float w = (pm[i] == -INFINITY) ? 0.f : expf(pm[i] - mx);
       m[i] = mx;
-      l[i] = warp_sum(ls * w);
-      for (int s = 0; s < splits; ++s) {
-        const float ws = __shfl_sync(0xffffffffu, w, s);
-        if (ws == 0.f) continue;
-        const int64_t base = (static_cast<int64_t>(s) * p.Hkv + kvh) * q_rows + qi;
-        float o[DPL];
-        vec_get(__ldcg(reinterpret_cast<const VD*>(part_O + base * HD) + lane), o);
+      l[i] = warp_sum(pl[i] * w);
+      for (int s0 = 0; s0 < splits; s0 += 4) {
+        float o[4][DPL];
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(o[d], ws, acc[i][d]);
+        for (int u = 0; u < 4; ++u) {
+          if (s0 + u < splits) {
+            const int64_t base = (static_cast<int64_t>(s0 + u) * p.Hkv + kvh) * part_rows + qi;
+            vec_get(__ldcg(reinterpret_cast<const VD*>(part_O + base * HD) + lane), o[u]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float ws = __shfl_sync(0xffffffffu, w, (s0 + u) & 31);
+          if (s0 + u < splits) {
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(o[u][d], ws, acc[i][d]);
+          }
+        }
       }
     }
   }
-  const int key_begin = part_O != nullptr ? p.P : 0;
-  const int total = p.P + p.N;
   for (int k0 = key_begin; k0 < total; k0 += kAttnKeys) {
     __syncthreads();
-    if (threadIdx.x < kAttnKeys) {
-      const int key = k0 + threadIdx.x;
-      int64_t kr = -1;
-      if (key >= p.P && key < total) {
-        const int j = key - p.P;
-        int64_t s = p.src[static_cast<int64_t>(b) * p.N + j];
-        if (s < 0 || s >= p.B1) { flag_error(p.err, SF_DEV_ERR_INDEX); s = b; }
-        kr = s * p.N + j;
-      }
-      krow[threadIdx.x] = kr;
-    }
-    __syncthreads();
-    float kv[TILE_VEC][V], vv[TILE_VEC][V];
-#pragma unroll
-    for (int u = 0; u < TILE_VEC; ++u) {
-      const int idx = threadIdx.x + 256 * u;
-      const int t = idx / VPR, d0 = (idx % VPR) * V;
-      const int key = k0 + t;
-      if (t < kAttnKeys && key < p.P) {
-        const int64_t o = kvh * p.kv_head_stride + static_cast<int64_t>(key) * HD + d0;
-        load_vec<T>(pk + o, kv[u]);
-        load_vec<T>(pv + o, vv[u]);
-      } else if (t < kAttnKeys && key < total) {
-        const int64_t o = krow[t] * kvd;
-        load_vec<T>(kvb + o + kvh * HD + d0, kv[u]);
-        load_vec<T>(kvb + o + (p.Hkv + kvh) * HD + d0, vv[u]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < V; ++k) kv[u][k] = vv[u][k] = 0.f;
-      }
-    }
 #pragma unroll
     for (int u = 0; u < TILE_VEC; ++u) {
       const int idx = threadIdx.x + 256 * u;
@@ -379,6 +360,7 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
       }
     }
     __syncthreads();
+    if (k0 + kAttnKeys < total) load_tile(k0 + kAttnKeys);   // next tile in flight meanwhile
     const bool valid = (k0 + lane) < total;
     // scores: lane = key; each K row read once for all of the warp's tasks
     float sc[TPW];
@@ -491,10 +473,19 @@ template <typename T, int HD>
 static cudaError_t rows_t(const AttnParams& p, const float* part_O, const float* part_ml,
                           int splits, int q_rows, cudaStream_t st) {
   const int G = p.H / p.Hkv;
-  const int rpc = std::max(1, std::min(p.N, kRowTasks / G));
+  // positions per CTA: as few as keep the grid within one wave at two CTAs per SM
+  // (register-bound), at most kRowTasks / G
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int slots = std::max(1, 2 * sms / std::max(1, p.B1 * p.Hkv));
+  int rpc = (p.N + slots - 1) / slots;
+  rpc = std::max(1, std::min(std::min(p.N, kRowTasks / G), rpc));
   const dim3 grid(p.B1, p.Hkv, (p.N + rpc - 1) / rpc);
-  const size_t smem = (static_cast<size_t>(kRowTasks) * HD + 2 * kAttnKeys * (HD + 4)) * 4 +
-                      static_cast<size_t>(kMaxRows) * 4;
+  const size_t smem = (static_cast<size_t>(kRowTasks) * HD + 2 * kAttnKeys * (HD + 4)) * 4;
   static size_t configured = 0;
   if (configured < smem) {
     cudaError_t e = cudaFuncSetAttribute(attn_rows_kernel<T, HD>,
@@ -514,7 +505,7 @@ cudaError_t launch_attention_rows_partials(int dtype, const AttnParams& p, const
                                            cudaStream_t st) {
   const int G = p.Hkv > 0 ? p.H / p.Hkv : 0;
   if (G <= 0 || p.H % p.Hkv != 0 || G > kRowTasks || splits > 32 ||
-      p.B1 * p.N > kMaxRows || (part_O != nullptr && p.rec == nullptr))
+      p.B1 * p.N > kMaxRows || p.N > kMaxRows)
     return cudaErrorInvalidValue;
   if (dtype == BF16) {
     if (p.hd == 128) return rows_t<__nv_bfloat16, 128>(p, part_O, part_ml, splits, q_rows, st);

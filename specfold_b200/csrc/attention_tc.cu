@@ -32,8 +32,12 @@ struct AttnTcParams {
   const int32_t* count;
   int bucket, G, q_rows, P, kv_rows, splits, keys_per_split, Hkv;
   float scale;
-  float* part_O;    // [splits][Hkv][q_rows][HD]
-  float* part_ml;   // [splits][Hkv][q_rows][2]
+  float* part_O;    // [splits][Hkv][part_rows][HD]
+  float* part_ml;   // [splits][Hkv][part_rows][2]
+  // partial row of query qi = slot*G + g: qi itself, or rows[slot]*G + g (indexed by the
+  // flat block row, for consumers that look rows up without the compaction order)
+  const int64_t* rows;
+  int part_rows;
   int* err;
 };
 
@@ -264,7 +268,9 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     asm volatile("bar.sync 1, 256;" ::: "memory");
     const float l_row = l + s_red[(hh ^ 1) * kQT + r];
     const int qi = q0 + r;
-    const int64_t base = (static_cast<int64_t>(split) * p.Hkv + kvh) * p.q_rows + qi;
+    int64_t pq = qi;
+    if (p.rows != nullptr && qi < Mq) pq = p.rows[qi / p.G] * p.G + qi % p.G;
+    const int64_t base = (static_cast<int64_t>(split) * p.Hkv + kvh) * p.part_rows + pq;
     if (ok && nb > 0) {
       tc_fence_after();
 #pragma unroll
@@ -350,15 +356,16 @@ static int kv_splits(int P) {
 static size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 size_t attn_scratch_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P,
-                          bool need_q_comp) {
+                          bool need_q_comp, int rows_total) {
   if (dtype != BF16 || P <= 0) return 0;
   const int G = H / Hkv;
   const size_t q_rows = static_cast<size_t>(bucket) * G;
+  const size_t part_rows = static_cast<size_t>(std::max(bucket, rows_total)) * G;
   const int S = kv_splits(P);
   size_t b = 0;
   if (need_q_comp) b += up256(Hkv * q_rows * hd * 2);
-  b += up256(static_cast<size_t>(S) * Hkv * q_rows * hd * 4);
-  b += up256(static_cast<size_t>(S) * Hkv * q_rows * 2 * 4);
+  b += up256(static_cast<size_t>(S) * Hkv * part_rows * hd * 4);
+  b += up256(static_cast<size_t>(S) * Hkv * part_rows * 2 * 4);
   return b;
 }
 
@@ -374,13 +381,15 @@ struct PrefixPartials {
 
 // prefix part of every recomputed row's attention: per-split partials in the scratch
 template <int HD>
-static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixPartials* out) {
+static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixPartials* out,
+                                   bool by_row) {
   const int G = a.H / a.Hkv;
   const int q_rows = a.bucket * G;
   const int S = kv_splits(a.P);
   const bool pack = a.q_comp == nullptr;
+  const int rows_total = by_row ? a.B1 * a.N : 0;
   if (a.scratch == nullptr ||
-      a.scratch_bytes < attn_scratch_bytes(BF16, a.bucket, a.H, a.Hkv, HD, a.P, pack))
+      a.scratch_bytes < attn_scratch_bytes(BF16, a.bucket, a.H, a.Hkv, HD, a.P, pack, rows_total))
     return cudaErrorInvalidValue;
   if (a.kv_head_stride % HD != 0) return cudaErrorInvalidValue;
   char* sc = static_cast<char*>(a.scratch);
@@ -405,8 +414,10 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
   p.keys_per_split = ((a.P + S - 1) / S + kKB - 1) / kKB * kKB;
   p.Hkv = a.Hkv;
   p.scale = a.scale;
+  p.part_rows = std::max(a.bucket, rows_total) * G;
+  p.rows = by_row ? a.rows : nullptr;
   p.part_O = reinterpret_cast<float*>(sc);
-  p.part_ml = reinterpret_cast<float*>(sc + up256(static_cast<size_t>(S) * a.Hkv * q_rows * HD * 4));
+  p.part_ml = reinterpret_cast<float*>(sc + up256(static_cast<size_t>(S) * a.Hkv * p.part_rows * HD * 4));
   p.err = a.err;
   CUtensorMap tq, tk, tv;
   if (!att_tmap(&tq, q_comp, static_cast<uint64_t>(a.Hkv) * q_rows, HD) ||
@@ -433,7 +444,7 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
   out->part_O = p.part_O;
   out->part_ml = p.part_ml;
   out->splits = S;
-  out->q_rows = q_rows;
+  out->q_rows = p.part_rows;
   return cudaSuccess;
 }
 
@@ -441,16 +452,17 @@ static bool prefix_on_tc(int dtype, const AttnParams& p) {
   return dtype == BF16 && p.P > 0 && p.pk != nullptr;
 }
 
-static cudaError_t prefix_partials_hd(const AttnParams& p, cudaStream_t st, PrefixPartials* pp) {
-  if (p.hd == 128) return prefix_partials<128>(p, st, pp);
-  if (p.hd == 64) return prefix_partials<64>(p, st, pp);
+static cudaError_t prefix_partials_hd(const AttnParams& p, cudaStream_t st, PrefixPartials* pp,
+                                      bool by_row) {
+  if (p.hd == 128) return prefix_partials<128>(p, st, pp, by_row);
+  if (p.hd == 64) return prefix_partials<64>(p, st, pp, by_row);
   return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st) {
   if (!prefix_on_tc(dtype, p)) return launch_attention_simt(dtype, p, st);
   PrefixPartials pp{};
-  cudaError_t e = prefix_partials_hd(p, st, &pp);
+  cudaError_t e = prefix_partials_hd(p, st, &pp, false);
   if (e != cudaSuccess) return e;
   return launch_attention_simt_partials(BF16, p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
 }
@@ -458,7 +470,7 @@ cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st) {
 cudaError_t launch_attention_rows(int dtype, const AttnParams& p, cudaStream_t st) {
   if (!prefix_on_tc(dtype, p)) return launch_attention_rows_partials(dtype, p, nullptr, nullptr, 0, 0, st);
   PrefixPartials pp{};
-  cudaError_t e = prefix_partials_hd(p, st, &pp);
+  cudaError_t e = prefix_partials_hd(p, st, &pp, true);
   if (e != cudaSuccess) return e;
   return launch_attention_rows_partials(BF16, p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
 }

@@ -176,7 +176,7 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   // tensor-core attention: query copy per kv head + split-KV partials
   const bool tc_attn = dtype == SF_DTYPE_BF16 && P > 0;
   b.q_comp = tc_attn ? c.take(static_cast<size_t>(bucket) * H * hd * es) : nullptr;
-  b.attn_ws_bytes = attn_scratch_bytes(dtype, bucket, H, Hkv, hd, P, false);
+  b.attn_ws_bytes = attn_scratch_bytes(dtype, bucket, H, Hkv, hd, P, false, BN);
   b.attn_ws = b.attn_ws_bytes ? c.take(b.attn_ws_bytes) : nullptr;
   b.total = c.off;
   return b;

@@ -223,8 +223,9 @@ struct AttnParams {
   void* scratch;
   size_t scratch_bytes;
 };
+// rows_total > 0: room for partials indexed by flat block row (launch_attention_rows)
 size_t attn_scratch_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P,
-                          bool need_q_comp);
+                          bool need_q_comp, int rows_total = 0);
 // recomputed rows only (the flash-attention operator)
 cudaError_t launch_attention(int dtype, const AttnParams& p, cudaStream_t st);
 cudaError_t launch_attention_simt(int dtype, const AttnParams& p, cudaStream_t st);
