@@ -598,6 +598,21 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
 }
 
 // The launches of one verify forward on stream st (validated arguments).
+// L2 prefetch plan of a GEMM of the forward (only the fields that shape its plan)
+static WPrefetch pf_plan(int dtype, int tiled, const void* W, int n_out, int K, int rows_cap,
+                         int kind, int inter) {
+  GemmArgs g{};
+  g.dtype = dtype;
+  g.w_tiled = tiled;
+  g.W = W;
+  g.n_out = n_out;
+  g.K = K;
+  g.rows_cap = rows_cap;
+  g.epi.kind = kind;
+  g.epi.inter = inter;
+  return gemm_prefetch_plan(g);
+}
+
 static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStream_t st) {
   const int dtype = a->dtype;
   const int B1 = a->B1, N = a->N, D = a->D, H = a->H, Hkv = a->Hkv, hd = a->hd, I = a->I,
@@ -685,6 +700,9 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     q.ws = b.gemm_ws;
     q.ws_bytes = b.gemm_ws_bytes;
     q.err = a->err;
+    // each GEMM's producer pulls the next GEMM's first weight blocks into L2
+    const int tl = a->weights_tiled;
+    q.next_pf = pf_plan(dtype, tl, ly.w_o, D, qd, BN, EPI_RESID, 0);
     if ((s = timed(K_QKV, st, [&] { return run_gemm(q, st, "qkv"); }))) return s;
 
     AttnParams at{};
@@ -732,6 +750,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     o.ws = b.gemm_ws;
     o.ws_bytes = b.gemm_ws_bytes;
     o.err = a->err;
+    o.next_pf = pf_plan(dtype, tl, ly.w_gate, 2 * I, D, bucket, EPI_SWIGLU, I);
     if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, st, "o_proj"); }))) return s;
 
     RmsRowsParams r{};
@@ -765,6 +784,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     gu.ws = b.gemm_ws;
     gu.ws_bytes = b.gemm_ws_bytes;
     gu.err = a->err;
+    gu.next_pf = pf_plan(dtype, tl, ly.w_down, D, I, bucket, EPI_SCATTER, 0);
     if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, st, "gate/up"); }))) return s;
 
     GemmArgs dn{};
@@ -783,6 +803,8 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     dn.ws = b.gemm_ws;
     dn.ws_bytes = b.gemm_ws_bytes;
     dn.err = a->err;
+    dn.next_pf = li + 1 < L ? pf_plan(dtype, tl, a->layers[li + 1].w_qkv, qd + 2 * kvd, D, bucket, EPI_QKV, 0)
+                            : pf_plan(dtype, tl, a->lm_w, V, D, BN, EPI_LOGITS, 0);
     if ((s = timed(K_DOWN, st, [&] { return run_gemm(dn, st, "down"); }))) return s;
   }
   // last layer's combine, final norm, lm_head

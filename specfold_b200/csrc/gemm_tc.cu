@@ -75,8 +75,8 @@ struct TcParams {
   int double_buf, acc_cols;
   int w_tiled;         // weights in the [tile][kb][128][64] layout
   int stage_budget;    // shared-memory bytes for the pipeline stages
-  const void* w_pf;    // tiled weights to prefetch into L2 before the dependency wait
-  int pf_kb;           // k-blocks per tile of the first unit to prefetch
+  WPrefetch next_pf;   // the next GEMM's first weight blocks, pulled into L2 by the
+                       // producer once it has issued its own last load
   float* partial;      // [splits][rows_cap][n_out] when splits > 1
   int* counters;       // [2 * n_groups]
   EpiParams epi;
@@ -273,12 +273,22 @@ __device__ __forceinline__ void sum_splits8(const float* partial, int splits, in
   }
 }
 
-// First k-block of unit u's K range (nkb blocks).  CTAs start at different k-blocks so
-// that, at any moment, they read different activation blocks: every CTA reads the same
-// activations, and in lockstep all 148 SMs would request the same L2 lines at once.
-// The order is a fixed function of the unit, so results are deterministic.
-__device__ __forceinline__ int kb_rotation(int u, int nkb) {
-  return nkb > 1 ? static_cast<int>((static_cast<unsigned>(u) * 7919u) % static_cast<unsigned>(nkb)) : 0;
+// L2 prefetch of another GEMM's weights (see WPrefetch): worker w of n takes units
+// w, w + n, ...; every (unit, tile) is one contiguous range of the tile layout.
+__device__ __forceinline__ void issue_w_prefetch(const WPrefetch& f, int worker, int n_workers) {
+  if (f.w == nullptr) return;
+  for (int u = worker; u < f.n_units; u += n_workers) {
+    const int grp = u / f.splits, split = u % f.splits;
+    const int kb0 = split * f.kb_per_split;
+    const int npf = min(min(f.kb_total, kb0 + f.kb_per_split) - kb0, f.npf);
+    for (int t = 0; t < f.sub; ++t) {
+      const int tile = grp * f.sub + t;
+      if (tile >= f.n_tiles) break;
+      const char* a = static_cast<const char*>(f.w) + (static_cast<int64_t>(tile) * f.kb_total + kb0) * kWBytes;
+      for (int c = 0; c < npf; c += 4)
+        prefetch_l2_bulk(a + static_cast<int64_t>(c) * kWBytes, min(4, npf - c) * kWBytes);
+    }
+  }
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -302,25 +312,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmX64);
     if (p.mode == 1 && !p.w_tiled) tma_prefetch_desc(&tmW2);
-    // The weights are constant: while the previous kernel still runs, pull the first
-    // unit's first k-blocks into L2 in the order the producer will read them.
-    if (p.w_pf != nullptr && blockIdx.x < p.n_units) {
-      const int u = blockIdx.x, grp = u / p.splits, split = u % p.splits;
-      const int kb0 = split * p.kb_per_split;
-      const int nkb = min(p.kb_total, kb0 + p.kb_per_split) - kb0;
-      const int rot = kb_rotation(u, nkb);
-      const int npf = min(nkb, p.pf_kb);
-      for (int t = 0; t < p.sub; ++t) {
-        const int tile = grp * p.sub + t;
-        if (tile >= p.n_tiles) break;
-        for (int i = 0; i < npf; ++i) {
-          const int kb = kb0 + (i + rot) % nkb;
-          prefetch_l2_bulk(static_cast<const char*>(p.w_pf) +
-                               (static_cast<int64_t>(tile) * p.kb_total + kb) * kWBytes,
-                           kWBytes);
-        }
-      }
-    }
   }
   pdl_trigger();
   pdl_wait();
@@ -381,9 +372,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int prows = min(kMaxPassRows, rows - prow0);
           const int x_rows = x_rows_loaded(prows);
           const uint32_t bytes = w_bytes + x_rows * kXRowBytes;
-          const int nkb = kb1 - kb0, rot = kb_rotation(u, nkb);
+          const int nkb = kb1 - kb0;
           for (int i = 0; i < nkb; ++i, ++it) {
-            const int kb = kb0 + (i + rot) % nkb;
+            const int kb = kb0 + i;
             const int s = it % stages;
             const uint32_t ph = (it / stages) & 1;
             if (!mbar_wait(&empty[s], ph ^ 1, p.err)) { *abort_flag = 1; break; }
@@ -410,6 +401,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
+      // HBM is about to idle for this kernel's tail: start the next GEMM's weights
+      if (!*abort_flag) issue_w_prefetch(p.next_pf, blockIdx.x, gridDim.x);
       // no copy into this CTA's shared memory may still be in flight at exit
       for (int i = max(0, it - stages); i < it; ++i)
         mbar_wait(&full[i % stages], (i / stages) & 1, p.err);
@@ -625,8 +618,8 @@ static int num_sms() {
 struct TcTuning {
   int sub = 0;
   int smem_kb = 170;
-  int pf_mb = 0;       // SF_GEMM_PF_MB: L2 prefetch of the first units' weights, whole grid
-                       // (off: it competed with the running kernel for HBM)
+  int pf_mb = 0;       // SF_GEMM_PF_MB: L2 prefetch budget for the next GEMM's weights
+                       // (off: measured, the step got slower at 40 and 80 MB)
 };
 static const TcTuning& tc_tuning() {
   static TcTuning t;
@@ -687,6 +680,26 @@ static TcPlan tc_plan(int n_out, int K, int mode, int inter, int rows_cap) {
   return pl;
 }
 
+WPrefetch gemm_prefetch_plan(const GemmArgs& a) {
+  WPrefetch f{};
+  if (a.dtype != BF16 || !a.w_tiled || a.W == nullptr) return f;
+  const int mode = a.epi.kind == EPI_SWIGLU ? 1 : 0;
+  const TcPlan pl = tc_plan(a.n_out, a.K, mode, a.epi.inter, a.rows_cap);
+  const int64_t per_kb = static_cast<int64_t>(pl.n_groups) * pl.splits * pl.sub * kWBytes;
+  const int64_t budget = static_cast<int64_t>(tc_tuning().pf_mb) << 20;
+  const int npf = static_cast<int>(std::min<int64_t>(pl.kb_per_split, per_kb > 0 ? budget / per_kb : 0));
+  if (npf <= 0) return f;
+  f.w = a.W;
+  f.n_tiles = pl.n_tiles;
+  f.sub = pl.sub;
+  f.splits = pl.splits;
+  f.kb_total = pl.kb_total;
+  f.kb_per_split = pl.kb_per_split;
+  f.n_units = pl.n_groups * pl.splits;
+  f.npf = npf;
+  return f;
+}
+
 size_t gemm_tc_ws_need(int rows_cap, int n_out, int K, int kind, int inter) {
   const int mode = kind == EPI_SWIGLU ? 1 : 0;
   const TcPlan pl = tc_plan(n_out, K, mode, inter, rows_cap);
@@ -719,15 +732,7 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
   p.acc_cols = pl.acc_cols;
   p.w_tiled = a.w_tiled ? 1 : 0;
   p.stage_budget = pl.stage_budget;
-  // L2 prefetch of each CTA's first k-blocks, capped so the prefetched lines (every CTA's
-  // share together) stay well inside L2 until the producer reads them
-  {
-    const int64_t per_kb = static_cast<int64_t>(std::min(pl.grid, p.n_units)) * pl.sub * kWBytes;
-    const int64_t cap = static_cast<int64_t>(tc_tuning().pf_mb) << 20;
-    const int pf = static_cast<int>(std::min<int64_t>(pl.kb_per_split, per_kb > 0 ? cap / per_kb : 0));
-    p.w_pf = (a.w_tiled && pf > 0) ? a.W : nullptr;
-    p.pf_kb = pf;
-  }
+  p.next_pf = a.next_pf;
   if (pl.splits > 1) {
     const size_t need = kGemmCounterBytes + static_cast<size_t>(pl.splits) * a.rows_cap * a.n_out * 4;
     if (a.ws == nullptr || a.ws_bytes < need) return cudaErrorInvalidValue;

@@ -168,6 +168,13 @@ struct EpiParams {
   int q_comp_rows;         //      (the A operand layout of the tensor-core attention)
 };
 
+// Weights of a GEMM to pull into L2 ahead of it: the first npf k-blocks of every (unit,
+// tile) of its plan, in the order its producer reads them (tile layout only).
+struct WPrefetch {
+  const void* w;           // nullptr: nothing to prefetch
+  int n_tiles, sub, splits, kb_total, kb_per_split, n_units, npf;
+};
+
 struct GemmArgs {
   int dtype;
   const void* X;           // [rows_cap, K] activations (row-major)
@@ -181,7 +188,9 @@ struct GemmArgs {
   size_t ws_bytes;
   int* err;
   int w_tiled;             // W (and W2) already in the tile layout of pack_weight_tiles
+  WPrefetch next_pf;       // optional: the next GEMM's weights to pull into L2
 };
+WPrefetch gemm_prefetch_plan(const GemmArgs& next);
 
 // Weight tile layout for the tensor-core GEMM: [n_tiles][k_blocks][128 rows][64] so
 // that the 16 KB a pipeline stage needs is one contiguous read.  mode 1 (SwiGLU) puts
