@@ -129,6 +129,18 @@ struct Carve {
   }
 };
 
+// device counters of the forward (zeroed per call): [0] the gate's grid barrier,
+// [kSyncFfn + 2*layer ..] the FFN chain's dependencies
+constexpr size_t kSyncBytes = 4096;
+constexpr int kSyncFfn = 16;
+static bool ffn_chain_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SF_CHAIN");
+    return v == nullptr || atoi(v) != 0;
+  }();
+  return on;
+}
+
 struct FwdBufs {
   void *q_buf, *kv_buf, *O, *ffn, *act, *hbuf, *hp, *xn, *gemm_ws, *q_comp, *attn_ws;
   float *M, *Z, *rstd, *rstd2;
@@ -164,7 +176,7 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   b.rec = static_cast<int8_t*>(c.take(static_cast<size_t>(BN)));
   b.gate_red = static_cast<float*>(
       c.take(static_cast<size_t>(BN) * gate_compact_slices(N, D) * 4 * sizeof(float)));
-  b.sync = static_cast<unsigned*>(c.take(256));
+  b.sync = static_cast<unsigned*>(c.take(kSyncBytes));
   size_t g = 0;
   g = std::max(g, ws_gemm(dtype, bucket, qd + 2 * kvd, D, EPI_QKV, 0));
   g = std::max(g, ws_gemm(dtype, BN, D, qd, EPI_RESID, 0));
@@ -572,7 +584,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   const int B1 = a->B1, N = a->N, D = a->D, H = a->H, Hkv = a->Hkv, hd = a->hd, I = a->I,
             V = a->V, L = a->L;
   const int BN = B1 * N;
-  if (B1 < 1 || B1 > kMaxBranches || N < 1 || BN > kMaxRows || L < 1 || I % 64 || V < 1)
+  if (B1 < 1 || B1 > kMaxBranches || N < 1 || BN > kMaxRows || L < 1 || I % 64 || V < 1 ||
+      kSyncFfn + 2 * L > static_cast<int>(kSyncBytes / 4))
     return fail(SF_ERR_ARG, "shape B1=%d N=%d L=%d I=%d V=%d unsupported", B1, N, L, I, V);
   const int bucket = a->bucket;
   if (bucket < 1 || bucket > BN) return fail(SF_ERR_ARG, "bucket %d outside [1, %d]", bucket, BN);
@@ -629,7 +642,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
   }
   s = cuda_status(cudaMemsetAsync(a->count_slab, 0, sizeof(int32_t) * L, st), "memset");
   if (s) return s;
-  s = cuda_status(cudaMemsetAsync(b.sync, 0, 256, st), "memset");
+  s = cuda_status(cudaMemsetAsync(b.sync, 0, kSyncBytes, st), "memset");
   if (s) return s;
   s = cuda_status(cudaMemsetAsync(a->segcnt_slab, 0, sizeof(int32_t) * L * B1, st), "memset");
   if (s) return s;
@@ -753,21 +766,6 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     o.next_pf = pf_plan(dtype, tl, ly.w_gate, 2 * I, D, bucket, EPI_SWIGLU, I);
     if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, st, "o_proj"); }))) return s;
 
-    RmsRowsParams r{};
-    r.x = b.hp;
-    r.rows = b.rows;
-    r.count = count;
-    r.n = bucket;
-    r.n_src = BN;
-    r.w = ly.ln2_w;
-    r.out = b.xn;
-    r.rstd = b.rstd2;
-    r.D = D;
-    r.eps = a->eps;
-    r.err = a->err;
-    if ((s = timed(K_FFN_NORM, st, [&] { return cuda_status(launch_rmsnorm_rows(dtype, r, st), "ffn norm"); })))
-      return s;
-
     GemmArgs gu{};
     gu.dtype = dtype;
     gu.X = b.xn;
@@ -785,7 +783,6 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     gu.ws_bytes = b.gemm_ws_bytes;
     gu.err = a->err;
     gu.next_pf = pf_plan(dtype, tl, ly.w_down, D, I, bucket, EPI_SCATTER, 0);
-    if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, st, "gate/up"); }))) return s;
 
     GemmArgs dn{};
     dn.dtype = dtype;
@@ -805,6 +802,43 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     dn.err = a->err;
     dn.next_pf = li + 1 < L ? pf_plan(dtype, tl, a->layers[li + 1].w_qkv, qd + 2 * kvd, D, bucket, EPI_QKV, 0)
                             : pf_plan(dtype, tl, a->lm_w, V, D, BN, EPI_LOGITS, 0);
+
+    if (dtype == SF_DTYPE_BF16 && a->weights_tiled && ffn_chain_enabled()) {
+      // post-attention RMSNorm + gate/up + down in one launch (fastdllm_v2_folded.py:
+      // 209-219; triton_kernels.py:103-174)
+      PreNormArgs pre{};
+      pre.x = b.hp;
+      pre.rows = b.rows;
+      pre.count = count;
+      pre.w = ly.ln2_w;
+      pre.out = b.xn;
+      pre.n = bucket;
+      pre.n_src = BN;
+      pre.D = D;
+      pre.eps = a->eps;
+      const GemmArgs chain[2] = {gu, dn};
+      if ((s = timed(K_GATEUP, st, [&] {
+             return cuda_status(gemm_chain(chain, 2, &pre, b.sync + kSyncFfn + 2 * li, st), "ffn");
+           })))
+        return s;
+      continue;
+    }
+
+    RmsRowsParams r{};
+    r.x = b.hp;
+    r.rows = b.rows;
+    r.count = count;
+    r.n = bucket;
+    r.n_src = BN;
+    r.w = ly.ln2_w;
+    r.out = b.xn;
+    r.rstd = b.rstd2;
+    r.D = D;
+    r.eps = a->eps;
+    r.err = a->err;
+    if ((s = timed(K_FFN_NORM, st, [&] { return cuda_status(launch_rmsnorm_rows(dtype, r, st), "ffn norm"); })))
+      return s;
+    if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, st, "gate/up"); }))) return s;
     if ((s = timed(K_DOWN, st, [&] { return run_gemm(dn, st, "down"); }))) return s;
   }
   // last layer's combine, final norm, lm_head

@@ -34,6 +34,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "sf_kernels.cuh"
 
@@ -72,7 +73,6 @@ struct TcParams {
   int sub;             // tiles per unit sharing one activation stage (1, 2 or 4)
   int n_groups;        // ceil(n_tiles / sub)
   int splits, kb_total, kb_per_split, n_units;
-  int double_buf, acc_cols;
   int w_tiled;         // weights in the [tile][kb][128][64] layout
   int stage_budget;    // shared-memory bytes for the pipeline stages
   WPrefetch next_pf;   // the next GEMM's first weight blocks, pulled into L2 by the
@@ -297,34 +297,269 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   return v;
 }
 
+// ------------------------------------------------------------------ GEMM chains
+// One launch may run up to two GEMMs back to back ("phases"), optionally preceded by
+// the RMSNorm of phase 0's activation rows.  Phase 1's activations are phase 0's
+// output (the FFN: gate_up -> down).  Units of both phases are spread over the same
+// persistent CTAs; a phase waits for its activations through device counters, and
+// only before its first activation load: the weight blocks of the first stages of a
+// phase are already in flight while the previous phase (or the norm) finishes.
+constexpr int kMaxPhases = 2;
+
+struct PreNorm {           // out[i] = T(w * T(x[rows[i]] * rstd)), i < min(*count, n)
+  const void* x;
+  const int64_t* rows;
+  const int32_t* count;
+  const void* w;
+  void* out;
+  int n;
+  int64_t n_src;
+  int D;
+  float eps;
+};
+
+struct ChainParams {
+  TcParams ph[kMaxPhases];
+  int n_phases;
+  int unit_base[kMaxPhases + 1];   // units of phase k: [unit_base[k], unit_base[k+1])
+  int stage_budget;
+  int max_sub;
+  int ctas_per_sm;                 // CTAs sharing an SM's TMEM
+  int pre_on;
+  PreNorm pre;
+  unsigned* dep;                   // [2] counters, zero at launch: pre-norm CTAs, phase-0 units
+  unsigned dep_target[2];
+  int* err;
+};
+
+// bounded wait for a device counter to reach target (acquire)
+__device__ __forceinline__ bool wait_counter(const unsigned* c, unsigned target, int* err) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+    if (static_cast<int>(v - target) >= 0) return true;
+    if (globaltimer() - t0 > kWaitNs) {
+      flag_error(err, SF_DEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+// generic-proxy stores by other CTAs are read next by this thread's TMA (async proxy)
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+struct EpiCtx {
+  uint32_t tmem;
+  int acc_cols, buf_cols;
+  int q, l, et, h, eh;
+  float* tileT;
+  volatile int* abort_flag;
+};
+
+// Epilogue of one unit (all passes of its activation rows) for phase parameters p.
 template <int KIND>
+__device__ __forceinline__ void epi_unit(const TcParams& p, const EpiCtx& x, int lu, int rows,
+                                         int& acc_it, bool double_buf, uint64_t* acc_full,
+                                         uint64_t* acc_empty) {
+  const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
+  const int grp = lu / p.splits, split = lu % p.splits;
+  const int lane = threadIdx.x & 31;
+  for (int pass = 0; pass < n_pass; ++pass, ++acc_it) {
+    const int prow0 = pass * kMaxPassRows;
+    const int prows = min(kMaxPassRows, rows - prow0);
+    const int buf = double_buf ? (acc_it & 1) : 0;
+    const uint32_t par = double_buf ? ((acc_it >> 1) & 1) : (acc_it & 1);
+    const bool ready = epi_vote_all(!*x.abort_flag && mbar_wait(&acc_full[buf], par, p.err));
+    if (!ready) *x.abort_flag = 1;
+    tc_fence_after();
+    for (int t = 0; ready && t < p.sub; ++t) {
+      const int tile = grp * p.sub + t;
+      if (tile >= p.n_tiles) break;
+      for (int c0 = x.h * kChunk; c0 < prows; c0 += 2 * kChunk) {
+        float v[kChunk];
+        const uint32_t ta = x.tmem + (static_cast<uint32_t>(x.q * 32) << 16) +
+                            static_cast<uint32_t>(buf * x.buf_cols + t * x.acc_cols + c0);
+        tmem_ld16(ta, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) x.tileT[i * kTileLd + x.l] = v[i];
+        epi_sync_half(x.h);
+        const int nr = min(kChunk, prows - c0);
+        if (p.splits > 1) {
+          // fp32 partial of this split, row-major, 16-byte stores
+          float* part = p.partial + (static_cast<int64_t>(split) * p.rows_cap + prow0 + c0) * p.n_out;
+#pragma unroll
+          for (int k = 0; k < kChunk * 32 / 128; ++k) {
+            const int item = x.eh + 128 * k;
+            const int r = item >> 5, l0 = (item & 31) * 4;
+            const int f0 = tc_feature(p, tile, l0);
+            if (r < nr && f0 >= 0)
+              *reinterpret_cast<float4*>(part + static_cast<int64_t>(r) * p.n_out + f0) =
+                  *reinterpret_cast<const float4*>(x.tileT + r * kTileLd + l0);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < kChunk * kGroupsOut<KIND> / 128; ++k) {
+            const int item = x.eh + 128 * k;
+            const int r = item / kGroupsOut<KIND>, l0 = (item % kGroupsOut<KIND>) * 8;
+            if (r < nr) {
+              const float4* a = reinterpret_cast<const float4*>(x.tileT + r * kTileLd + l0);
+              const float4* b =
+                  reinterpret_cast<const float4*>(x.tileT + r * kTileLd + tc_partner_l<KIND>(p, l0));
+              float va[8], vb[8];
+              vec_get(a[0], va); vec_get(a[1], va + 4);
+              vec_get(b[0], vb); vec_get(b[1], vb + 4);
+              epi_group8<KIND>(p, tile, prow0 + c0 + r, l0, va, vb);
+            }
+          }
+        }
+        epi_sync_half(x.h);
+      }
+    }
+    tc_fence_before();
+    if (lane == 0) mbar_arrive(&acc_empty[buf]);
+  }
+  if (p.splits > 1) {
+    // every split of this tile group publishes, then each reduces its slice of rows
+    __threadfence();
+    bool go = epi_vote_all(!*x.abort_flag);
+    if (x.et == 0 && go) {
+      atomicAdd(&p.counters[2 * grp], 1);
+      const uint64_t t0 = globaltimer();
+      while (ld_acquire(&p.counters[2 * grp]) < p.splits) {
+        if (globaltimer() - t0 > kWaitNs) {
+          flag_error(p.err, SF_DEV_ERR_TIMEOUT);
+          *x.abort_flag = 1;
+          break;
+        }
+      }
+    }
+    go = epi_vote_all(!*x.abort_flag);
+    const int slice = (rows + p.splits - 1) / p.splits;
+    const int r0 = split * slice, r1 = min(rows, r0 + slice);
+    const int64_t split_stride = static_cast<int64_t>(p.rows_cap) * p.n_out;
+    // items: (tile t, row r, group of 8 weight rows l0 that emits output)
+    constexpr int GPR = kGroupsOut<KIND>;
+    const int n_items = go ? p.sub * max(0, r1 - r0) * GPR : 0;
+    for (int item = x.et; item < n_items; item += kEpiThreads) {
+      const int t = item / ((r1 - r0) * GPR);
+      const int rem = item - t * (r1 - r0) * GPR;
+      const int r = r0 + rem / GPR, l0 = (rem % GPR) * 8;
+      const int tile = grp * p.sub + t;
+      if (tile >= p.n_tiles) continue;
+      const int fa = tc_feature(p, tile, l0);
+      if (fa < 0) continue;
+      const int fb = tc_feature(p, tile, tc_partner_l<KIND>(p, l0));
+      float va[8] = {}, vb[8] = {};
+      const int64_t row_off = static_cast<int64_t>(r) * p.n_out;
+      sum_splits8(p.partial, p.splits, split_stride, row_off + fa, va);
+      if (fb >= 0 && fb != fa) sum_splits8(p.partial, p.splits, split_stride, row_off + fb, vb);
+      epi_group8<KIND>(p, tile, r, l0, va, fb == fa ? va : vb);
+    }
+    epi_sync_all();
+    if (x.et == 0 && go) {
+      const int prev = atomicAdd(&p.counters[2 * grp + 1], 1);
+      if (prev == p.splits - 1) {      // everyone has passed the wait: reset
+        p.counters[2 * grp] = 0;
+        p.counters[2 * grp + 1] = 0;
+      }
+    }
+  }
+}
+
+// RMSNorm of rows i = blockIdx.x, blockIdx.x + gridDim.x, ... by the 256 epilogue
+// threads (D <= 256 * 8 * 4): one load of the row into registers, block reduction,
+// normalised from the registers (the rmsnorm_cta_kernel arithmetic).
+__device__ __forceinline__ void pre_norm_rows(const PreNorm& pr, int et, float* red, int* err) {
+  using T = __nv_bfloat16;
+  constexpr int V = 8, MAXV = 4;
+  int n = pr.n;
+  if (pr.count) n = min(n, *pr.count);
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int64_t row = pr.rows ? pr.rows[i] : i;
+    const bool okrow = row >= 0 && row < pr.n_src;
+    if (!okrow && et == 0) flag_error(err, SF_DEV_ERR_INDEX);
+    const T* xr = reinterpret_cast<const T*>(pr.x) + (okrow ? row : 0) * pr.D;
+    const T* w = reinterpret_cast<const T*>(pr.w);
+    float a[MAXV][V], g[MAXV][V];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < MAXV; ++u) {
+      const int d = (et + kEpiThreads * u) * V;
+      if (d < pr.D) {
+        load_vec<T>(xr + d, a[u]);
+        load_vec<T>(w + d, g[u]);
+#pragma unroll
+        for (int k = 0; k < V; ++k) ss = fmaf(a[u][k], a[u][k], ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if ((et & 31) == 0) red[et >> 5] = ss;
+    epi_sync_all();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < kEpiWarps; ++k) tot += red[k];
+    epi_sync_all();
+    const float rs = 1.0f / sqrtf(tot / static_cast<float>(pr.D) + pr.eps);
+    T* out = reinterpret_cast<T*>(pr.out) + static_cast<int64_t>(i) * pr.D;
+#pragma unroll
+    for (int u = 0; u < MAXV; ++u) {
+      const int d = (et + kEpiThreads * u) * V;
+      if (d < pr.D) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) a[u][k] = g[u][k] * Elt<T>::rnd(a[u][k] * rs);
+        if (okrow) store_vec<T>(out + d, a[u]);
+      }
+    }
+  }
+}
+
+template <int K0, int K1>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmW2,
-                   const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX64,
-                   TcParams p) {
+    tc_chain_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW2_0,
+                    const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmX64_0,
+                    const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmX1,
+                    const __grid_constant__ CUtensorMap tmX64_1, ChainParams c) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmW);
-    tma_prefetch_desc(&tmX);
-    tma_prefetch_desc(&tmX64);
-    if (p.mode == 1 && !p.w_tiled) tma_prefetch_desc(&tmW2);
+    tma_prefetch_desc(&tmW0);
+    tma_prefetch_desc(&tmX0);
+    tma_prefetch_desc(&tmX64_0);
+    if (c.ph[0].mode == 1 && !c.ph[0].w_tiled) tma_prefetch_desc(&tmW2_0);
+    if (c.n_phases > 1) {
+      tma_prefetch_desc(&tmW1);
+      tma_prefetch_desc(&tmX1);
+      tma_prefetch_desc(&tmX64_1);
+    }
   }
   pdl_trigger();
   pdl_wait();
-  int rows = p.rows_cap;
-  if (p.count) rows = min(rows, *p.count);
-  if (rows <= 0) return;                         // uniform over the grid
-  const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
-  // stage layout from the actual row count: sub weight tiles + the activation boxes
-  const int w_bytes = p.sub * kWBytes;
-  const int stage_bytes = w_bytes + x_rows_loaded(min(rows, kMaxPassRows)) * kXRowBytes;
-  const int stages = min(kMaxStages, p.stage_budget / stage_bytes);
+  int rows_ph[kMaxPhases] = {0, 0};
+  int max_rows = 0;
+  for (int k = 0; k < c.n_phases; ++k) {
+    int r = c.ph[k].rows_cap;
+    if (c.ph[k].count) r = min(r, *c.ph[k].count);
+    rows_ph[k] = max(r, 0);
+    max_rows = max(max_rows, rows_ph[k]);
+  }
+  if (max_rows <= 0) return;                     // uniform over the grid
+  // stage layout from the actual row count: max_sub weight tiles + the activation rows
+  const int w_bytes = c.max_sub * kWBytes;
+  const int stage_bytes = w_bytes + x_rows_loaded(min(max_rows, kMaxPassRows)) * kXRowBytes;
+  const int stages = min(kMaxStages, c.stage_budget / stage_bytes);
+  // TMEM: accumulator columns for the actual rows; double-buffered when two fit
+  const int acc_cols = max_rows <= 128 ? 128 : 256;
+  const bool double_buf = 2 * c.max_sub * acc_cols * c.ctas_per_sm <= 512;
+  const uint32_t buf_cols = c.max_sub * acc_cols;
+  const uint32_t tmem_cols = (double_buf ? 2u : 1u) * buf_cols;
   unsigned char* stage_base = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.stage_budget + kTileTBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.stage_budget + kTileTBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
   uint64_t* acc_full = bars + 2 * kMaxStages;    // [2]
@@ -332,8 +567,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* drain = acc_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const uint32_t tmem_cols = (p.double_buf ? 2u : 1u) * p.sub * p.acc_cols;
-  const uint32_t buf_cols = p.sub * p.acc_cols;
+  float* red = reinterpret_cast<float*>(tmem_slot + 2);   // [kEpiWarps] norm partial sums
+  const int total_units = c.unit_base[c.n_phases];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -362,22 +597,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
+      // activation loads of the stages issued before a phase's input was ready
+      struct Pending { unsigned char* st; uint64_t* bar; int kx, prow0, x_rows; };
+      Pending pend[kMaxStages];
+      int npend = 0;
+      bool dep_ok[kMaxPhases] = {c.pre_on == 0, c.dep_target[1] == 0};
       int it = 0;
-      for (int u = blockIdx.x; u < p.n_units && !*abort_flag; u += gridDim.x) {
-        const int grp = u / p.splits, split = u % p.splits;
+      for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
+        const int ph = (c.n_phases > 1 && u >= c.unit_base[1]) ? 1 : 0;
+        const TcParams& p = c.ph[ph];
+        const CUtensorMap* mW = ph ? &tmW1 : &tmW0;
+        const CUtensorMap* mX = ph ? &tmX1 : &tmX0;
+        const CUtensorMap* mX64 = ph ? &tmX64_1 : &tmX64_0;
+        const int rows = rows_ph[ph];
+        const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
+        const int lu = u - c.unit_base[ph];
+        const int grp = lu / p.splits, split = lu % p.splits;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        auto flush = [&]() -> bool {
+          if (!wait_counter(c.dep + ph, c.dep_target[ph], c.err)) return false;
+          fence_proxy_async_global();
+          for (int k = 0; k < npend; ++k)
+            for (int r = 0; r < pend[k].x_rows; r += 128) {
+              const bool wide = pend[k].x_rows - r > 64;
+              tma_load_2d(pend[k].st + w_bytes + r * kXRowBytes, wide ? mX : mX64, pend[k].bar,
+                          pend[k].kx, pend[k].prow0 + r, pol_x);
+            }
+          npend = 0;
+          dep_ok[ph] = true;
+          return true;
+        };
         for (int pass = 0; pass < n_pass && !*abort_flag; ++pass) {
           const int prow0 = pass * kMaxPassRows;
           const int prows = min(kMaxPassRows, rows - prow0);
           const int x_rows = x_rows_loaded(prows);
-          const uint32_t bytes = w_bytes + x_rows * kXRowBytes;
-          const int nkb = kb1 - kb0;
-          for (int i = 0; i < nkb; ++i, ++it) {
-            const int kb = kb0 + i;
+          const uint32_t bytes = p.sub * kWBytes + x_rows * kXRowBytes;
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = it % stages;
-            const uint32_t ph = (it / stages) & 1;
-            if (!mbar_wait(&empty[s], ph ^ 1, p.err)) { *abort_flag = 1; break; }
+            const uint32_t phs = (it / stages) & 1;
+            if (!mbar_wait(&empty[s], phs ^ 1, p.err)) { *abort_flag = 1; break; }
             unsigned char* st = stage_base + s * stage_bytes;
             mbar_arrive_expect_tx(&full[s], bytes);
             const int kx = kb * kBK;
@@ -385,50 +644,62 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               const int tile = grp * p.sub + t;
               unsigned char* wdst = st + t * kWBytes;
               if (p.w_tiled) {
-                tma_load_2d(wdst, &tmW, &full[s], 0, (tile * p.kb_total + kb) * kTileF, pol_w);
+                tma_load_2d(wdst, mW, &full[s], 0, (tile * p.kb_total + kb) * kTileF, pol_w);
               } else if (p.mode == 1) {
-                tma_load_2d(wdst, &tmW, &full[s], kx, tile * 64, pol_w);
-                tma_load_2d(wdst + kWBytes / 2, &tmW2, &full[s], kx, tile * 64, pol_w);
+                tma_load_2d(wdst, &tmW0, &full[s], kx, tile * 64, pol_w);
+                tma_load_2d(wdst + kWBytes / 2, &tmW2_0, &full[s], kx, tile * 64, pol_w);
               } else {
-                tma_load_2d(wdst, &tmW, &full[s], kx, tile * kTileF, pol_w);
+                tma_load_2d(wdst, mW, &full[s], kx, tile * kTileF, pol_w);
               }
             }
-            for (int r = 0; r < x_rows; r += 128) {
-              const bool wide = x_rows - r > 64;
-              tma_load_2d(st + w_bytes + r * kXRowBytes, wide ? &tmX : &tmX64, &full[s], kx,
-                          prow0 + r, pol_x);
+            if (dep_ok[ph]) {
+              for (int r = 0; r < x_rows; r += 128) {
+                const bool wide = x_rows - r > 64;
+                tma_load_2d(st + w_bytes + r * kXRowBytes, wide ? mX : mX64, &full[s], kx,
+                            prow0 + r, pol_x);
+              }
+            } else {
+              pend[npend++] = {st, &full[s], kx, prow0, x_rows};
+              // every stage holds weights waiting for activations: wait for the input now
+              if (npend == stages && !flush()) { *abort_flag = 1; break; }
             }
           }
         }
+        if (npend > 0 && !*abort_flag && !flush()) *abort_flag = 1;
       }
       // HBM is about to idle for this kernel's tail: start the next GEMM's weights
-      if (!*abort_flag) issue_w_prefetch(p.next_pf, blockIdx.x, gridDim.x);
+      if (!*abort_flag) issue_w_prefetch(c.ph[c.n_phases - 1].next_pf, blockIdx.x, gridDim.x);
       // no copy into this CTA's shared memory may still be in flight at exit
       for (int i = max(0, it - stages); i < it; ++i)
-        mbar_wait(&full[i % stages], (i / stages) & 1, p.err);
+        mbar_wait(&full[i % stages], (i / stages) & 1, c.err);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       int it = 0, acc_it = 0;
-      for (int u = blockIdx.x; u < p.n_units && !*abort_flag; u += gridDim.x) {
-        const int split = u % p.splits;
+      for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
+        const int ph = (c.n_phases > 1 && u >= c.unit_base[1]) ? 1 : 0;
+        const TcParams& p = c.ph[ph];
+        const int rows = rows_ph[ph];
+        const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
+        const int lu = u - c.unit_base[ph];
+        const int split = lu % p.splits;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
-        for (int pass = 0; pass < n_pass; ++pass, ++acc_it) {
+        bool ok = true;
+        for (int pass = 0; pass < n_pass && ok; ++pass, ++acc_it) {
           const int prows = min(kMaxPassRows, rows - pass * kMaxPassRows);
           const int n_mma = ((prows + 15) / 16) * 16;
           const uint32_t idesc = idesc_bf16(128, n_mma);
-          const int buf = p.double_buf ? (acc_it & 1) : 0;
-          const uint32_t par = p.double_buf ? ((acc_it >> 1) & 1) : (acc_it & 1);
-          if (!mbar_wait(&acc_empty[buf], par ^ 1, p.err)) { *abort_flag = 1; break; }
+          const int buf = double_buf ? (acc_it & 1) : 0;
+          const uint32_t par = double_buf ? ((acc_it >> 1) & 1) : (acc_it & 1);
+          if (!mbar_wait(&acc_empty[buf], par ^ 1, p.err)) { *abort_flag = 1; ok = false; break; }
           tc_fence_after();
           const uint32_t d0 = tmem + buf * buf_cols;
-          bool ok = true;
           for (int i = 0; i < kb1 - kb0; ++i, ++it) {
             const int s = it % stages;
-            const uint32_t ph = (it / stages) & 1;
-            if (*abort_flag || !mbar_wait(&full[s], ph, p.err)) { *abort_flag = 1; ok = false; break; }
+            const uint32_t phs = (it / stages) & 1;
+            if (*abort_flag || !mbar_wait(&full[s], phs, p.err)) { *abort_flag = 1; ok = false; break; }
             tc_fence_after();
             const uint32_t a0 = smem_u32(stage_base + s * stage_bytes);
             const uint32_t b0 = a0 + w_bytes;
@@ -436,7 +707,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int k = 0; k < kBK / 16; ++k) {
               const uint64_t bd = sdesc_kmajor_sw128(b0 + k * 32);
               for (int t = 0; t < p.sub; ++t)
-                umma_f16(d0 + t * p.acc_cols, sdesc_kmajor_sw128(a0 + t * kWBytes + k * 32), bd,
+                umma_f16(d0 + t * acc_cols, sdesc_kmajor_sw128(a0 + t * kWBytes + k * 32), bd,
                          idesc, (i > 0 || k > 0) ? 1u : 0u);
             }
             umma_commit(&empty[s]);
@@ -444,123 +715,48 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!ok) break;
           umma_commit(&acc_full[buf]);
         }
+        if (!ok) break;
       }
       umma_commit(drain);                 // every issued MMA done before TMEM is freed
-      mbar_wait(drain, 0, p.err);
+      mbar_wait(drain, 0, c.err);
     }
   } else {
     // ---------------------------------------------------------------- epilogue
     // Two warps per TMEM lane quarter: half h takes the even (h = 0) or odd (h = 1)
     // chunks of kChunk activation rows, so two chunks are in flight per SM sub-partition.
-    const int q = warp & 3;               // TMEM lane quarter of this warp
-    const int l = q * 32 + lane;          // tile-local weight row == TMEM lane
-    const int et = threadIdx.x - 64;      // 0..255 within the epilogue warps
-    const int h = et >> 7;                // epilogue half
-    const int eh = et & 127;              // thread within the half
-    float* tileT = reinterpret_cast<float*>(smem + p.stage_budget) + h * kChunk * kTileLd;
-    int acc_it = 0;
-    for (int u = blockIdx.x; u < p.n_units; u += gridDim.x) {
-      const int grp = u / p.splits, split = u % p.splits;
-      for (int pass = 0; pass < n_pass; ++pass, ++acc_it) {
-        const int prow0 = pass * kMaxPassRows;
-        const int prows = min(kMaxPassRows, rows - prow0);
-        const int buf = p.double_buf ? (acc_it & 1) : 0;
-        const uint32_t par = p.double_buf ? ((acc_it >> 1) & 1) : (acc_it & 1);
-        const bool ready = epi_vote_all(!*abort_flag && mbar_wait(&acc_full[buf], par, p.err));
-        if (!ready) *abort_flag = 1;
-        tc_fence_after();
-        for (int t = 0; ready && t < p.sub; ++t) {
-          const int tile = grp * p.sub + t;
-          if (tile >= p.n_tiles) break;
-          for (int c0 = h * kChunk; c0 < prows; c0 += 2 * kChunk) {
-            float v[kChunk];
-            const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                                static_cast<uint32_t>(buf * buf_cols + t * p.acc_cols + c0);
-            tmem_ld16(ta, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < kChunk; ++i) tileT[i * kTileLd + l] = v[i];
-            epi_sync_half(h);
-            const int nr = min(kChunk, prows - c0);
-            if (p.splits > 1) {
-              // fp32 partial of this split, row-major, 16-byte stores
-              float* part = p.partial + (static_cast<int64_t>(split) * p.rows_cap + prow0 + c0) * p.n_out;
-#pragma unroll
-              for (int k = 0; k < kChunk * 32 / 128; ++k) {
-                const int item = eh + 128 * k;
-                const int r = item >> 5, l0 = (item & 31) * 4;
-                const int f0 = tc_feature(p, tile, l0);
-                if (r < nr && f0 >= 0)
-                  *reinterpret_cast<float4*>(part + static_cast<int64_t>(r) * p.n_out + f0) =
-                      *reinterpret_cast<const float4*>(tileT + r * kTileLd + l0);
-              }
-              epi_sync_half(h);
-            } else {
-#pragma unroll
-              for (int k = 0; k < kChunk * kGroupsOut<KIND> / 128; ++k) {
-                const int item = eh + 128 * k;
-                const int r = item / kGroupsOut<KIND>, l0 = (item % kGroupsOut<KIND>) * 8;
-                if (r < nr) {
-                  const float4* a = reinterpret_cast<const float4*>(tileT + r * kTileLd + l0);
-                  const float4* b =
-                      reinterpret_cast<const float4*>(tileT + r * kTileLd + tc_partner_l<KIND>(p, l0));
-                  float va[8], vb[8];
-                  vec_get(a[0], va); vec_get(a[1], va + 4);
-                  vec_get(b[0], vb); vec_get(b[1], vb + 4);
-                  epi_group8<KIND>(p, tile, prow0 + c0 + r, l0, va, vb);
-                }
-              }
-              epi_sync_half(h);
-            }
-          }
-        }
-        tc_fence_before();
-        if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      }
-      if (p.splits > 1) {
-        // every split of this tile group publishes, then each reduces its slice of rows
+    EpiCtx x;
+    x.tmem = tmem;
+    x.acc_cols = acc_cols;
+    x.buf_cols = buf_cols;
+    x.q = warp & 3;                       // TMEM lane quarter of this warp
+    x.l = x.q * 32 + lane;                // tile-local weight row == TMEM lane
+    x.et = threadIdx.x - 64;              // 0..255 within the epilogue warps
+    x.h = x.et >> 7;                      // epilogue half
+    x.eh = x.et & 127;                    // thread within the half
+    x.tileT = reinterpret_cast<float*>(smem + c.stage_budget) + x.h * kChunk * kTileLd;
+    x.abort_flag = abort_flag;
+    if (c.pre_on) {
+      pre_norm_rows(c.pre, x.et, red, c.err);
+      epi_sync_all();
+      if (x.et == 0) {
         __threadfence();
-        bool go = epi_vote_all(!*abort_flag);
-        if (et == 0 && go) {
-          atomicAdd(&p.counters[2 * grp], 1);
-          const uint64_t t0 = globaltimer();
-          while (ld_acquire(&p.counters[2 * grp]) < p.splits) {
-            if (globaltimer() - t0 > kWaitNs) {
-              flag_error(p.err, SF_DEV_ERR_TIMEOUT);
-              *abort_flag = 1;
-              break;
-            }
-          }
-        }
-        go = epi_vote_all(!*abort_flag);
-        const int slice = (rows + p.splits - 1) / p.splits;
-        const int r0 = split * slice, r1 = min(rows, r0 + slice);
-        const int64_t split_stride = static_cast<int64_t>(p.rows_cap) * p.n_out;
-        // items: (tile t, row r, group of 8 weight rows l0 that emits output)
-        constexpr int GPR = kGroupsOut<KIND>;
-        const int n_items = go ? p.sub * max(0, r1 - r0) * GPR : 0;
-        for (int item = et; item < n_items; item += kEpiThreads) {
-          const int t = item / ((r1 - r0) * GPR);
-          const int rem = item - t * (r1 - r0) * GPR;
-          const int r = r0 + rem / GPR, l0 = (rem % GPR) * 8;
-          const int tile = grp * p.sub + t;
-          if (tile >= p.n_tiles) continue;
-          const int fa = tc_feature(p, tile, l0);
-          if (fa < 0) continue;
-          const int fb = tc_feature(p, tile, tc_partner_l<KIND>(p, l0));
-          float va[8] = {}, vb[8] = {};
-          const int64_t row_off = static_cast<int64_t>(r) * p.n_out;
-          sum_splits8(p.partial, p.splits, split_stride, row_off + fa, va);
-          if (fb >= 0 && fb != fa) sum_splits8(p.partial, p.splits, split_stride, row_off + fb, vb);
-          epi_group8<KIND>(p, tile, r, l0, va, fb == fa ? va : vb);
-        }
+        atomicAdd(c.dep, 1u);
+      }
+    }
+    int acc_it = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+      const int ph = (c.n_phases > 1 && u >= c.unit_base[1]) ? 1 : 0;
+      const int lu = u - c.unit_base[ph];
+      if (ph == 0)
+        epi_unit<K0>(c.ph[0], x, lu, rows_ph[0], acc_it, double_buf, acc_full, acc_empty);
+      else
+        epi_unit<K1>(c.ph[1], x, lu, rows_ph[1], acc_it, double_buf, acc_full, acc_empty);
+      if (ph == 0 && c.n_phases > 1) {
+        // this unit's output is phase 1's input
         epi_sync_all();
-        if (et == 0 && go) {
-          const int prev = atomicAdd(&p.counters[2 * grp + 1], 1);
-          if (prev == p.splits - 1) {      // everyone has passed the wait: reset
-            p.counters[2 * grp] = 0;
-            p.counters[2 * grp + 1] = 0;
-          }
+        if (x.et == 0) {
+          __threadfence();
+          atomicAdd(c.dep + 1, 1u);
         }
       }
     }
@@ -709,7 +905,11 @@ size_t gemm_tc_ws_need(int rows_cap, int n_out, int K, int kind, int inter) {
 
 int gemm_path_is_tc(int dtype) { return dtype == BF16; }
 
-cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
+// Phase parameters and tensor maps of one GEMM (counters at `counters`, partials after
+// the counter region of the workspace).
+static cudaError_t make_phase(const GemmArgs& a, int* counters, TcParams* out, TcPlan* plan,
+                              CUtensorMap* tmW, CUtensorMap* tmW2, CUtensorMap* tmX,
+                              CUtensorMap* tmX64) {
   const int mode = a.epi.kind == EPI_SWIGLU ? 1 : 0;
   const int inter = a.epi.inter;
   if (a.n_out % 8 != 0 || (mode == 1 && inter % 8 != 0)) return cudaErrorInvalidValue;
@@ -728,60 +928,130 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
   p.kb_total = pl.kb_total;
   p.kb_per_split = pl.kb_per_split;
   p.n_units = pl.n_groups * pl.splits;
-  p.double_buf = pl.double_buf;
-  p.acc_cols = pl.acc_cols;
   p.w_tiled = a.w_tiled ? 1 : 0;
   p.stage_budget = pl.stage_budget;
   p.next_pf = a.next_pf;
   if (pl.splits > 1) {
     const size_t need = kGemmCounterBytes + static_cast<size_t>(pl.splits) * a.rows_cap * a.n_out * 4;
     if (a.ws == nullptr || a.ws_bytes < need) return cudaErrorInvalidValue;
-    p.counters = static_cast<int*>(a.ws);
+    p.counters = counters;
     p.partial = reinterpret_cast<float*>(static_cast<char*>(a.ws) + kGemmCounterBytes);
   }
   p.epi = a.epi;
   p.err = a.err;
-
-  CUtensorMap tmW, tmW2, tmX;
   if (p.w_tiled) {
     const uint64_t blocks = static_cast<uint64_t>(pl.n_tiles) * pl.kb_total * kTileF;
-    if (!make_tmap(&tmW, a.W, blocks, kBK, kTileF)) return cudaErrorInvalidValue;
-    tmW2 = tmW;
+    if (!make_tmap(tmW, a.W, blocks, kBK, kTileF)) return cudaErrorInvalidValue;
+    *tmW2 = *tmW;
   } else {
     const uint32_t wrows = mode == 1 ? 64 : kTileF;
     const int w_rows_total = mode == 1 ? inter : a.n_out;
-    if (!make_tmap(&tmW, a.W, w_rows_total, a.K, wrows)) return cudaErrorInvalidValue;
-    if (!make_tmap(&tmW2, mode == 1 ? a.W2 : a.W, w_rows_total, a.K, wrows))
+    if (!make_tmap(tmW, a.W, w_rows_total, a.K, wrows)) return cudaErrorInvalidValue;
+    if (!make_tmap(tmW2, mode == 1 ? a.W2 : a.W, w_rows_total, a.K, wrows))
       return cudaErrorInvalidValue;
   }
-  CUtensorMap tmX64;
-  if (!make_tmap(&tmX, a.X, a.rows_cap, a.K, 128) || !make_tmap(&tmX64, a.X, a.rows_cap, a.K, 64))
+  if (!make_tmap(tmX, a.X, a.rows_cap, a.K, 128) || !make_tmap(tmX64, a.X, a.rows_cap, a.K, 64))
     return cudaErrorInvalidValue;
+  *out = p;
+  *plan = pl;
+  return cudaSuccess;
+}
 
-  const size_t smem = static_cast<size_t>(pl.stage_budget) + kSmemFixed;
-  using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, TcParams);
-  KernelFn kern = nullptr;
-  switch (a.epi.kind) {
-    case EPI_RAW: kern = tc_gemm_kernel<EPI_RAW>; break;
-    case EPI_QKV: kern = tc_gemm_kernel<EPI_QKV>; break;
-    case EPI_RESID: kern = tc_gemm_kernel<EPI_RESID>; break;
-    case EPI_SWIGLU: kern = tc_gemm_kernel<EPI_SWIGLU>; break;
-    case EPI_SCATTER: kern = tc_gemm_kernel<EPI_SCATTER>; break;
-    case EPI_LOGITS: kern = tc_gemm_kernel<EPI_LOGITS>; break;
-    default: return cudaErrorInvalidValue;
+using ChainFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
+                         CUtensorMap, CUtensorMap, ChainParams);
+
+static ChainFn chain_kernel(int k0, int k1) {
+  if (k0 == k1) {
+    switch (k0) {
+      case EPI_RAW: return tc_chain_kernel<EPI_RAW, EPI_RAW>;
+      case EPI_QKV: return tc_chain_kernel<EPI_QKV, EPI_QKV>;
+      case EPI_RESID: return tc_chain_kernel<EPI_RESID, EPI_RESID>;
+      case EPI_SWIGLU: return tc_chain_kernel<EPI_SWIGLU, EPI_SWIGLU>;
+      case EPI_SCATTER: return tc_chain_kernel<EPI_SCATTER, EPI_SCATTER>;
+      case EPI_LOGITS: return tc_chain_kernel<EPI_LOGITS, EPI_LOGITS>;
+      default: return nullptr;
+    }
   }
-  static size_t configured[EPI_LOGITS + 1] = {};
-  if (configured[a.epi.kind] < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  if (k0 == EPI_SWIGLU && k1 == EPI_SCATTER) return tc_chain_kernel<EPI_SWIGLU, EPI_SCATTER>;
+  return nullptr;
+}
+
+cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* pre, unsigned* dep,
+                       cudaStream_t st) {
+  if (n < 1 || n > kMaxPhases || (n > 1 && dep == nullptr) || (pre != nullptr && dep == nullptr))
+    return cudaErrorInvalidValue;
+  ChainParams c{};
+  CUtensorMap tm[kMaxPhases][4];
+  TcPlan pl[kMaxPhases];
+  int* counters = static_cast<int*>(g[0].ws);
+  for (int k = 0; k < n; ++k) {
+    if (k > 0 && !g[k].w_tiled) return cudaErrorInvalidValue;   // untiled SwiGLU: phase 0 only
+    cudaError_t e = make_phase(g[k], counters, &c.ph[k], &pl[k], &tm[k][0], &tm[k][1], &tm[k][2],
+                               &tm[k][3]);
     if (e != cudaSuccess) return e;
-    configured[a.epi.kind] = smem;
+    if (pl[k].splits > 1) counters += 2 * pl[k].n_groups;   // each split phase its own counters
   }
-  // split K: the split CTAs of a tile group wait for one another, all must be resident
-  cudaError_t e = launch_ex(kern, dim3(pl.grid), dim3(kTcThreads), smem, st, pl.splits > 1, tmW,
-                            tmW2, tmX, tmX64, p);
+  if (counters - static_cast<int*>(g[0].ws) > kMaxCounterTiles * 2) return cudaErrorInvalidValue;
+  c.n_phases = n;
+  int grid = 0;
+  bool coop = n > 1 || pre != nullptr;
+  c.unit_base[0] = 0;
+  for (int k = 0; k < n; ++k) {
+    c.unit_base[k + 1] = c.unit_base[k] + c.ph[k].n_units;
+    grid = std::max(grid, pl[k].grid);
+    c.max_sub = std::max(c.max_sub, pl[k].sub);
+    coop = coop || pl[k].splits > 1;
+  }
+  // split phases: every unit on its own resident CTA (the splits of a group wait on each
+  // other); the persistent grid serves all phases
+  for (int k = 0; k < n; ++k)
+    if (pl[k].splits > 1 && c.ph[k].n_units > grid) return cudaErrorInvalidValue;
+  c.stage_budget = pl[0].stage_budget;
+  c.ctas_per_sm = pl[0].ctas_per_sm;
+  c.err = g[0].err;
+  c.dep = dep;
+  if (pre != nullptr) {
+    if (pre->D % 8 != 0 || pre->D > kEpiThreads * 8 * 4) return cudaErrorInvalidValue;
+    c.pre_on = 1;
+    c.pre.x = pre->x;
+    c.pre.rows = pre->rows;
+    c.pre.count = pre->count;
+    c.pre.w = pre->w;
+    c.pre.out = pre->out;
+    c.pre.n = pre->n;
+    c.pre.n_src = pre->n_src;
+    c.pre.D = pre->D;
+    c.pre.eps = pre->eps;
+    c.dep_target[0] = static_cast<unsigned>(grid);
+  }
+  if (n > 1) c.dep_target[1] = static_cast<unsigned>(c.ph[0].n_units);
+
+  ChainFn kern = chain_kernel(g[0].epi.kind, g[n - 1].epi.kind);
+  if (kern == nullptr) return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(c.stage_budget) + kSmemFixed;
+  {
+    static std::mutex mu;
+    static std::vector<std::pair<ChainFn, size_t>> configured;
+    std::lock_guard<std::mutex> lock(mu);
+    bool done = false;
+    for (auto& cf : configured)
+      if (cf.first == kern && cf.second >= smem) done = true;
+    if (!done) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      configured.push_back({kern, smem});
+    }
+  }
+  const int k1 = n > 1 ? 1 : 0;
+  cudaError_t e = launch_ex(kern, dim3(grid), dim3(kTcThreads), smem, st, coop, tm[0][0],
+                            tm[0][1], tm[0][2], tm[0][3], tm[k1][0], tm[k1][2], tm[k1][3], c);
   if (e != cudaSuccess) return e;
   return launched();
+}
+
+cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
+  return gemm_chain(&a, 1, nullptr, nullptr, st);
 }
 
 // ------------------------------------------------------------------ weight tiling

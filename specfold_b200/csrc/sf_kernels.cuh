@@ -192,6 +192,25 @@ struct GemmArgs {
 };
 WPrefetch gemm_prefetch_plan(const GemmArgs& next);
 
+// RMSNorm of the activation rows of a chain's first GEMM, done inside the chain launch:
+// out[i] = T(w * T(x[rows[i]] * rstd)) for i < min(*count, n) (bf16, D <= 8192)
+struct PreNormArgs {
+  const void* x;
+  const int64_t* rows;
+  const int32_t* count;
+  const void* w;
+  void* out;
+  int n;
+  int64_t n_src;
+  int D;
+  float eps;
+};
+// Up to two bf16 GEMMs in one persistent launch, the second reading the first's output
+// (g[1].X == what g[0]'s epilogue writes), optionally preceded by `pre` (which writes
+// g[0].X).  dep: two device counters, zero before the launch.  Shares g[0].ws.
+cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* pre, unsigned* dep,
+                       cudaStream_t st);
+
 // Weight tile layout for the tensor-core GEMM: [n_tiles][k_blocks][128 rows][64] so
 // that the 16 KB a pipeline stage needs is one contiguous read.  mode 1 (SwiGLU) puts
 // rows [64 gate | 64 up] of the same 64 output features in each 128-row block.
