@@ -79,6 +79,23 @@ def build_workload(device, dtype=torch.bfloat16, layers=None, seed=0):
     return dims, model, cache, ids
 
 
+def profiled_traffic(kind):
+    """DRAM bytes (read + write) per launch of the kernel `kind`, from the committed ncu
+    summary profiles/roofline_traffic.txt (lines `kind: bytes`), or None."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles",
+                        "roofline_traffic.txt")
+    try:
+        for line in open(path):
+            line = line.split("#", 1)[0].strip()
+            if ":" in line:
+                k, v = line.split(":", 1)
+                if k.strip() == kind:
+                    return int(float(v.strip()))
+    except OSError:
+        pass
+    return None
+
+
 def algorithmic_bytes(dims, P):
     """Bytes one verify step must move: every weight once + the prefix K/V once."""
     w = dims.weight_bytes(2)
@@ -232,11 +249,18 @@ def run_b200(args):
 
     hbm, tflops, src = peaks()
     wbytes, kvbytes = algorithmic_bytes(dims, P_PREFIX)
-    # dominant kernel: the fused gate/up projection (37888 x 3584 bf16 weights per layer)
-    gu_ms, gu_calls = prof.get("gate_up", (0.0, 0))
-    gu_bytes = 2 * 2 * dims.inter * dims.hidden
+    # dominant kernel: the chained FFN (post-attention norm + gate/up + down: 3 x I x D bf16
+    # weights per layer, one launch per layer), or gate/up alone when not chained
+    if prof.get("ffn", (0.0, 0))[1]:
+        dom, dom_name = "ffn", "ffn chain (RMSNorm + tcgen05 gate/up + SwiGLU + down, one launch)"
+        gu_bytes = 3 * 2 * dims.inter * dims.hidden
+    else:
+        dom, dom_name = "gate_up", "gate_up (tcgen05 swap-AB GEMM + SwiGLU)"
+        gu_bytes = 2 * 2 * dims.inter * dims.hidden
+    gu_ms, gu_calls = prof.get(dom, (0.0, 0))
     gu_avg_s = gu_ms / max(gu_calls, 1) / 1e3
     achieved = gu_bytes / gu_avg_s / 1e9 if gu_avg_s > 0 else 0.0
+    traffic = profiled_traffic(dom)
     step_achieved = (wbytes + kvbytes) / (step_ms / 1e3) / 1e9
     clocks = clk.summary()
     kernels = {k: {"ms_per_step": round(v[0] / args.steps, 4), "calls_per_step": v[1] / args.steps}
@@ -263,11 +287,11 @@ def run_b200(args):
         "e2e": {"value": round(e2e_value, 4), "unit": UNIT,
                 "ms_per_step": round(e2e_ms / args.steps, 4),
                 "h2d_bytes_per_step": B1 * N * 8, "d2h_bytes_per_step": B1 * N * 8},
-        "roofline": {"bound": "hbm", "kernel": "gate_up (tcgen05 swap-AB GEMM + SwiGLU)",
+        "roofline": {"bound": "hbm", "kernel": dom_name,
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": src,
                      "algorithmic_bytes_per_launch": gu_bytes,
-                     "launch_ms": round(gu_avg_s * 1e3, 4), "traffic": None,
+                     "launch_ms": round(gu_avg_s * 1e3, 4), "traffic": traffic,
                      "step_bytes": wbytes + kvbytes,
                      "step_achieved_gbs": round(step_achieved, 1),
                      "step_frac": round(step_achieved / hbm, 4)},

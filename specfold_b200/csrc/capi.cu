@@ -76,11 +76,11 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 // only; one host thread at a time.
 enum ProfKind {
   K_GATE = 0, K_COMPACT, K_QKV, K_ATTN, K_MERGE, K_OPROJ, K_FFN_NORM, K_GATEUP, K_DOWN,
-  K_COMBINE, K_FINAL_NORM, K_LM_HEAD, K_NUM
+  K_COMBINE, K_FINAL_NORM, K_LM_HEAD, K_FFN, K_NUM
 };
 const char* kProfNames[K_NUM] = {"gate", "compact", "qkv", "attention", "merge", "o_proj",
                                  "ffn_norm", "gate_up", "down", "combine", "final_norm",
-                                 "lm_head"};
+                                 "lm_head", "ffn"};
 struct Profiler {
   bool on = false;
   std::vector<cudaEvent_t> ev;
@@ -817,7 +817,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
       pre.D = D;
       pre.eps = a->eps;
       const GemmArgs chain[2] = {gu, dn};
-      if ((s = timed(K_GATEUP, st, [&] {
+      if ((s = timed(K_FFN, st, [&] {
              return cuda_status(gemm_chain(chain, 2, &pre, b.sync + kSyncFfn + 2 * li, st), "ffn");
            })))
         return s;
