@@ -63,6 +63,22 @@ def dist_env():
     return ws, rank, local
 
 
+def max_over_ranks(values, device):
+    """Element-wise max of per-rank timings (device-timed on each rank); identity at N=1."""
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(values)
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def weak_scaling_value(ws, steps, ms):
+    """Whole-job verify steps per second: every rank runs `steps` steps of its own
+    stream (data-parallel replicas, no collective on the path); ms = max over ranks."""
+    return ws * steps / (ms / 1e3)
+
+
 # ----------------------------------------------------------------------------- workload
 def build_workload(device, dtype=torch.bfloat16, layers=None, seed=0):
     from specfold_b200 import synthetic as syn
@@ -238,14 +254,10 @@ def run_b200(args):
     e2e_ms = e0.elapsed_time(e1)
 
     # ---- max over ranks
-    if ws > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms, e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = t.tolist()
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dev)
     step_ms = ms / args.steps
-    value = ws * args.steps / (ms / 1e3)
-    e2e_value = ws * args.steps / (e2e_ms / 1e3)
+    value = weak_scaling_value(ws, args.steps, ms)
+    e2e_value = weak_scaling_value(ws, args.steps, e2e_ms)
 
     hbm, tflops, src = peaks()
     wbytes, kvbytes = algorithmic_bytes(dims, P_PREFIX)
