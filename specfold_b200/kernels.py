@@ -90,6 +90,18 @@ def residual_delta_gate(Hf: torch.Tensor, par_idx: torch.Tensor, delta: float, B
     return out
 
 
+def parent_map(ids: torch.Tensor) -> torch.Tensor:
+    """par_idx [B1] int64 of a [B1, N] int64 token block, on the device
+    (SpecFold*Generation._build_parent_map, fastdllm_v2_folded.py:55-75)."""
+    _check_cuda(ids)
+    ids = ids.contiguous()
+    B1, N = ids.shape
+    out = torch.empty(B1, dtype=torch.int64, device=ids.device)
+    _lib.check(_lib.load().sf_parent_map(ids.data_ptr(), B1, N, out.data_ptr(), _stream()),
+               "parent map")
+    return out
+
+
 def src_resolve(f: torch.Tensor, B1: int, N: int, err: Optional[torch.Tensor] = None):
     _check_cuda(f)
     src = torch.empty_like(f)

@@ -292,3 +292,28 @@ def test_kv_append(dtype):
     ref_k = before_k.clone(); ref_k[:, P:P + n] = nk
     ref_v = before_v.clone(); ref_v[:, P:P + n] = nv
     assert torch.equal(ck, ref_k) and torch.equal(cv, ref_v)
+
+
+# --------------------------------------------------------------------------- parent map
+@pytest.mark.parametrize("B1,N", [(8, 32), (4, 16), (32, 32), (1, 8)])
+def test_parent_map_matches_host(B1, N):
+    """Device parent map == the reference helper's host computation, on draft blocks
+    built as nested edit sets (chains, trees) plus unrelated drafts."""
+    from specfold_b200.folded import FoldedVerifyB200
+    g = torch.Generator().manual_seed(B1 * 100 + N)
+    for trial in range(20):
+        main = torch.randint(0, 50, (N,), generator=g)
+        rows = [main.clone()]
+        for i in range(1, B1):
+            if i > 1 and torch.rand(1, generator=g).item() < 0.7:
+                base = rows[int(torch.randint(0, i, (1,), generator=g))].clone()
+            else:
+                base = main.clone()
+            pos = int(torch.randint(0, N, (1,), generator=g))
+            base[pos] = (base[pos] + 1 + int(torch.randint(0, 5, (1,), generator=g))) % 50
+            rows.append(base)
+        ids = torch.stack(rows).to(torch.int64)
+        parent, _ = FoldedVerifyB200._build_parent_map(ids)
+        want = torch.tensor([0] + [parent[i] for i in range(1, B1)], dtype=torch.int64)
+        got = K.parent_map(ids.cuda()).cpu()
+        assert torch.equal(got, want), (trial, got.tolist(), want.tolist())
