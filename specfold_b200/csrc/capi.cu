@@ -133,12 +133,13 @@ struct Carve {
 // [kSyncFfn + 2*layer ..] the FFN chain's dependencies
 constexpr size_t kSyncBytes = 4096;
 constexpr int kSyncFfn = 16;
-static bool ffn_chain_enabled() {
-  static const bool on = [] {
+// SF_CHAIN: 0 = separate launches, 1 = the FFN chained, 2 (default) = o_proj + FFN chained
+static int chain_level() {
+  static const int lvl = [] {
     const char* v = getenv("SF_CHAIN");
-    return v == nullptr || atoi(v) != 0;
+    return v == nullptr ? 2 : std::max(0, std::min(2, atoi(v)));
   }();
-  return on;
+  return lvl;
 }
 
 struct FwdBufs {
@@ -585,7 +586,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
             V = a->V, L = a->L;
   const int BN = B1 * N;
   if (B1 < 1 || B1 > kMaxBranches || N < 1 || BN > kMaxRows || L < 1 || I % 64 || V < 1 ||
-      kSyncFfn + 2 * L > static_cast<int>(kSyncBytes / 4))
+      kSyncFfn + 8 * L > static_cast<int>(kSyncBytes / 4))
     return fail(SF_ERR_ARG, "shape B1=%d N=%d L=%d I=%d V=%d unsupported", B1, N, L, I, V);
   const int bucket = a->bucket;
   if (bucket < 1 || bucket > BN) return fail(SF_ERR_ARG, "bucket %d outside [1, %d]", bucket, BN);
@@ -764,7 +765,9 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     o.ws_bytes = b.gemm_ws_bytes;
     o.err = a->err;
     o.next_pf = pf_plan(dtype, tl, ly.w_gate, 2 * I, D, bucket, EPI_SWIGLU, I);
-    if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, st, "o_proj"); }))) return s;
+    const bool chained = dtype == SF_DTYPE_BF16 && a->weights_tiled && chain_level() > 0;
+    if (!(chained && chain_level() >= 2))
+      if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, st, "o_proj"); }))) return s;
 
     GemmArgs gu{};
     gu.dtype = dtype;
@@ -803,7 +806,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     dn.next_pf = li + 1 < L ? pf_plan(dtype, tl, a->layers[li + 1].w_qkv, qd + 2 * kvd, D, bucket, EPI_QKV, 0)
                             : pf_plan(dtype, tl, a->lm_w, V, D, BN, EPI_LOGITS, 0);
 
-    if (dtype == SF_DTYPE_BF16 && a->weights_tiled && ffn_chain_enabled()) {
+    if (chained) {
       // post-attention RMSNorm + gate/up + down in one launch (fastdllm_v2_folded.py:
       // 209-219; triton_kernels.py:103-174)
       PreNormArgs pre{};
@@ -816,11 +819,23 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
       pre.n_src = BN;
       pre.D = D;
       pre.eps = a->eps;
-      const GemmArgs chain[2] = {gu, dn};
-      if ((s = timed(K_FFN, st, [&] {
-             return cuda_status(gemm_chain(chain, 2, &pre, b.sync + kSyncFfn + 2 * li, st), "ffn");
-           })))
-        return s;
+      if (chain_level() >= 2) {
+        // o_proj + residual, then the norm, gate/up and down: one launch
+        const GemmArgs chain[3] = {o, gu, dn};
+        const PreNormArgs* norms[3] = {nullptr, &pre, nullptr};
+        if ((s = timed(K_FFN, st, [&] {
+               return cuda_status(gemm_chain(chain, 3, norms, b.sync + kSyncFfn + 8 * li, st),
+                                  "o_proj + ffn");
+             })))
+          return s;
+      } else {
+        const GemmArgs chain[2] = {gu, dn};
+        const PreNormArgs* norms[2] = {&pre, nullptr};
+        if ((s = timed(K_FFN, st, [&] {
+               return cuda_status(gemm_chain(chain, 2, norms, b.sync + kSyncFfn + 8 * li, st), "ffn");
+             })))
+          return s;
+      }
       continue;
     }
 

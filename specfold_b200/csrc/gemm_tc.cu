@@ -298,13 +298,14 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 
 // ------------------------------------------------------------------ GEMM chains
-// One launch may run up to two GEMMs back to back ("phases"), optionally preceded by
-// the RMSNorm of phase 0's activation rows.  Phase 1's activations are phase 0's
-// output (the FFN: gate_up -> down).  Units of both phases are spread over the same
-// persistent CTAs; a phase waits for its activations through device counters, and
-// only before its first activation load: the weight blocks of the first stages of a
-// phase are already in flight while the previous phase (or the norm) finishes.
-constexpr int kMaxPhases = 2;
+// One launch may run up to three GEMMs back to back ("phases"), each optionally preceded
+// by an RMSNorm of its activation rows.  Phase k's activations come from phase k-1's
+// output, directly or through that norm (o_proj -> norm -> gate_up -> down).  Units of
+// all phases are spread over the same persistent CTAs; a phase waits for its
+// activations through device counters, and only before its first activation load: the
+// weight blocks of its first stages are already in flight while the previous phase (or
+// the norm) finishes.
+constexpr int kMaxPhases = 3;
 
 struct PreNorm {           // out[i] = T(w * T(x[rows[i]] * rstd)), i < min(*count, n)
   const void* x;
@@ -320,17 +321,30 @@ struct PreNorm {           // out[i] = T(w * T(x[rows[i]] * rstd)), i < min(*cou
 
 struct ChainParams {
   TcParams ph[kMaxPhases];
+  PreNorm norm[kMaxPhases];        // norm[k].x != nullptr: RMSNorm writing phase k's input
   int n_phases;
   int unit_base[kMaxPhases + 1];   // units of phase k: [unit_base[k], unit_base[k+1])
   int stage_budget;
   int max_sub;
   int ctas_per_sm;                 // CTAs sharing an SM's TMEM
-  int pre_on;
-  PreNorm pre;
-  unsigned* dep;                   // [2] counters, zero at launch: pre-norm CTAs, phase-0 units
-  unsigned dep_target[2];
+  // counters, zero at launch: dep[2k] CTAs done with norm k, dep[2k+1] units of phase k
+  // done (the latter only counted for phases whose output a later phase reads)
+  unsigned* dep;
   int* err;
 };
+
+// what phase k's activation loads wait for: (counter, target), or counter == nullptr
+__device__ __forceinline__ const unsigned* phase_dep(const ChainParams& c, int k, unsigned* target) {
+  if (c.norm[k].x != nullptr) {
+    *target = gridDim.x;
+    return c.dep + 2 * k;
+  }
+  if (k > 0) {
+    *target = static_cast<unsigned>(c.ph[k - 1].n_units);
+    return c.dep + 2 * (k - 1) + 1;
+  }
+  return nullptr;
+}
 
 // bounded wait for a device counter to reach target (acquire)
 __device__ __forceinline__ bool wait_counter(const unsigned* c, unsigned target, int* err) {
@@ -516,12 +530,14 @@ __device__ __forceinline__ void pre_norm_rows(const PreNorm& pr, int et, float* 
   }
 }
 
-template <int K0, int K1>
+template <int K0, int K1, int K2>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_chain_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW2_0,
                     const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmX64_0,
                     const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmX1,
-                    const __grid_constant__ CUtensorMap tmX64_1, ChainParams c) {
+                    const __grid_constant__ CUtensorMap tmX64_1, const __grid_constant__ CUtensorMap tmW2,
+                    const __grid_constant__ CUtensorMap tmX2, const __grid_constant__ CUtensorMap tmX64_2,
+                    ChainParams c) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -537,10 +553,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tma_prefetch_desc(&tmX1);
       tma_prefetch_desc(&tmX64_1);
     }
+    if (c.n_phases > 2) {
+      tma_prefetch_desc(&tmW2);
+      tma_prefetch_desc(&tmX2);
+      tma_prefetch_desc(&tmX64_2);
+    }
   }
   pdl_trigger();
   pdl_wait();
-  int rows_ph[kMaxPhases] = {0, 0};
+  int rows_ph[kMaxPhases] = {0, 0, 0};
   int max_rows = 0;
   for (int k = 0; k < c.n_phases; ++k) {
     int r = c.ph[k].rows_cap;
@@ -549,14 +570,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     max_rows = max(max_rows, rows_ph[k]);
   }
   if (max_rows <= 0) return;                     // uniform over the grid
-  // stage layout from the actual row count: max_sub weight tiles + the activation rows
-  const int w_bytes = c.max_sub * kWBytes;
-  const int stage_bytes = w_bytes + x_rows_loaded(min(max_rows, kMaxPassRows)) * kXRowBytes;
+  // stage layout from the actual row counts: phase k puts its sub_k weight tiles first and its activation rows right
+  // after them; the stage size is the largest over the phases
+  int stage_bytes = 0, buf_cols_i = 0;
+  int acc_ph[kMaxPhases] = {128, 128, 128};
+  for (int k = 0; k < c.n_phases; ++k) {
+    const int xr = rows_ph[k] > 0 ? x_rows_loaded(min(rows_ph[k], kMaxPassRows)) : 0;
+    stage_bytes = max(stage_bytes, c.ph[k].sub * kWBytes + xr * kXRowBytes);
+    // TMEM columns per accumulator from the phase's actual rows
+    acc_ph[k] = rows_ph[k] <= 128 ? 128 : 256;
+    buf_cols_i = max(buf_cols_i, c.ph[k].sub * acc_ph[k]);
+  }
   const int stages = min(kMaxStages, c.stage_budget / stage_bytes);
-  // TMEM: accumulator columns for the actual rows; double-buffered when two fit
-  const int acc_cols = max_rows <= 128 ? 128 : 256;
-  const bool double_buf = 2 * c.max_sub * acc_cols * c.ctas_per_sm <= 512;
-  const uint32_t buf_cols = c.max_sub * acc_cols;
+  // TMEM: double-buffered when two accumulators fit (one unit's epilogue overlaps the next)
+  const bool double_buf = 2 * buf_cols_i * c.ctas_per_sm <= 512;
+  const uint32_t buf_cols = buf_cols_i;
   const uint32_t tmem_cols = (double_buf ? 2u : 1u) * buf_cols;
   unsigned char* stage_base = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.stage_budget + kTileTBytes);
@@ -601,14 +629,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       struct Pending { unsigned char* st; uint64_t* bar; int kx, prow0, x_rows; };
       Pending pend[kMaxStages];
       int npend = 0;
-      bool dep_ok[kMaxPhases] = {c.pre_on == 0, c.dep_target[1] == 0};
+      bool dep_ok[kMaxPhases];
+      for (int k = 0; k < kMaxPhases; ++k) {
+        unsigned tg;
+        dep_ok[k] = k >= c.n_phases || phase_dep(c, k, &tg) == nullptr;
+      }
       int it = 0;
       for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
-        const int ph = (c.n_phases > 1 && u >= c.unit_base[1]) ? 1 : 0;
+        const int ph = u >= c.unit_base[2] ? 2 : (u >= c.unit_base[1] ? 1 : 0);
         const TcParams& p = c.ph[ph];
-        const CUtensorMap* mW = ph ? &tmW1 : &tmW0;
-        const CUtensorMap* mX = ph ? &tmX1 : &tmX0;
-        const CUtensorMap* mX64 = ph ? &tmX64_1 : &tmX64_0;
+        const CUtensorMap* mW = ph == 2 ? &tmW2 : (ph ? &tmW1 : &tmW0);
+        const CUtensorMap* mX = ph == 2 ? &tmX2 : (ph ? &tmX1 : &tmX0);
+        const CUtensorMap* mX64 = ph == 2 ? &tmX64_2 : (ph ? &tmX64_1 : &tmX64_0);
         const int rows = rows_ph[ph];
         const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
         const int lu = u - c.unit_base[ph];
@@ -616,12 +648,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         auto flush = [&]() -> bool {
-          if (!wait_counter(c.dep + ph, c.dep_target[ph], c.err)) return false;
+          unsigned tg = 0;
+          const unsigned* dc = phase_dep(c, ph, &tg);
+          if (dc != nullptr && !wait_counter(dc, tg, c.err)) return false;
           fence_proxy_async_global();
           for (int k = 0; k < npend; ++k)
             for (int r = 0; r < pend[k].x_rows; r += 128) {
               const bool wide = pend[k].x_rows - r > 64;
-              tma_load_2d(pend[k].st + w_bytes + r * kXRowBytes, wide ? mX : mX64, pend[k].bar,
+              tma_load_2d(pend[k].st + p.sub * kWBytes + r * kXRowBytes, wide ? mX : mX64, pend[k].bar,
                           pend[k].kx, pend[k].prow0 + r, pol_x);
             }
           npend = 0;
@@ -655,7 +689,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (dep_ok[ph]) {
               for (int r = 0; r < x_rows; r += 128) {
                 const bool wide = x_rows - r > 64;
-                tma_load_2d(st + w_bytes + r * kXRowBytes, wide ? mX : mX64, &full[s], kx,
+                tma_load_2d(st + p.sub * kWBytes + r * kXRowBytes, wide ? mX : mX64, &full[s], kx,
                             prow0 + r, pol_x);
               }
             } else {
@@ -678,7 +712,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       int it = 0, acc_it = 0;
       for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
-        const int ph = (c.n_phases > 1 && u >= c.unit_base[1]) ? 1 : 0;
+        const int ph = u >= c.unit_base[2] ? 2 : (u >= c.unit_base[1] ? 1 : 0);
         const TcParams& p = c.ph[ph];
         const int rows = rows_ph[ph];
         const int n_pass = (rows + kMaxPassRows - 1) / kMaxPassRows;
@@ -702,12 +736,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (*abort_flag || !mbar_wait(&full[s], phs, p.err)) { *abort_flag = 1; ok = false; break; }
             tc_fence_after();
             const uint32_t a0 = smem_u32(stage_base + s * stage_bytes);
-            const uint32_t b0 = a0 + w_bytes;
+            const uint32_t b0 = a0 + p.sub * kWBytes;
 #pragma unroll
             for (int k = 0; k < kBK / 16; ++k) {
               const uint64_t bd = sdesc_kmajor_sw128(b0 + k * 32);
               for (int t = 0; t < p.sub; ++t)
-                umma_f16(d0 + t * acc_cols, sdesc_kmajor_sw128(a0 + t * kWBytes + k * 32), bd,
+                umma_f16(d0 + t * acc_ph[ph], sdesc_kmajor_sw128(a0 + t * kWBytes + k * 32), bd,
                          idesc, (i > 0 || k > 0) ? 1u : 0u);
             }
             umma_commit(&empty[s]);
@@ -726,7 +760,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // chunks of kChunk activation rows, so two chunks are in flight per SM sub-partition.
     EpiCtx x;
     x.tmem = tmem;
-    x.acc_cols = acc_cols;
     x.buf_cols = buf_cols;
     x.q = warp & 3;                       // TMEM lane quarter of this warp
     x.l = x.q * 32 + lane;                // tile-local weight row == TMEM lane
@@ -735,28 +768,45 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     x.eh = x.et & 127;                    // thread within the half
     x.tileT = reinterpret_cast<float*>(smem + c.stage_budget) + x.h * kChunk * kTileLd;
     x.abort_flag = abort_flag;
-    if (c.pre_on) {
-      pre_norm_rows(c.pre, x.et, red, c.err);
-      epi_sync_all();
-      if (x.et == 0) {
-        __threadfence();
-        atomicAdd(c.dep, 1u);
-      }
-    }
     int acc_it = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-      const int ph = (c.n_phases > 1 && u >= c.unit_base[1]) ? 1 : 0;
-      const int lu = u - c.unit_base[ph];
-      if (ph == 0)
-        epi_unit<K0>(c.ph[0], x, lu, rows_ph[0], acc_it, double_buf, acc_full, acc_empty);
-      else
-        epi_unit<K1>(c.ph[1], x, lu, rows_ph[1], acc_it, double_buf, acc_full, acc_empty);
-      if (ph == 0 && c.n_phases > 1) {
-        // this unit's output is phase 1's input
+    for (int k = 0; k < c.n_phases; ++k) {
+      if (c.norm[k].x != nullptr) {
+        // the norm reads every row of the previous phase's output
+        if (k > 0) {
+          bool ok = true;
+          if (x.et == 0)
+            ok = wait_counter(c.dep + 2 * (k - 1) + 1, static_cast<unsigned>(c.ph[k - 1].n_units), c.err);
+          if (!epi_vote_all(ok && !*abort_flag)) *abort_flag = 1;
+        }
+        if (!*abort_flag) pre_norm_rows(c.norm[k], x.et, red, c.err);
         epi_sync_all();
         if (x.et == 0) {
           __threadfence();
-          atomicAdd(c.dep + 1, 1u);
+          fence_proxy_async_global();
+          atomicAdd(c.dep + 2 * k, 1u);
+        }
+      }
+      // this CTA's units of phase k: u = blockIdx.x + j * gridDim.x in the phase's range
+      const int base = c.unit_base[k];
+      const int first = base + ((static_cast<int>(blockIdx.x) - base) % static_cast<int>(gridDim.x) +
+                                static_cast<int>(gridDim.x)) % static_cast<int>(gridDim.x);
+      for (int u = first; u < c.unit_base[k + 1]; u += gridDim.x) {
+        const int lu = u - base;
+        x.acc_cols = acc_ph[k];
+        if (k == 0)
+          epi_unit<K0>(c.ph[0], x, lu, rows_ph[0], acc_it, double_buf, acc_full, acc_empty);
+        else if (k == 1)
+          epi_unit<K1>(c.ph[1], x, lu, rows_ph[1], acc_it, double_buf, acc_full, acc_empty);
+        else
+          epi_unit<K2>(c.ph[2], x, lu, rows_ph[2], acc_it, double_buf, acc_full, acc_empty);
+        if (k + 1 < c.n_phases) {
+          // this unit's output is the next phase's input
+          epi_sync_all();
+          if (x.et == 0) {
+            __threadfence();
+            fence_proxy_async_global();
+            atomicAdd(c.dep + 2 * k + 1, 1u);
+          }
         }
       }
     }
@@ -958,31 +1008,51 @@ static cudaError_t make_phase(const GemmArgs& a, int* counters, TcParams* out, T
 }
 
 using ChainFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
-                         CUtensorMap, CUtensorMap, ChainParams);
+                         CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
+                         ChainParams);
 
-static ChainFn chain_kernel(int k0, int k1) {
-  if (k0 == k1) {
-    switch (k0) {
-      case EPI_RAW: return tc_chain_kernel<EPI_RAW, EPI_RAW>;
-      case EPI_QKV: return tc_chain_kernel<EPI_QKV, EPI_QKV>;
-      case EPI_RESID: return tc_chain_kernel<EPI_RESID, EPI_RESID>;
-      case EPI_SWIGLU: return tc_chain_kernel<EPI_SWIGLU, EPI_SWIGLU>;
-      case EPI_SCATTER: return tc_chain_kernel<EPI_SCATTER, EPI_SCATTER>;
-      case EPI_LOGITS: return tc_chain_kernel<EPI_LOGITS, EPI_LOGITS>;
+static ChainFn chain_kernel(int n, const int* k) {
+  if (n == 1) {
+    switch (k[0]) {
+      case EPI_RAW: return tc_chain_kernel<EPI_RAW, EPI_RAW, EPI_RAW>;
+      case EPI_QKV: return tc_chain_kernel<EPI_QKV, EPI_QKV, EPI_QKV>;
+      case EPI_RESID: return tc_chain_kernel<EPI_RESID, EPI_RESID, EPI_RESID>;
+      case EPI_SWIGLU: return tc_chain_kernel<EPI_SWIGLU, EPI_SWIGLU, EPI_SWIGLU>;
+      case EPI_SCATTER: return tc_chain_kernel<EPI_SCATTER, EPI_SCATTER, EPI_SCATTER>;
+      case EPI_LOGITS: return tc_chain_kernel<EPI_LOGITS, EPI_LOGITS, EPI_LOGITS>;
       default: return nullptr;
     }
   }
-  if (k0 == EPI_SWIGLU && k1 == EPI_SCATTER) return tc_chain_kernel<EPI_SWIGLU, EPI_SCATTER>;
+  // the FFN (gate/up -> down), and o_proj -> norm -> FFN
+  if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_SCATTER)
+    return tc_chain_kernel<EPI_SWIGLU, EPI_SCATTER, EPI_SCATTER>;
+  if (n == 3 && k[0] == EPI_RESID && k[1] == EPI_SWIGLU && k[2] == EPI_SCATTER)
+    return tc_chain_kernel<EPI_RESID, EPI_SWIGLU, EPI_SCATTER>;
   return nullptr;
 }
 
-cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* pre, unsigned* dep,
+static void set_norm(PreNorm* d, const PreNormArgs* s) {
+  d->x = s->x;
+  d->rows = s->rows;
+  d->count = s->count;
+  d->w = s->w;
+  d->out = s->out;
+  d->n = s->n;
+  d->n_src = s->n_src;
+  d->D = s->D;
+  d->eps = s->eps;
+}
+
+cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms, unsigned* dep,
                        cudaStream_t st) {
-  if (n < 1 || n > kMaxPhases || (n > 1 && dep == nullptr) || (pre != nullptr && dep == nullptr))
-    return cudaErrorInvalidValue;
+  if (n < 1 || n > kMaxPhases) return cudaErrorInvalidValue;
+  bool any_norm = false;
+  for (int k = 0; k < n; ++k) any_norm = any_norm || (norms != nullptr && norms[k] != nullptr);
+  if ((n > 1 || any_norm) && dep == nullptr) return cudaErrorInvalidValue;
   ChainParams c{};
   CUtensorMap tm[kMaxPhases][4];
   TcPlan pl[kMaxPhases];
+  int kinds[kMaxPhases];
   int* counters = static_cast<int*>(g[0].ws);
   for (int k = 0; k < n; ++k) {
     if (k > 0 && !g[k].w_tiled) return cudaErrorInvalidValue;   // untiled SwiGLU: phase 0 only
@@ -990,14 +1060,21 @@ cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* pre, unsigne
                                &tm[k][3]);
     if (e != cudaSuccess) return e;
     if (pl[k].splits > 1) counters += 2 * pl[k].n_groups;   // each split phase its own counters
+    kinds[k] = g[k].epi.kind;
+    if (norms != nullptr && norms[k] != nullptr) {
+      if (norms[k]->D % 8 != 0 || norms[k]->D > kEpiThreads * 8 * 4) return cudaErrorInvalidValue;
+      set_norm(&c.norm[k], norms[k]);
+    }
   }
+  for (int k = n; k < kMaxPhases; ++k) tm[k][0] = tm[k][1] = tm[k][2] = tm[k][3] = tm[0][0];
   if (counters - static_cast<int*>(g[0].ws) > kMaxCounterTiles * 2) return cudaErrorInvalidValue;
   c.n_phases = n;
   int grid = 0;
-  bool coop = n > 1 || pre != nullptr;
+  bool coop = n > 1 || any_norm;
   c.unit_base[0] = 0;
-  for (int k = 0; k < n; ++k) {
-    c.unit_base[k + 1] = c.unit_base[k] + c.ph[k].n_units;
+  for (int k = 0; k < kMaxPhases; ++k) {
+    c.unit_base[k + 1] = c.unit_base[k] + (k < n ? c.ph[k].n_units : 0);
+    if (k >= n) continue;
     grid = std::max(grid, pl[k].grid);
     c.max_sub = std::max(c.max_sub, pl[k].sub);
     coop = coop || pl[k].splits > 1;
@@ -1010,42 +1087,29 @@ cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* pre, unsigne
   c.ctas_per_sm = pl[0].ctas_per_sm;
   c.err = g[0].err;
   c.dep = dep;
-  if (pre != nullptr) {
-    if (pre->D % 8 != 0 || pre->D > kEpiThreads * 8 * 4) return cudaErrorInvalidValue;
-    c.pre_on = 1;
-    c.pre.x = pre->x;
-    c.pre.rows = pre->rows;
-    c.pre.count = pre->count;
-    c.pre.w = pre->w;
-    c.pre.out = pre->out;
-    c.pre.n = pre->n;
-    c.pre.n_src = pre->n_src;
-    c.pre.D = pre->D;
-    c.pre.eps = pre->eps;
-    c.dep_target[0] = static_cast<unsigned>(grid);
-  }
-  if (n > 1) c.dep_target[1] = static_cast<unsigned>(c.ph[0].n_units);
 
-  ChainFn kern = chain_kernel(g[0].epi.kind, g[n - 1].epi.kind);
+  ChainFn kern = chain_kernel(n, kinds);
   if (kern == nullptr) return cudaErrorInvalidValue;
   const size_t smem = static_cast<size_t>(c.stage_budget) + kSmemFixed;
   {
     static std::mutex mu;
-    static std::vector<std::pair<ChainFn, size_t>> configured;
+    static std::vector<std::pair<std::pair<int, ChainFn>, size_t>> configured;
+    int dev = 0;
+    cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     bool done = false;
     for (auto& cf : configured)
-      if (cf.first == kern && cf.second >= smem) done = true;
+      if (cf.first.first == dev && cf.first.second == kern && cf.second >= smem) done = true;
     if (!done) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
       if (e != cudaSuccess) return e;
-      configured.push_back({kern, smem});
+      configured.push_back({{dev, kern}, smem});
     }
   }
-  const int k1 = n > 1 ? 1 : 0;
   cudaError_t e = launch_ex(kern, dim3(grid), dim3(kTcThreads), smem, st, coop, tm[0][0],
-                            tm[0][1], tm[0][2], tm[0][3], tm[k1][0], tm[k1][2], tm[k1][3], c);
+                            tm[0][1], tm[0][2], tm[0][3], tm[1][0], tm[1][2], tm[1][3], tm[2][0],
+                            tm[2][2], tm[2][3], c);
   if (e != cudaSuccess) return e;
   return launched();
 }

@@ -205,10 +205,11 @@ struct PreNormArgs {
   int D;
   float eps;
 };
-// Up to two bf16 GEMMs in one persistent launch, the second reading the first's output
-// (g[1].X == what g[0]'s epilogue writes), optionally preceded by `pre` (which writes
-// g[0].X).  dep: two device counters, zero before the launch.  Shares g[0].ws.
-cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* pre, unsigned* dep,
+// Up to three bf16 GEMMs in one persistent launch, each reading the previous one's
+// output (g[k].X == what g[k-1]'s epilogue writes, or what norms[k] writes from it);
+// norms[k] (nullable array, nullable entries) is an RMSNorm writing g[k].X.
+// dep: 2 * n device counters, zero before the launch.  Shares g[0].ws.
+cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms, unsigned* dep,
                        cudaStream_t st);
 
 // Weight tile layout for the tensor-core GEMM: [n_tiles][k_blocks][128 rows][64] so
