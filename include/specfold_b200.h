@@ -221,7 +221,23 @@ typedef struct sf_verify_args {
   size_t ws_bytes;
   int* err;                    /* device error word (SF_DEV_*), zeroed by the call */
   void* stream;
+  /* tensor parallelism (the 14B configuration: attention heads and the intermediate
+   * dimension sharded over tp_size ranks).  tp_size <= 1: off.  Otherwise
+   * H, Hkv and I are this rank's shard, the weights and prefix K/V are its shards, and
+   * tp_comm comes from sf_tp_comm_init; o_proj and down are all-reduced in fp32. */
+  void* tp_comm;
+  int tp_size;
 } sf_verify_args;
+
+/* Tensor-parallel communicator (NCCL, loaded at run time).  Rank 0 calls
+ * sf_tp_unique_id (128 bytes), the host broadcasts it, every rank calls
+ * sf_tp_comm_init on its own device.  Release captured graphs (sf_release_graphs)
+ * before sf_tp_comm_destroy. */
+int sf_tp_unique_id(void* id_out, int bytes);
+int sf_tp_comm_init(const void* id, int nranks, int rank, void** comm_out);
+int sf_tp_comm_destroy(void* comm);
+/* Destroys every CUDA graph the forward captured (all devices). */
+int sf_release_graphs(void);
 
 /* The parent map of a verify block on the device: par_idx[i] = the first branch whose
  * set of positions differing from the main branch (row 0 of ids) is a subset of

@@ -40,6 +40,7 @@ class SfVerifyArgs(C.Structure):
         ("q_scale", c_void_p), ("logits", c_void_p), ("count_slab", c_void_p),
         ("segcnt_slab", c_void_p), ("rec_slab", c_void_p), ("ws", c_void_p),
         ("ws_bytes", c_size_t), ("err", c_void_p), ("stream", c_void_p),
+        ("tp_comm", c_void_p), ("tp_size", c_int),
     ]
 
 
@@ -86,6 +87,10 @@ _SIGS = {
                              c_int, c_int, c_int, c_int, c_void_p]),
     "sf_weight_tiles_bytes": (c_size_t, [c_int] * 4),
     "sf_parent_map": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "sf_tp_unique_id": (c_int, [c_void_p, c_int]),
+    "sf_tp_comm_init": (c_int, [c_void_p, c_int, c_int, C.POINTER(c_void_p)]),
+    "sf_tp_comm_destroy": (c_int, [c_void_p]),
+    "sf_release_graphs": (c_int, []),
     "sf_pack_weight_tiles": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                      c_void_p]),
     "sf_launch_count": (C.c_longlong, []),

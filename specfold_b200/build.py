@@ -18,7 +18,8 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libspecfold_b200.so")
-SOURCES = ["gate.cu", "gemm.cu", "gemm_tc.cu", "attention.cu", "attention_tc.cu", "merge.cu", "capi.cu", "ffn_static.cu"]
+SOURCES = ["gate.cu", "gemm.cu", "gemm_tc.cu", "attention.cu", "attention_tc.cu", "merge.cu",
+           "tp.cu", "capi.cu", "ffn_static.cu"]
 HEADERS = ["sf_common.cuh", "sf_kernels.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -61,7 +62,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         objs.append(obj)
-    cmd = [nvcc(), "-shared", "-o", LIB] + objs + ARCH + ["-cudart", "static", "-Xcompiler", "-fPIC"]
+    cmd = [nvcc(), "-shared", "-o", LIB] + objs + ARCH + ["-cudart", "static", "-Xcompiler", "-fPIC",
+                                                          "-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

@@ -148,6 +148,7 @@ struct FwdBufs {
   int64_t *f, *src, *seg, *rows;
   int8_t* rec;
   float* gate_red;        // gate partial sums [BN][S][4]
+  float* tp_sum;          // tensor parallel: fp32 partial sums [BN][D] of o_proj / down
   unsigned* sync;         // grid barrier counter (zeroed per forward)
   size_t gemm_ws_bytes, attn_ws_bytes, total;
 };
@@ -178,6 +179,7 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   b.gate_red = static_cast<float*>(
       c.take(static_cast<size_t>(BN) * gate_compact_slices(N, D) * 4 * sizeof(float)));
   b.sync = static_cast<unsigned*>(c.take(kSyncBytes));
+  b.tp_sum = static_cast<float*>(c.take(static_cast<size_t>(BN) * D * sizeof(float)));
   size_t g = 0;
   g = std::max(g, ws_gemm(dtype, bucket, qd + 2 * kvd, D, EPI_QKV, 0));
   g = std::max(g, ws_gemm(dtype, BN, D, qd, EPI_RESID, 0));
@@ -597,6 +599,8 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     return fail(SF_ERR_ARG, "null pointer in verify args");
   if (a->P < 0 || (a->P > 0 && a->kv_head_stride < static_cast<int64_t>(a->P) * hd))
     return fail(SF_ERR_ARG, "prefix length / stride mismatch");
+  if (a->tp_size > 1 && (a->tp_comm == nullptr || D % 4 != 0))
+    return fail(SF_ERR_ARG, "tensor parallel forward needs a communicator (sf_tp_comm_init)");
   FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket, a->P);
   if (b.total > a->ws_bytes)
     return fail(SF_ERR_WORKSPACE, "workspace %zu < %zu bytes", a->ws_bytes, b.total);
@@ -612,6 +616,11 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
 }
 
 // The launches of one verify forward on stream st (validated arguments).
+static int tp_status(int r) {
+  if (r == 0) return 0;
+  return fail(SF_ERR_CUDA, "tensor-parallel all-reduce: %s", tp_error_string(r));
+}
+
 // L2 prefetch plan of a GEMM of the forward (only the fields that shape its plan)
 static WPrefetch pf_plan(int dtype, int tiled, const void* W, int n_out, int K, int rows_cap,
                          int kind, int inter) {
@@ -765,8 +774,25 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     o.ws_bytes = b.gemm_ws_bytes;
     o.err = a->err;
     o.next_pf = pf_plan(dtype, tl, ly.w_gate, 2 * I, D, bucket, EPI_SWIGLU, I);
-    const bool chained = dtype == SF_DTYPE_BF16 && a->weights_tiled && chain_level() > 0;
-    if (!(chained && chain_level() >= 2))
+    if (a->tp_size > 1) {
+      // tensor parallel: this rank's heads give a partial o_proj sum; all-reduce, then
+      // hp = T(x + T(sum)) as the unsharded epilogue does
+      GemmArgs op = o;
+      op.epi.kind = EPI_RAW;
+      op.epi.out = b.tp_sum;
+      op.epi.resid = nullptr;
+      op.epi.ld_out = D;
+      op.next_pf = WPrefetch{};
+      if ((s = timed(K_OPROJ, st, [&] { return run_gemm(op, st, "o_proj (tp)"); }))) return s;
+      if ((s = tp_status(tp_allreduce_f32(a->tp_comm, b.tp_sum, static_cast<size_t>(BN) * D, st))))
+        return s;
+      if ((s = cuda_status(launch_resid_add(dtype, b.tp_sum, Hf, b.hp, static_cast<int64_t>(BN) * D, st),
+                           "residual add")))
+        return s;
+    }
+    const bool chained = dtype == SF_DTYPE_BF16 && a->weights_tiled && chain_level() > 0 &&
+                         a->tp_size <= 1;
+    if (a->tp_size <= 1 && !(chained && chain_level() >= 2))
       if ((s = timed(K_OPROJ, st, [&] { return run_gemm(o, st, "o_proj"); }))) return s;
 
     GemmArgs gu{};
@@ -806,6 +832,59 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     dn.next_pf = li + 1 < L ? pf_plan(dtype, tl, a->layers[li + 1].w_qkv, qd + 2 * kvd, D, bucket, EPI_QKV, 0)
                             : pf_plan(dtype, tl, a->lm_w, V, D, BN, EPI_LOGITS, 0);
 
+    if (a->tp_size > 1) {
+      // this rank's intermediate shard: gate/up + down partial sums, all-reduce, scatter
+      GemmArgs dp = dn;
+      dp.epi.kind = EPI_RAW;
+      dp.epi.out = b.tp_sum;
+      dp.epi.rows = nullptr;
+      dp.epi.ld_out = D;
+      dp.next_pf = WPrefetch{};
+      const bool tp_chain = dtype == SF_DTYPE_BF16 && a->weights_tiled && chain_level() > 0;
+      if (tp_chain) {
+        PreNormArgs pre{};
+        pre.x = b.hp;
+        pre.rows = b.rows;
+        pre.count = count;
+        pre.w = ly.ln2_w;
+        pre.out = b.xn;
+        pre.n = bucket;
+        pre.n_src = BN;
+        pre.D = D;
+        pre.eps = a->eps;
+        const GemmArgs chain[2] = {gu, dp};
+        const PreNormArgs* norms[2] = {&pre, nullptr};
+        if ((s = timed(K_FFN, st, [&] {
+               return cuda_status(gemm_chain(chain, 2, norms, b.sync + kSyncFfn + 8 * li, st),
+                                  "ffn (tp)");
+             })))
+          return s;
+      } else {
+        RmsRowsParams r{};
+        r.x = b.hp;
+        r.rows = b.rows;
+        r.count = count;
+        r.n = bucket;
+        r.n_src = BN;
+        r.w = ly.ln2_w;
+        r.out = b.xn;
+        r.rstd = b.rstd2;
+        r.D = D;
+        r.eps = a->eps;
+        r.err = a->err;
+        if ((s = timed(K_FFN_NORM, st, [&] { return cuda_status(launch_rmsnorm_rows(dtype, r, st), "ffn norm"); })))
+          return s;
+        if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, st, "gate/up"); }))) return s;
+        if ((s = timed(K_DOWN, st, [&] { return run_gemm(dp, st, "down (tp)"); }))) return s;
+      }
+      if ((s = tp_status(tp_allreduce_f32(a->tp_comm, b.tp_sum, static_cast<size_t>(bucket) * D, st))))
+        return s;
+      if ((s = cuda_status(launch_scatter_rows(dtype, b.tp_sum, b.rows, count, bucket, D, BN + 1,
+                                               b.ffn, a->err, st),
+                           "ffn scatter")))
+        return s;
+      continue;
+    }
     if (chained) {
       // post-attention RMSNorm + gate/up + down in one launch (fastdllm_v2_folded.py:
       // 209-219; triton_kernels.py:103-174)
@@ -933,6 +1012,20 @@ cudaStream_t capture_stream(int device) {
 
 }  // namespace
 
+int sf_release_graphs(void) {
+  std::lock_guard<std::mutex> lock(g_graph_mu);
+  int dev0 = 0;
+  cudaGetDevice(&dev0);
+  for (auto& e : g_graphs) {
+    cudaSetDevice(e.device);
+    cudaGraphExecDestroy(e.exec);
+  }
+  cudaSetDevice(dev0);
+  g_graphs.clear();
+  g_seen.clear();
+  return 0;
+}
+
 static int forward_graph(const sf_verify_args* a, const FwdBufs& b) {
   int dev = 0;
   int s = cuda_status(cudaGetDevice(&dev), "get device");
@@ -996,6 +1089,28 @@ static int forward_graph(const sf_verify_args* a, const FwdBufs& b) {
   s = cuda_status(cudaGraphLaunch(exec, st), "graph launch");
   if (!s) count_launch(static_cast<int>(n));
   return s;
+}
+
+int sf_tp_unique_id(void* id_out, int bytes) {
+  if (!id_out) return fail(SF_ERR_ARG, "null pointer");
+  const int r = tp_unique_id(id_out, bytes);
+  if (r == -1) return fail(SF_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
+  if (r == -2) return fail(SF_ERR_ARG, "id buffer smaller than 128 bytes");
+  return r ? fail(SF_ERR_CUDA, "ncclGetUniqueId: %s", tp_error_string(r)) : 0;
+}
+
+int sf_tp_comm_init(const void* id, int nranks, int rank, void** comm_out) {
+  if (!id || !comm_out || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(SF_ERR_ARG, "bad communicator arguments");
+  const int r = tp_comm_init(id, nranks, rank, comm_out);
+  if (r == -1) return fail(SF_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
+  return r ? fail(SF_ERR_CUDA, "ncclCommInitRank: %s", tp_error_string(r)) : 0;
+}
+
+int sf_tp_comm_destroy(void* comm) {
+  if (!comm) return 0;
+  const int r = tp_comm_destroy(comm);
+  return r ? fail(SF_ERR_CUDA, "ncclCommDestroy: %s", tp_error_string(r)) : 0;
 }
 
 int sf_parent_map(const int64_t* ids, int B1, int N, int64_t* par_idx, void* stream) {

@@ -1026,6 +1026,9 @@ static ChainFn chain_kernel(int n, const int* k) {
   // the FFN (gate/up -> down), and o_proj -> norm -> FFN
   if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_SCATTER)
     return tc_chain_kernel<EPI_SWIGLU, EPI_SCATTER, EPI_SCATTER>;
+  // tensor parallel: the down projection's fp32 partial sums go to the all-reduce
+  if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_RAW)
+    return tc_chain_kernel<EPI_SWIGLU, EPI_RAW, EPI_RAW>;
   if (n == 3 && k[0] == EPI_RESID && k[1] == EPI_SWIGLU && k[2] == EPI_SCATTER)
     return tc_chain_kernel<EPI_RESID, EPI_SWIGLU, EPI_SCATTER>;
   return nullptr;

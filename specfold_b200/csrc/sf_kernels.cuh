@@ -284,6 +284,18 @@ struct MergeParams {
 };
 cudaError_t launch_merge(int dtype, const MergeParams& p, cudaStream_t st);
 
+// ------------------------------------------------------------------ tensor parallel
+const char* tp_error_string(int r);
+int tp_unique_id(void* out, int bytes);
+int tp_comm_init(const void* id, int nranks, int rank, void** comm);
+int tp_comm_destroy(void* comm);
+int tp_allreduce_f32(void* comm, float* buf, size_t n, cudaStream_t st);
+cudaError_t launch_resid_add(int dtype, const float* sum, const void* resid, void* out, int64_t n,
+                             cudaStream_t st);
+cudaError_t launch_scatter_rows(int dtype, const float* sum, const int64_t* rows,
+                                const int32_t* count, int n, int D, int64_t n_out_rows, void* out,
+                                int* err, cudaStream_t st);
+
 cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, const void* nk,
                              const void* nv, int64_t n_stride, int Hkv, int hd, int P, int n,
                              cudaStream_t st);

@@ -1,0 +1,156 @@
+// Tensor parallelism of the folded verify forward (the 14B configuration): each rank
+// holds a head / intermediate shard of every layer; the two row-sharded projections
+// (o_proj and down) produce fp32 partial sums that are all-reduced over NVLink, then the
+// residual add (o_proj) and the row scatter (down) run on the reduced sums.
+//
+// NCCL is loaded at run time (dlopen "libnccl.so.2"): the process's own copy when torch
+// already loaded it, the system one otherwise; the library has no link-time dependency
+// on it.  The communicator is this library's own (ncclCommInitRank on an id that rank 0
+// creates and the host broadcasts), so the all-reduces are plain stream operations that
+// a CUDA graph of the forward captures.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <mutex>
+
+#include "sf_kernels.cuh"
+
+namespace sf {
+
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce &&
+             api.error_string;
+  });
+  return api;
+}
+
+}  // namespace
+
+const char* tp_error_string(int r) {
+  const NcclApi& a = nccl();
+  return a.ok ? a.error_string(static_cast<ncclResult_t>(r)) : "NCCL not loadable";
+}
+
+int tp_unique_id(void* out, int bytes) {
+  const NcclApi& a = nccl();
+  if (!a.ok) return -1;
+  if (bytes < static_cast<int>(sizeof(ncclUniqueId))) return -2;
+  return static_cast<int>(a.get_unique_id(static_cast<ncclUniqueId*>(out)));
+}
+
+int tp_comm_init(const void* id, int nranks, int rank, void** comm) {
+  const NcclApi& a = nccl();
+  if (!a.ok) return -1;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclComm_t c = nullptr;
+  const ncclResult_t r = a.comm_init_rank(&c, nranks, uid, rank);
+  *comm = c;
+  return static_cast<int>(r);
+}
+
+int tp_comm_destroy(void* comm) {
+  const NcclApi& a = nccl();
+  if (!a.ok) return -1;
+  return static_cast<int>(a.comm_destroy(static_cast<ncclComm_t>(comm)));
+}
+
+int tp_allreduce_f32(void* comm, float* buf, size_t n, cudaStream_t st) {
+  const NcclApi& a = nccl();
+  if (!a.ok) return -1;
+  return static_cast<int>(
+      a.all_reduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(comm), st));
+}
+
+// hp[i] = T(resid[i] + T(sum[i])): the EPI_RESID arithmetic on the all-reduced sums
+template <typename T>
+__global__ void __launch_bounds__(256) resid_add_kernel(const float* __restrict__ sum,
+                                                        const T* __restrict__ resid, T* out,
+                                                        int64_t n) {
+  for (int64_t i = (blockIdx.x * 256ll + threadIdx.x) * 4; i < n; i += 256ll * gridDim.x * 4) {
+    const float4 s = *reinterpret_cast<const float4*>(sum + i);
+    float r[4], o[4];
+    const float sv[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      r[k] = Elt<T>::to_f(resid[i + k]);
+      o[k] = __fadd_rn(r[k], Elt<T>::rnd(sv[k]));
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) out[i + k] = Elt<T>::from_f(o[k]);
+  }
+}
+
+// out[rows[j]][:] = T(sum[j][:]) for j < min(*count, n): the EPI_SCATTER arithmetic
+template <typename T>
+__global__ void __launch_bounds__(256) scatter_rows_kernel(const float* __restrict__ sum,
+                                                           const int64_t* rows,
+                                                           const int32_t* count, int n, int D,
+                                                           int64_t n_out_rows, T* out, int* err) {
+  const int j = blockIdx.x;
+  const int cnt = min(*count, n);
+  if (j >= cnt) return;
+  const int64_t r = rows[j];
+  if (r < 0 || r >= n_out_rows) {
+    if (threadIdx.x == 0) flag_error(err, SF_DEV_ERR_INDEX);
+    return;
+  }
+  for (int d = threadIdx.x * 4; d < D; d += 256 * 4) {
+    const float4 s = *reinterpret_cast<const float4*>(sum + static_cast<int64_t>(j) * D + d);
+    out[r * D + d] = Elt<T>::from_f(s.x);
+    out[r * D + d + 1] = Elt<T>::from_f(s.y);
+    out[r * D + d + 2] = Elt<T>::from_f(s.z);
+    out[r * D + d + 3] = Elt<T>::from_f(s.w);
+  }
+}
+
+cudaError_t launch_resid_add(int dtype, const float* sum, const void* resid, void* out, int64_t n,
+                             cudaStream_t st) {
+  if (n % 4 != 0) return cudaErrorInvalidValue;
+  const int blocks = static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256, 148 * 8));
+  if (dtype == BF16)
+    resid_add_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        sum, static_cast<const __nv_bfloat16*>(resid), static_cast<__nv_bfloat16*>(out), n);
+  else
+    resid_add_kernel<float><<<blocks, 256, 0, st>>>(sum, static_cast<const float*>(resid),
+                                                    static_cast<float*>(out), n);
+  return launched();
+}
+
+cudaError_t launch_scatter_rows(int dtype, const float* sum, const int64_t* rows,
+                                const int32_t* count, int n, int D, int64_t n_out_rows, void* out,
+                                int* err, cudaStream_t st) {
+  if (D % 4 != 0 || n <= 0) return n <= 0 ? cudaSuccess : cudaErrorInvalidValue;
+  if (dtype == BF16)
+    scatter_rows_kernel<__nv_bfloat16><<<n, 256, 0, st>>>(sum, rows, count, n, D, n_out_rows,
+                                                          static_cast<__nv_bfloat16*>(out), err);
+  else
+    scatter_rows_kernel<float><<<n, 256, 0, st>>>(sum, rows, count, n, D, n_out_rows,
+                                                  static_cast<float*>(out), err);
+  return launched();
+}
+
+}  // namespace sf

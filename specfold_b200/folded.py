@@ -24,6 +24,7 @@ Standalone (tests, benchmarks) they need only ``model_executor.model``.
 
 from __future__ import annotations
 
+import ctypes
 import logging
 from typing import Dict, List, Optional, Tuple
 
@@ -111,22 +112,87 @@ class FoldedVerifyB200:
                    "pack weight tiles")
         return out
 
+    # -------------------------------------------------------------- tensor parallel
+    # rank, size and the library's communicator of the 14B configuration; size 1 = off
+    _tp = (0, 1, None)
+
+    def set_tensor_parallel(self, rank: int, size: int) -> None:
+        """Shard every layer over `size` ranks (attention heads and the intermediate
+        dimension) and all-reduce o_proj and down over NCCL.  Collective over the default
+        torch.distributed group: rank 0 creates the communicator id and broadcasts it."""
+        import torch.distributed as dist
+        lib = _lib.load()
+        if size <= 1:
+            self._tp = (0, 1, None)
+            return
+        uid = (ctypes.c_char * 128)()
+        if rank == 0:
+            _lib.check(lib.sf_tp_unique_id(ctypes.cast(uid, ctypes.c_void_p), 128), "tp id")
+        box = [bytes(uid) if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ctypes.memmove(uid, box[0], 128)
+        comm = ctypes.c_void_p()
+        _lib.check(lib.sf_tp_comm_init(ctypes.cast(uid, ctypes.c_void_p), size, rank,
+                                       ctypes.byref(comm)), "tp communicator")
+        self._tp = (rank, size, comm.value)
+        self._packed_weights = None
+        self.__dict__.pop("_statics", None)
+
+    def close_tensor_parallel(self) -> None:
+        """Release the captured graphs (they hold NCCL calls), then the communicator."""
+        lib = _lib.load()
+        lib.sf_release_graphs()
+        self.__dict__.pop("_statics", None)
+        if self._tp[2] is not None:
+            _lib.check(lib.sf_tp_comm_destroy(self._tp[2]), "tp communicator")
+        self._tp = (0, 1, None)
+
+    @staticmethod
+    def tp_shard(q_w, k_w, v_w, q_b, k_b, v_b, o_w, g_w, u_w, d_w, heads, kv_heads, rank, size):
+        """This rank's shard of one layer: q heads [r*H/s, (r+1)*H/s) with their kv heads
+        (GQA groups stay whole), o_proj's matching input columns, and rows / columns
+        [r*I/s, (r+1)*I/s) of gate+up / down.  Returns (w_qkv, b_qkv, w_o, w_g, w_u, w_d)."""
+        hd = q_w.shape[0] // heads
+        if heads % size or kv_heads % size or g_w.shape[0] % size:
+            raise ValueError(f"heads {heads} / kv heads {kv_heads} / intermediate "
+                             f"{g_w.shape[0]} not divisible by {size} ranks")
+        hq, hk, inter = heads // size, kv_heads // size, g_w.shape[0] // size
+        qs = slice(rank * hq * hd, (rank + 1) * hq * hd)
+        ks = slice(rank * hk * hd, (rank + 1) * hk * hd)
+        isl = slice(rank * inter, (rank + 1) * inter)
+        w_qkv = torch.cat([q_w[qs], k_w[ks], v_w[ks]], 0).contiguous()
+        b_qkv = None if q_b is None else torch.cat([q_b[qs], k_b[ks], v_b[ks]], 0).contiguous()
+        return (w_qkv, b_qkv, o_w[:, qs].contiguous(), g_w[isl].contiguous(),
+                u_w[isl].contiguous(), d_w[:, isl].contiguous())
+
     def _pack_layer_weights(self, layers) -> None:
         """Per layer: [Wq; Wk; Wv] and its bias packed once (one weight stream for the
         QKV projection, fastdllm_v2_folded.py:77-87).  For bf16 models every projection is
         also laid out in 128x64 tiles for the tensor-core GEMM, gate and up interleaved
-        per tile (the reference's [Wg; Wu] packing, done tile by tile)."""
+        per tile (the reference's [Wg; Wu] packing, done tile by tile).  Under tensor
+        parallelism each rank packs its shard (tp_shard)."""
         packed = []
+        tp_rank, tp_size, _ = self._tp
+        cfg = self.model_executor.model.config
         for lyr in layers:
             a, mlp = lyr.self_attn, lyr.mlp
-            w_qkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous()
-            if a.q_proj.bias is not None:
-                b_qkv = torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0).contiguous()
+            if tp_size > 1:
+                bq = a.q_proj.bias
+                w_qkv, b_qkv, w_o, w_g, w_u, w_d = self.tp_shard(
+                    a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, bq,
+                    None if bq is None else a.k_proj.bias, None if bq is None else a.v_proj.bias,
+                    a.o_proj.weight, mlp.gate_proj.weight, mlp.up_proj.weight,
+                    mlp.down_proj.weight, cfg.num_attention_heads, cfg.num_key_value_heads,
+                    tp_rank, tp_size)
             else:
-                b_qkv = None   # NLD: no bias (nld_folded.py:92-102 packs zeros)
-            w_o = a.o_proj.weight.contiguous()
-            w_g, w_u = mlp.gate_proj.weight.contiguous(), mlp.up_proj.weight.contiguous()
-            w_d = mlp.down_proj.weight.contiguous()
+                w_qkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous()
+                if a.q_proj.bias is not None:
+                    b_qkv = torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0).contiguous()
+                else:
+                    b_qkv = None   # NLD: no bias (nld_folded.py:92-102 packs zeros)
+                w_o = a.o_proj.weight.contiguous()
+                w_g, w_u = mlp.gate_proj.weight.contiguous(), mlp.up_proj.weight.contiguous()
+                w_d = mlp.down_proj.weight.contiguous()
             if self._use_tiles(w_qkv):
                 w_qkv, w_o, w_g, w_u, w_d = (self._tiles(w_qkv), self._tiles(w_o),
                                              self._tiles(w_g, w_u), None, self._tiles(w_d))
@@ -225,27 +291,31 @@ class FoldedVerifyB200:
         L = len(layers)
         B1, N = batched_input.shape
         BN = B1 * N
-        H, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        tp_rank, tp_size, tp_comm = self._tp
+        H, Hkv = cfg.num_attention_heads // tp_size, cfg.num_key_value_heads // tp_size
         hd = layers[0].self_attn.head_dim
         kv, keep, kv_stride = [], [], 0
         if P > 0:
             for li in range(L):
                 k, v = past_key_values[li]
                 k0, v0 = self._prefix_view(k), self._prefix_view(v)
+                if tp_size > 1 and k0.shape[0] == Hkv * tp_size:   # this rank's kv heads
+                    k0, v0 = k0[tp_rank * Hkv:(tp_rank + 1) * Hkv], v0[tp_rank * Hkv:(tp_rank + 1) * Hkv]
                 if kv_stride == 0:
                     kv_stride = k0.stride(0)
                 if k0.stride(0) != kv_stride or v0.stride(0) != kv_stride:
                     raise ValueError("prefix cache layers must share one head stride")
                 keep += [k0, v0]
                 kv.append((k0.data_ptr(), v0.data_ptr()))
-        key = (dev.index, dtype, B1, N, P, bucket, bool(self.record_masks), kv_stride, tuple(kv))
+        key = (dev.index, dtype, B1, N, P, bucket, bool(self.record_masks), kv_stride, tuple(kv),
+               tp_size, tp_comm)
         statics = self.__dict__.setdefault("_statics", {})
         st = statics.get(key)
         if st is not None:
             return st
 
         D = layers[0].self_attn.q_proj.weight.shape[1]
-        I = layers[0].mlp.gate_proj.weight.shape[0]
+        I = layers[0].mlp.gate_proj.weight.shape[0] // tp_size
         V = self._head().weight.shape[0]
         scale = float(layers[0].self_attn.scaling)
         probe = torch.zeros(1, N, D, dtype=dtype, device=dev)
@@ -301,6 +371,8 @@ class FoldedVerifyB200:
         args.ws = st["ws"].data_ptr()
         args.ws_bytes = st["ws"].numel()
         args.err = slab[L + L * B1:].data_ptr()
+        args.tp_comm = tp_comm
+        args.tp_size = tp_size
         st["layer_arr"] = layer_arr
         st["args"] = args
         if len(statics) >= 4:
