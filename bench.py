@@ -390,6 +390,80 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_tp(args):
+    """The 14B configuration (SURVEY config C4): a Llama-style 14B-shape model, tensor
+    parallel over all torchrun ranks (heads and the intermediate dimension sharded, o_proj
+    and down all-reduced over NVLink), one verify stream, prefix 2048.  Strong scaling:
+    the whole group serves one stream; value = verify steps/s of that stream."""
+    from specfold_b200 import SpecFoldB200NLDGeneration, _lib
+    from specfold_b200 import synthetic as syn
+    import datetime
+    import torch.distributed as dist
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.check(_lib.load().sf_check_device(), "device")
+    dims = syn.SHAPES["llama14b"]
+    P = 2048
+    model = syn.build_model(dims, family="nld", dtype=torch.bfloat16, seed=0, device=str(dev))
+    cache = syn.random_prefix_cache(dims, P, dtype=torch.bfloat16, seed=1, device=str(dev))
+    hidden = syn.config0_hidden(dims, B1, N, dtype=torch.bfloat16, seed=3,
+                                frac_recompute=FRAC_RECOMPUTE)
+    syn.inject_hidden(model, hidden.to(dev))
+    gen = SpecFoldB200NLDGeneration(model_executor=syn.StandinExecutor(model), delta=DELTA)
+    if ws > 1:
+        gen.set_tensor_parallel(rank, ws)
+    ids = torch.zeros(B1, N, dtype=torch.int64, device=dev)
+    for _ in range(args.warmup):
+        gen._batched_block_forward(ids, cache)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(args.steps):
+            gen._batched_block_forward(ids, cache)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+    ms = max_over_ranks([t0.elapsed_time(t1)], dev)[0]
+    step_ms = ms / args.steps
+    hbm, _, src = peaks()
+    wbytes, kvbytes = algorithmic_bytes(dims, P)
+    # per GPU: its shard of the layers + the replicated LM head + its kv heads
+    head = 2 * dims.vocab * dims.hidden
+    per_gpu = (wbytes - head) / ws + head + kvbytes / ws
+    line = {
+        "metric": "folded verify-step, 14B Llama shape, tensor parallel", "value": round(args.steps / (ms / 1e3), 4),
+        "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init 14B shape)",
+        "config": {"workload": "folded verify step, Llama-style 14B shape, B1=8, N=32, prefix 2048, "
+                               "delta 0.1", "shape": "llama14b", "prefix": P,
+                   "parallelism": f"tp{ws} (heads / intermediate sharded; NCCL fp32 all-reduce "
+                                  "after o_proj and down)",
+                   "fold_ratio": round(gen.fold_ratio, 4)},
+        "roofline": {"bound": "hbm", "per_gpu_bytes": int(per_gpu),
+                     "achieved": round(per_gpu / (step_ms / 1e3) / 1e9, 1), "peak": hbm,
+                     "unit": "GB/s", "peak_source": src,
+                     "frac": round(per_gpu / (step_ms / 1e3) / 1e9 / hbm, 4)},
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        gen.close_tensor_parallel()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -398,10 +472,14 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="the 14B tensor-parallel configuration over all ranks instead")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.tp and args.impl == "b200":
+        run_tp(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)
