@@ -16,6 +16,7 @@
 // All mbarrier waits are bounded (sf_common.cuh).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "sf_kernels.cuh"
@@ -448,6 +449,15 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
   return cudaSuccess;
 }
 
+// SF_ROWS_MMA=0: the SIMT rows kernel instead of the tensor-core one (read once)
+static bool rows_mma_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SF_ROWS_MMA");
+    return v == nullptr || atoi(v) != 0;
+  }();
+  return on;
+}
+
 static bool prefix_on_tc(int dtype, const AttnParams& p) {
   return dtype == BF16 && p.P > 0 && p.pk != nullptr;
 }
@@ -472,6 +482,8 @@ cudaError_t launch_attention_rows(int dtype, const AttnParams& p, cudaStream_t s
   PrefixPartials pp{};
   cudaError_t e = prefix_partials_hd(p, st, &pp, true);
   if (e != cudaSuccess) return e;
+  if (attention_rows_mma_ok(dtype, p, pp.splits) && rows_mma_enabled())
+    return launch_attention_rows_mma(p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
   return launch_attention_rows_partials(BF16, p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
 }
 

@@ -264,6 +264,11 @@ cudaError_t launch_attention_rows(int dtype, const AttnParams& p, cudaStream_t s
 cudaError_t launch_attention_rows_partials(int dtype, const AttnParams& p, const float* part_O,
                                            const float* part_ml, int splits, int q_rows,
                                            cudaStream_t st);
+// the same on the tensor cores (mma.sync block of <= 32 keys): bf16, hd 64 / 128, N <= 32
+bool attention_rows_mma_ok(int dtype, const AttnParams& p, int splits);
+cudaError_t launch_attention_rows_mma(const AttnParams& p, const float* part_O,
+                                      const float* part_ml, int splits, int part_rows,
+                                      cudaStream_t st);
 
 struct MergeParams {
   const void* q_buf;
