@@ -261,18 +261,25 @@ def run_b200(args):
 
     hbm, tflops, src = peaks()
     wbytes, kvbytes = algorithmic_bytes(dims, P_PREFIX)
-    # dominant kernel: the chained FFN (post-attention norm + gate/up + down: 3 x I x D bf16
-    # weights per layer, one launch per layer), or gate/up alone when not chained
+    # dominant kernel: the chained layer tail, one launch per layer -- o_proj + residual
+    # (split-K reduction fused into the norm), post-attention RMSNorm, gate/up + SwiGLU,
+    # down (SF_CHAIN=2, the default: (H*hd + 3*I) x D bf16 weights), or the FFN alone
+    # (SF_CHAIN=1: 3 x I x D), or gate/up alone when not chained
     if prof.get("ffn", (0.0, 0))[1]:
-        dom, dom_name = "ffn", "ffn chain (RMSNorm + tcgen05 gate/up + SwiGLU + down, one launch)"
         gu_bytes = 3 * 2 * dims.inter * dims.hidden
+        if int(os.environ.get("SF_CHAIN", "2")) >= 2:
+            dom, dom_name = "ffn", ("layer tail chain (tcgen05 o_proj + residual, RMSNorm, "
+                                    "gate/up + SwiGLU, down; one launch)")
+            gu_bytes += 2 * dims.heads * dims.head_dim * dims.hidden
+        else:
+            dom, dom_name = "ffn", "ffn chain (RMSNorm + tcgen05 gate/up + SwiGLU + down, one launch)"
     else:
         dom, dom_name = "gate_up", "gate_up (tcgen05 swap-AB GEMM + SwiGLU)"
         gu_bytes = 2 * 2 * dims.inter * dims.hidden
     gu_ms, gu_calls = prof.get(dom, (0.0, 0))
     gu_avg_s = gu_ms / max(gu_calls, 1) / 1e3
     achieved = gu_bytes / gu_avg_s / 1e9 if gu_avg_s > 0 else 0.0
-    traffic = profiled_traffic(dom)
+    traffic = profiled_traffic("layer_tail" if "layer tail" in dom_name else dom)
     step_achieved = (wbytes + kvbytes) / (step_ms / 1e3) / 1e9
     clocks = clk.summary()
     kernels = {k: {"ms_per_step": round(v[0] / args.steps, 4), "calls_per_step": v[1] / args.steps}

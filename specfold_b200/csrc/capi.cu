@@ -898,6 +898,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
       pre.n_src = BN;
       pre.D = D;
       pre.eps = a->eps;
+      pre.rec = rec;   // the o_proj split reduction happens in the norm (gemm_chain)
       if (chain_level() >= 2) {
         // o_proj + residual, then the norm, gate/up and down: one launch
         const GemmArgs chain[3] = {o, gu, dn};

@@ -75,6 +75,7 @@ struct TcParams {
   int splits, kb_total, kb_per_split, n_units;
   int w_tiled;         // weights in the [tile][kb][128][64] layout
   int stage_budget;    // shared-memory bytes for the pipeline stages
+  int defer_reduce;    // split phase whose reduction the next phase's norm performs
   WPrefetch next_pf;   // the next GEMM's first weight blocks, pulled into L2 by the
                        // producer once it has issued its own last load
   float* partial;      // [splits][rows_cap][n_out] when splits > 1
@@ -317,6 +318,7 @@ struct PreNorm {           // out[i] = T(w * T(x[rows[i]] * rstd)), i < min(*cou
   int64_t n_src;
   int D;
   float eps;
+  const int8_t* rec;               // recompute flags (deferred reduction only)
 };
 
 struct ChainParams {
@@ -397,23 +399,23 @@ __device__ __forceinline__ void epi_unit(const TcParams& p, const EpiCtx& x, int
                             static_cast<uint32_t>(buf * x.buf_cols + t * x.acc_cols + c0);
         tmem_ld16(ta, v);
         tmem_ld_wait();
+        const int nr = min(kChunk, prows - c0);
+        if (p.splits > 1) {
+          // fp32 partial of this split, row-major, straight from the registers: lane l
+          // holds feature f(l) of rows c0.., so each row is one 128-byte store per warp
+          const int f = tc_feature(p, tile, x.l);
+          if (f >= 0) {
+            float* part = p.partial + (static_cast<int64_t>(split) * p.rows_cap + prow0 + c0) * p.n_out + f;
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i)
+              if (i < nr) __stcg(part + static_cast<int64_t>(i) * p.n_out, v[i]);
+          }
+          continue;
+        }
 #pragma unroll
         for (int i = 0; i < kChunk; ++i) x.tileT[i * kTileLd + x.l] = v[i];
         epi_sync_half(x.h);
-        const int nr = min(kChunk, prows - c0);
-        if (p.splits > 1) {
-          // fp32 partial of this split, row-major, 16-byte stores
-          float* part = p.partial + (static_cast<int64_t>(split) * p.rows_cap + prow0 + c0) * p.n_out;
-#pragma unroll
-          for (int k = 0; k < kChunk * 32 / 128; ++k) {
-            const int item = x.eh + 128 * k;
-            const int r = item >> 5, l0 = (item & 31) * 4;
-            const int f0 = tc_feature(p, tile, l0);
-            if (r < nr && f0 >= 0)
-              *reinterpret_cast<float4*>(part + static_cast<int64_t>(r) * p.n_out + f0) =
-                  *reinterpret_cast<const float4*>(x.tileT + r * kTileLd + l0);
-          }
-        } else {
+        {
 #pragma unroll
           for (int k = 0; k < kChunk * kGroupsOut<KIND> / 128; ++k) {
             const int item = x.eh + 128 * k;
@@ -435,7 +437,7 @@ __device__ __forceinline__ void epi_unit(const TcParams& p, const EpiCtx& x, int
     tc_fence_before();
     if (lane == 0) mbar_arrive(&acc_empty[buf]);
   }
-  if (p.splits > 1) {
+  if (p.splits > 1 && !p.defer_reduce) {
     // every split of this tile group publishes, then each reduces its slice of rows
     __threadfence();
     bool go = epi_vote_all(!*x.abort_flag);
@@ -526,6 +528,91 @@ __device__ __forceinline__ void pre_norm_rows(const PreNorm& pr, int et, float* 
         for (int k = 0; k < V; ++k) a[u][k] = g[u][k] * Elt<T>::rnd(a[u][k] * rs);
         if (okrow) store_vec<T>(out + d, a[u]);
       }
+    }
+  }
+}
+
+// The split reduction of a residual GEMM (EPI_RESID, partials of every row) fused with the
+// RMSNorm that reads it: for the recomputed rows r = rows[i], i < min(*count, n),
+//   x[r]   = T(resid[r] + T(sum_s partial[s][r]))   (the EPI_RESID arithmetic, split order)
+//   out[i] = T(w * T(x[r] * rstd))                  (the pre_norm_rows arithmetic)
+// from the same registers: one pass over the partials instead of a reduction, a device
+// counter hop and a re-read.
+__device__ __forceinline__ void pre_resid_norm_rows(const PreNorm& pr, const TcParams& g, int et,
+                                                    float* red, int* err) {
+  using T = __nv_bfloat16;
+  constexpr int V = 8, MAXV = 4;
+  int n = pr.n;
+  if (pr.count) n = min(n, *pr.count);
+  const int64_t split_stride = static_cast<int64_t>(g.rows_cap) * g.n_out;
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int64_t row = pr.rows[i];
+    const bool okrow = row >= 0 && row < pr.n_src && row < g.rows_cap;
+    if (!okrow && et == 0) flag_error(err, SF_DEV_ERR_INDEX);
+    const int64_t r = okrow ? row : 0;
+    const T* w = reinterpret_cast<const T*>(pr.w);
+    float a[MAXV][V];
+    uint4 gw[MAXV];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < MAXV; ++u) {
+      const int d = (et + kEpiThreads * u) * V;
+      if (d < pr.D) {
+        float v[V] = {}, rs[V];
+        gw[u] = *reinterpret_cast<const uint4*>(w + d);
+        sum_splits8(g.partial, g.splits, split_stride, r * g.n_out + d, v);
+        ld8<T>(g.epi.resid, r * g.epi.ld_out + d, rs);
+#pragma unroll
+        for (int k = 0; k < V; ++k) a[u][k] = Elt<T>::rnd(__fadd_rn(rs[k], Elt<T>::rnd(v[k])));
+        if (okrow) st8<T>(g.epi.out, r * g.epi.ld_out + d, a[u]);
+#pragma unroll
+        for (int k = 0; k < V; ++k) ss = fmaf(a[u][k], a[u][k], ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if ((et & 31) == 0) red[et >> 5] = ss;
+    epi_sync_all();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < kEpiWarps; ++k) tot += red[k];
+    epi_sync_all();
+    const float rsd = 1.0f / sqrtf(tot / static_cast<float>(pr.D) + pr.eps);
+    T* out = reinterpret_cast<T*>(pr.out) + static_cast<int64_t>(i) * pr.D;
+#pragma unroll
+    for (int u = 0; u < MAXV; ++u) {
+      const int d = (et + kEpiThreads * u) * V;
+      if (d < pr.D) {
+        const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&gw[u]);
+#pragma unroll
+        for (int k = 0; k < V / 2; ++k) {
+          const float2 wf = __bfloat1622float2(wp[k]);
+          a[u][2 * k] = wf.x * Elt<T>::rnd(a[u][2 * k] * rsd);
+          a[u][2 * k + 1] = wf.y * Elt<T>::rnd(a[u][2 * k + 1] * rsd);
+        }
+        if (okrow) store_vec<T>(out + d, a[u]);
+      }
+    }
+  }
+}
+
+// The rest of that residual GEMM's output: x[r] for the rows the norm did not reduce (not
+// flagged for recompute; every row when the compaction overflowed its bucket).  Runs after
+// the norm has released the next phase.
+__device__ __forceinline__ void resid_rows_rest(const PreNorm& pr, const TcParams& g, int et) {
+  using T = __nv_bfloat16;
+  const bool all = pr.count != nullptr && *pr.count > pr.n;
+  const int64_t split_stride = static_cast<int64_t>(g.rows_cap) * g.n_out;
+  const int groups = g.n_out / 8;
+  for (int r = blockIdx.x; r < g.rows_cap; r += gridDim.x) {
+    if (!all && r < pr.n_src && pr.rec[r] != 0) continue;   // uniform over the CTA
+    for (int q = et; q < groups; q += kEpiThreads) {
+      const int d = q * 8;
+      float v[8] = {}, rs[8], o[8];
+      sum_splits8(g.partial, g.splits, split_stride, static_cast<int64_t>(r) * g.n_out + d, v);
+      ld8<T>(g.epi.resid, static_cast<int64_t>(r) * g.epi.ld_out + d, rs);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = __fadd_rn(rs[k], Elt<T>::rnd(v[k]));
+      st8<T>(g.epi.out, static_cast<int64_t>(r) * g.epi.ld_out + d, o);
     }
   }
 }
@@ -778,13 +865,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = wait_counter(c.dep + 2 * (k - 1) + 1, static_cast<unsigned>(c.ph[k - 1].n_units), c.err);
           if (!epi_vote_all(ok && !*abort_flag)) *abort_flag = 1;
         }
-        if (!*abort_flag) pre_norm_rows(c.norm[k], x.et, red, c.err);
+        const bool fused = k > 0 && c.ph[k - 1].defer_reduce;
+        if (!*abort_flag) {
+          if (fused) pre_resid_norm_rows(c.norm[k], c.ph[k - 1], x.et, red, c.err);
+          else pre_norm_rows(c.norm[k], x.et, red, c.err);
+        }
         epi_sync_all();
         if (x.et == 0) {
           __threadfence();
           fence_proxy_async_global();
           atomicAdd(c.dep + 2 * k, 1u);
         }
+        // the residual rows no later phase reads, while phase k streams its weights
+        if (fused && !*abort_flag) resid_rows_rest(c.norm[k], c.ph[k - 1], x.et);
       }
       // this CTA's units of phase k: u = blockIdx.x + j * gridDim.x in the phase's range
       const int base = c.unit_base[k];
@@ -981,6 +1074,7 @@ static cudaError_t make_phase(const GemmArgs& a, int* counters, TcParams* out, T
   p.w_tiled = a.w_tiled ? 1 : 0;
   p.stage_budget = pl.stage_budget;
   p.next_pf = a.next_pf;
+
   if (pl.splits > 1) {
     const size_t need = kGemmCounterBytes + static_cast<size_t>(pl.splits) * a.rows_cap * a.n_out * 4;
     if (a.ws == nullptr || a.ws_bytes < need) return cudaErrorInvalidValue;
@@ -1044,6 +1138,7 @@ static void set_norm(PreNorm* d, const PreNormArgs* s) {
   d->n_src = s->n_src;
   d->D = s->D;
   d->eps = s->eps;
+  d->rec = s->rec;
 }
 
 cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms, unsigned* dep,
@@ -1069,6 +1164,15 @@ cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms
       set_norm(&c.norm[k], norms[k]);
     }
   }
+  // a split-K residual GEMM over every row followed by the norm of its output: the norm
+  // performs the split reduction (pre_resid_norm_rows / resid_rows_rest)
+  static const bool defer_on = getenv("SF_DEFER") == nullptr || atoi(getenv("SF_DEFER")) != 0;
+  for (int k = 1; k < n; ++k)
+    if (defer_on && norms != nullptr && norms[k] != nullptr && norms[k]->rec != nullptr && norms[k]->rows != nullptr &&
+        g[k - 1].epi.kind == EPI_RESID && pl[k - 1].splits > 1 && g[k - 1].count == nullptr &&
+        norms[k]->x == g[k - 1].epi.out && g[k - 1].epi.ld_out == g[k - 1].n_out &&
+        norms[k]->D == g[k - 1].n_out && g[k - 1].n_out % 8 == 0)
+      c.ph[k - 1].defer_reduce = 1;
   for (int k = n; k < kMaxPhases; ++k) tm[k][0] = tm[k][1] = tm[k][2] = tm[k][3] = tm[0][0];
   if (counters - static_cast<int*>(g[0].ws) > kMaxCounterTiles * 2) return cudaErrorInvalidValue;
   c.n_phases = n;
@@ -1088,6 +1192,7 @@ cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms
     if (pl[k].splits > 1 && c.ph[k].n_units > grid) return cudaErrorInvalidValue;
   c.stage_budget = pl[0].stage_budget;
   c.ctas_per_sm = pl[0].ctas_per_sm;
+
   c.err = g[0].err;
   c.dep = dep;
 

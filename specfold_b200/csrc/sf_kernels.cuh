@@ -204,6 +204,11 @@ struct PreNormArgs {
   int64_t n_src;
   int D;
   float eps;
+  // optional: the recompute flag per source row (rows[] lists the flagged ones).  With it,
+  // when x is the output of a split-K residual GEMM (EPI_RESID, all rows) that precedes
+  // the norm in the chain, that GEMM leaves its split reduction to the norm: flagged rows
+  // are reduced, stored and normalised in one pass, the others stored after the norm.
+  const int8_t* rec;
 };
 // Up to three bf16 GEMMs in one persistent launch, each reading the previous one's
 // output (g[k].X == what g[k-1]'s epilogue writes, or what norms[k] writes from it);
