@@ -186,6 +186,10 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   g = std::max(g, ws_gemm(dtype, bucket, 2 * I, D, EPI_SWIGLU, I));
   g = std::max(g, ws_gemm(dtype, bucket, D, I, EPI_SCATTER, 0));
   g = std::max(g, ws_gemm(dtype, BN, V, D, EPI_LOGITS, 0));
+  // the chained o_proj's partials live beside the later phases' (its split reduction is
+  // deferred to the post-attention norm)
+  const size_t o_ws = ws_gemm(dtype, BN, D, qd, EPI_RESID, 0);
+  if (o_ws > kGemmCounterBytes) g += o_ws - kGemmCounterBytes;
   b.gemm_ws_bytes = g;
   b.gemm_ws = c.take(g + 256);
   // tensor-core attention: query copy per kv head + split-KV partials

@@ -76,6 +76,7 @@ struct TcParams {
   int w_tiled;         // weights in the [tile][kb][128][64] layout
   int stage_budget;    // shared-memory bytes for the pipeline stages
   int defer_reduce;    // split phase whose reduction the next phase's norm performs
+  int no_dep;          // phase k > 0 that does not read phase k-1's output
   WPrefetch next_pf;   // the next GEMM's first weight blocks, pulled into L2 by the
                        // producer once it has issued its own last load
   float* partial;      // [splits][rows_cap][n_out] when splits > 1
@@ -341,7 +342,7 @@ __device__ __forceinline__ const unsigned* phase_dep(const ChainParams& c, int k
     *target = gridDim.x;
     return c.dep + 2 * k;
   }
-  if (k > 0) {
+  if (k > 0 && !c.ph[k].no_dep) {
     *target = static_cast<unsigned>(c.ph[k - 1].n_units);
     return c.dep + 2 * (k - 1) + 1;
   }
@@ -892,7 +893,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           epi_unit<K1>(c.ph[1], x, lu, rows_ph[1], acc_it, double_buf, acc_full, acc_empty);
         else
           epi_unit<K2>(c.ph[2], x, lu, rows_ph[2], acc_it, double_buf, acc_full, acc_empty);
-        if (k + 1 < c.n_phases) {
+        if (k + 1 < c.n_phases && !c.ph[k + 1].no_dep) {
           // this unit's output is the next phase's input
           epi_sync_all();
           if (x.et == 0) {
@@ -1039,10 +1040,17 @@ WPrefetch gemm_prefetch_plan(const GemmArgs& a) {
   return f;
 }
 
+static int wave_tail_tiles0(int n_out, int K, int kind, int rows_cap, int* splits1);
+
 size_t gemm_tc_ws_need(int rows_cap, int n_out, int K, int kind, int inter) {
   const int mode = kind == EPI_SWIGLU ? 1 : 0;
   const TcPlan pl = tc_plan(n_out, K, mode, inter, rows_cap);
-  if (pl.splits <= 1) return 0;
+  if (pl.splits <= 1) {
+    int s1 = 0;
+    const int tiles0 = wave_tail_tiles0(n_out, K, kind, rows_cap, &s1);
+    if (tiles0 <= 0) return 0;
+    return kGemmCounterBytes + static_cast<size_t>(s1) * rows_cap * (n_out - tiles0 * kTileF) * 4;
+  }
   return kGemmCounterBytes + static_cast<size_t>(pl.splits) * rows_cap * n_out * 4;
 }
 
@@ -1118,6 +1126,10 @@ static ChainFn chain_kernel(int n, const int* k) {
     }
   }
   // the FFN (gate/up -> down), and o_proj -> norm -> FFN
+  // a long GEMM and its wave tail (independent phases of one epilogue kind)
+  if (n == 2 && k[0] == k[1] && (k[0] == EPI_LOGITS || k[0] == EPI_RAW))
+    return k[0] == EPI_LOGITS ? tc_chain_kernel<EPI_LOGITS, EPI_LOGITS, EPI_LOGITS>
+                              : tc_chain_kernel<EPI_RAW, EPI_RAW, EPI_RAW>;
   if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_SCATTER)
     return tc_chain_kernel<EPI_SWIGLU, EPI_SCATTER, EPI_SCATTER>;
   // tensor parallel: the down projection's fp32 partial sums go to the all-reduce
@@ -1141,22 +1153,30 @@ static void set_norm(PreNorm* d, const PreNormArgs* s) {
   d->rec = s->rec;
 }
 
-cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms, unsigned* dep,
-                       cudaStream_t st) {
+// indep: bit k set -> phase k does not read phase k-1's output (no counter wait)
+static cudaError_t chain_launch(const GemmArgs* g, int n, const PreNormArgs* const* norms,
+                                unsigned* dep, cudaStream_t st, unsigned indep) {
   if (n < 1 || n > kMaxPhases) return cudaErrorInvalidValue;
-  bool any_norm = false;
-  for (int k = 0; k < n; ++k) any_norm = any_norm || (norms != nullptr && norms[k] != nullptr);
-  if ((n > 1 || any_norm) && dep == nullptr) return cudaErrorInvalidValue;
+  bool any_norm = false, any_dep = false;
+  for (int k = 0; k < n; ++k) {
+    any_norm = any_norm || (norms != nullptr && norms[k] != nullptr);
+    any_dep = any_dep || (k > 0 && !((indep >> k) & 1u));
+    if (k > 0 && ((indep >> k) & 1u) && norms != nullptr && norms[k] != nullptr)
+      return cudaErrorInvalidValue;
+  }
+  if ((any_dep || any_norm) && dep == nullptr) return cudaErrorInvalidValue;
   ChainParams c{};
   CUtensorMap tm[kMaxPhases][4];
   TcPlan pl[kMaxPhases];
   int kinds[kMaxPhases];
   int* counters = static_cast<int*>(g[0].ws);
   for (int k = 0; k < n; ++k) {
-    if (k > 0 && !g[k].w_tiled) return cudaErrorInvalidValue;   // untiled SwiGLU: phase 0 only
+    // untiled SwiGLU reads its up half through phase 0's second weight map: phase 0 only
+    if (k > 0 && !g[k].w_tiled && g[k].epi.kind == EPI_SWIGLU) return cudaErrorInvalidValue;
     cudaError_t e = make_phase(g[k], counters, &c.ph[k], &pl[k], &tm[k][0], &tm[k][1], &tm[k][2],
                                &tm[k][3]);
     if (e != cudaSuccess) return e;
+    c.ph[k].no_dep = (k > 0 && ((indep >> k) & 1u)) ? 1 : 0;
     if (pl[k].splits > 1) counters += 2 * pl[k].n_groups;   // each split phase its own counters
     kinds[k] = g[k].epi.kind;
     if (norms != nullptr && norms[k] != nullptr) {
@@ -1171,8 +1191,19 @@ cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms
     if (defer_on && norms != nullptr && norms[k] != nullptr && norms[k]->rec != nullptr && norms[k]->rows != nullptr &&
         g[k - 1].epi.kind == EPI_RESID && pl[k - 1].splits > 1 && g[k - 1].count == nullptr &&
         norms[k]->x == g[k - 1].epi.out && g[k - 1].epi.ld_out == g[k - 1].n_out &&
-        norms[k]->D == g[k - 1].n_out && g[k - 1].n_out % 8 == 0)
+        norms[k]->D == g[k - 1].n_out && g[k - 1].n_out % 8 == 0) {
+      // the deferred partials are read after the norm has released phase k, while later
+      // split phases write theirs: they get a region of their own, after the largest of
+      // the other split phases' (which run one after another and share theirs)
+      size_t other = 0;
+      for (int j = 0; j < n; ++j)
+        if (j != k - 1 && pl[j].splits > 1)
+          other = std::max(other, static_cast<size_t>(pl[j].splits) * g[j].rows_cap * g[j].n_out * 4);
+      const size_t mine = static_cast<size_t>(pl[k - 1].splits) * g[k - 1].rows_cap * g[k - 1].n_out * 4;
+      if (g[k - 1].ws == nullptr || kGemmCounterBytes + other + mine > g[k - 1].ws_bytes) continue;
+      c.ph[k - 1].partial = reinterpret_cast<float*>(static_cast<char*>(g[k - 1].ws) + kGemmCounterBytes + other);
       c.ph[k - 1].defer_reduce = 1;
+    }
   for (int k = n; k < kMaxPhases; ++k) tm[k][0] = tm[k][1] = tm[k][2] = tm[k][3] = tm[0][0];
   if (counters - static_cast<int*>(g[0].ws) > kMaxCounterTiles * 2) return cudaErrorInvalidValue;
   c.n_phases = n;
@@ -1222,8 +1253,58 @@ cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms
   return launched();
 }
 
+cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms, unsigned* dep,
+                       cudaStream_t st) {
+  return chain_launch(g, n, norms, dep, st, 0u);
+}
+
+// Wave tail of a long unsplit GEMM (the lm_head: 594 two-tile units on 148 CTAs leave a
+// fifth round of 2 units, a whole unit's time with the GPU nearly idle): when the last
+// round is at most a quarter full, its tiles become a second, independent phase of the
+// same launch, split over K across the CTAs that would otherwise idle.  Same MMAs per
+// tile; only the unit boundaries move (the split sums add in split order).
+// tiles of the full rounds (0: no tail split) and the tail phase's split count
+static int wave_tail_tiles0(int n_out, int K, int kind, int rows_cap, int* splits1) {
+  if ((kind != EPI_LOGITS && kind != EPI_RAW) || rows_cap > kMaxPassRows) return 0;
+  const TcPlan pl = tc_plan(n_out, K, 0, 0, rows_cap);
+  if (pl.splits > 1) return 0;
+  const int n_units = pl.n_groups * pl.splits;
+  const int rem = n_units % pl.grid;
+  if (rem == 0 || rem * 4 > pl.grid) return 0;
+  const int tiles0 = (n_units - rem) * pl.sub;
+  const TcPlan p1 = tc_plan(n_out - tiles0 * kTileF, K, 0, 0, rows_cap);
+  if (p1.splits <= 1 || p1.n_groups * p1.splits > pl.grid) return 0;
+  *splits1 = p1.splits;
+  return tiles0;
+}
+
+static bool split_wave_tail(const GemmArgs& a, GemmArgs* g) {
+  if (a.dtype != BF16) return false;
+  int s1 = 0;
+  const int tiles0 = wave_tail_tiles0(a.n_out, a.K, a.epi.kind, a.rows_cap, &s1);
+  if (tiles0 <= 0) return false;
+  const TcPlan pl = tc_plan(a.n_out, a.K, 0, 0, a.rows_cap);
+  const int n1 = a.n_out - tiles0 * kTileF;
+  const size_t need = kGemmCounterBytes + static_cast<size_t>(s1) * a.rows_cap * n1 * 4;
+  if (a.ws == nullptr || a.ws_bytes < need) return false;
+  g[0] = a;
+  g[0].n_out = tiles0 * kTileF;
+  g[1] = a;
+  g[1].n_out = n1;
+  const size_t w_off = a.w_tiled ? static_cast<size_t>(tiles0) * pl.kb_total * kWBytes
+                                 : static_cast<size_t>(tiles0) * kTileF * a.K * 2;
+  g[1].W = static_cast<const char*>(a.W) + w_off;
+  const size_t esz = a.epi.kind == EPI_RAW ? 4 : 2;
+  g[1].epi.out = static_cast<char*>(a.epi.out) + static_cast<size_t>(tiles0) * kTileF * esz;
+  g[0].next_pf = WPrefetch{};
+  return true;
+}
+
 cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t st) {
-  return gemm_chain(&a, 1, nullptr, nullptr, st);
+  static const bool tail_on = getenv("SF_WAVE_TAIL") == nullptr || atoi(getenv("SF_WAVE_TAIL")) != 0;
+  GemmArgs g[2];
+  if (tail_on && split_wave_tail(a, g)) return chain_launch(g, 2, nullptr, nullptr, st, 2u);
+  return chain_launch(&a, 1, nullptr, nullptr, st, 0u);
 }
 
 // ------------------------------------------------------------------ weight tiling

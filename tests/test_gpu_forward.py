@@ -94,6 +94,9 @@ EXTRA = {
     "mid_nld_bf16_chain": ("nld", ModelDims(hidden=1024, heads=8, kv_heads=4, head_dim=128,
                                             inter=2048, layers=2, vocab=512, eps=1e-5,
                                             theta=5e5), 64, "chain"),
+    # Qwen2.5's vocabulary: the tiled lm_head runs its last round's tiles as a split-K phase
+    "mid_bf16_qwen_vocab": ("fastdllm", ModelDims(hidden=512, heads=4, kv_heads=2, head_dim=128,
+                                                  inter=1408, layers=1, vocab=152064), 64, "tree"),
 }
 
 

@@ -279,6 +279,25 @@ def test_final_norm_lm_head(dtype, shift):
     assert_close(logits.cpu(), ref, dtype, "logits")
 
 
+def test_final_norm_lm_head_wave_tail():
+    """A Qwen-sized vocabulary (152064 = 1188 weight tiles): 594 two-tile units leave a
+    last round of 2 units on 148 SMs, so the library runs the last 4 tiles as a split-K
+    phase of the same launch.  Logits of every tile, the tail's included, match."""
+    dtype, B1, N, D, V, eps = torch.bfloat16, 8, 32, 1024, 152064, 1e-6
+    g = torch.Generator(device="cuda").manual_seed(11)
+    h = torch.randn(B1 * N, D, generator=g, device="cuda").to(dtype)
+    nw = (1 + 0.1 * torch.randn(D, generator=g, device="cuda")).to(dtype)
+    W = (torch.randn(V, D, generator=g, device="cuda") * 0.05).to(dtype)
+    logits, err = K.final_norm_lm_head(h, nw, W, B1, N, eps, 0)
+    torch.cuda.synchronize()
+    K.raise_device_error(err)
+    x = h.float()
+    z = (nw.float() * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)).to(dtype).float()).to(dtype)
+    ref = (z.float() @ W.float().t()).to(dtype).view(B1, N, V)
+    assert_close(logits[..., -1024:].cpu(), ref[..., -1024:].cpu(), dtype, "logits (tail tiles)")
+    assert_close(logits.cpu(), ref.cpu(), dtype, "logits")
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_kv_append(dtype):
     Hkv, cap, hd, P, n = 4, 256, 128, 100, 32
