@@ -457,23 +457,33 @@ __device__ __forceinline__ void epi_unit(const TcParams& p, const EpiCtx& x, int
     const int slice = (rows + p.splits - 1) / p.splits;
     const int r0 = split * slice, r1 = min(rows, r0 + slice);
     const int64_t split_stride = static_cast<int64_t>(p.rows_cap) * p.n_out;
-    // items: (tile t, row r, group of 8 weight rows l0 that emits output)
-    constexpr int GPR = kGroupsOut<KIND>;
+    // items: (tile t, row r, group of 8 weight rows l0 that emits output).  QKV: one item
+    // per RoPE pair (l0 in the lower half of its head), which sums both halves once and
+    // emits both -- every partial is read once
+    constexpr bool kPair = KIND == EPI_QKV;
+    constexpr int GPR = kPair ? 8 : kGroupsOut<KIND>;
     const int n_items = go ? p.sub * max(0, r1 - r0) * GPR : 0;
     for (int item = x.et; item < n_items; item += kEpiThreads) {
       const int t = item / ((r1 - r0) * GPR);
       const int rem = item - t * (r1 - r0) * GPR;
-      const int r = r0 + rem / GPR, l0 = (rem % GPR) * 8;
+      const int r = r0 + rem / GPR;
+      int l0 = (rem % GPR) * 8;
+      if (kPair) {
+        const int half = p.epi.hd >> 1;
+        l0 = (l0 / half) * p.epi.hd + l0 % half;
+      }
       const int tile = grp * p.sub + t;
       if (tile >= p.n_tiles) continue;
       const int fa = tc_feature(p, tile, l0);
       if (fa < 0) continue;
-      const int fb = tc_feature(p, tile, tc_partner_l<KIND>(p, l0));
+      const int lp = tc_partner_l<KIND>(p, l0);
+      const int fb = tc_feature(p, tile, lp);
       float va[8] = {}, vb[8] = {};
       const int64_t row_off = static_cast<int64_t>(r) * p.n_out;
       sum_splits8(p.partial, p.splits, split_stride, row_off + fa, va);
       if (fb >= 0 && fb != fa) sum_splits8(p.partial, p.splits, split_stride, row_off + fb, vb);
       epi_group8<KIND>(p, tile, r, l0, va, fb == fa ? va : vb);
+      if (kPair && fb >= 0 && fb != fa) epi_group8<KIND>(p, tile, r, lp, vb, va);
     }
     epi_sync_all();
     if (x.et == 0 && go) {
@@ -955,9 +965,11 @@ static int num_sms() {
 // Tuning, read once from the environment: SF_GEMM_SUB (weight tiles per CTA stage: 0 =
 // chosen per GEMM, or 1 / 2 / 4 wherever TMEM allows) and SF_GEMM_SMEM_KB (shared memory
 // per CTA; below ~113 two CTAs share an SM).
+constexpr int kDefaultSmemKb = 170;
+constexpr int kMaxSmemKb = 226;
 struct TcTuning {
   int sub = 0;
-  int smem_kb = 170;
+  int smem_kb = kDefaultSmemKb;
   int pf_mb = 0;       // SF_GEMM_PF_MB: L2 prefetch budget for the next GEMM's weights
                        // (off: measured, the step got slower at 40 and 80 MB)
 };
@@ -969,7 +981,7 @@ static const TcTuning& tc_tuning() {
       const int s = atoi(v);
       t.sub = (s == 1 || s == 2 || s == 4) ? s : 0;
     }
-    if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(226, atoi(v)));
+    if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(kMaxSmemKb, atoi(v)));
     if (const char* v = getenv("SF_GEMM_PF_MB")) t.pf_mb = std::max(0, std::min(96, atoi(v)));
   });
   return t;
@@ -1223,6 +1235,16 @@ static cudaError_t chain_launch(const GemmArgs* g, int n, const PreNormArgs* con
     if (pl[k].splits > 1 && c.ph[k].n_units > grid) return cudaErrorInvalidValue;
   c.stage_budget = pl[0].stage_budget;
   c.ctas_per_sm = pl[0].ctas_per_sm;
+  // the lm_head streams 256 activation rows with two weight tiles per stage (64 KB
+  // stages): at the default budget it keeps two stages in flight and waits on latency;
+  // the largest budget gives it three (measured 301 -> 275 us per step at the 7B shape;
+  // the other GEMMs measured no faster or slower with it)
+  bool all_logits = tc_tuning().smem_kb == kDefaultSmemKb;
+  for (int k = 0; k < n; ++k) all_logits = all_logits && g[k].epi.kind == EPI_LOGITS;
+  if (all_logits) {
+    c.stage_budget = kMaxSmemKb * 1024 - kSmemFixed;
+    c.ctas_per_sm = 1;
+  }
 
   c.err = g[0].err;
   c.dep = dep;
