@@ -6,5 +6,7 @@ hand-written CUDA kernels behind the C ABI in ``include/specfold_b200.h``.
 """
 
 from .folded import FoldedVerifyB200, SpecFoldB200FastDLLMV2Generation, SpecFoldB200NLDGeneration
+from .kv_cache import PreallocatedKVCache
 
-__all__ = ["FoldedVerifyB200", "SpecFoldB200FastDLLMV2Generation", "SpecFoldB200NLDGeneration"]
+__all__ = ["FoldedVerifyB200", "SpecFoldB200FastDLLMV2Generation", "SpecFoldB200NLDGeneration",
+           "PreallocatedKVCache"]

@@ -231,7 +231,19 @@ class FoldedVerifyB200:
             self._ws[key] = ws
         return ws
 
-    def _run(self, batched_input, past_key_values, bucket, count_stats=True):
+    @torch.no_grad()
+    def dense_block_forward(self, batched_input: torch.Tensor, past_key_values) -> torch.Tensor:
+        """The base generators' dense batched block forward -- every branch computed in
+        full against the shared prefix (fastdllm_v2_generation.py:151-186,
+        nld_generation.py:77-105) -- on the same kernels: with a negative threshold the
+        gate recomputes every row, and the folded forward is then the dense one
+        (fastdllm_v2_folded.py:6).  Used for the vanilla / unfolded comparisons; the fold
+        counters are left alone.  Returns logits [B1, N, V] (shifted for Fast-dLLM)."""
+        B1, N = batched_input.shape
+        logits, _ = self._run(batched_input, past_key_values, B1 * N, count_stats=False, delta=-1.0)
+        return logits
+
+    def _run(self, batched_input, past_key_values, bucket, count_stats=True, delta=None):
         lib = _lib.load()
         m_ = self.model_executor.model
         base = self._base()
@@ -258,6 +270,7 @@ class FoldedVerifyB200:
                                      stream.cuda_stream), "parent map")
         st["hidden"].copy_(hidden.reshape(BN, -1))
         st["args"].stream = stream.cuda_stream
+        st["args"].delta = self.delta if delta is None else float(delta)
         _lib.check(lib.sf_folded_verify_forward(st["args"]), "folded verify forward")
         logits = st["logits"].clone()
         rec = st["rec"].clone() if st["rec"] is not None else None

@@ -227,9 +227,13 @@ def kv_append(cache_k, cache_v, new_k, new_v, P):
     for t in (cache_k, cache_v):
         if t.stride(2) != 1 or t.stride(1) != hd:
             raise ValueError("cache rows must be contiguous [cap, hd] per head")
+    if cache_v.stride(0) != cache_k.stride(0):
+        raise ValueError("cache_k and cache_v must share one head stride")
     for t in (new_k, new_v):
-        if t.stride(2) != 1 or t.stride(1) != hd:
+        if t.stride(2) != 1 or (n > 1 and t.stride(1) != hd):
             raise ValueError("new rows must be contiguous [n, hd] per head")
+    if new_v.stride(0) != new_k.stride(0):
+        raise ValueError("new_k and new_v must share one head stride")
     if P + n > cap:
         raise ValueError(f"cache capacity {cap} < {P + n}")
     _lib.check(_lib.load().sf_kv_append(

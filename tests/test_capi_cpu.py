@@ -4,6 +4,8 @@ import ctypes
 import os
 import re
 
+import pytest
+
 import torch
 
 from specfold_b200 import _lib
@@ -66,3 +68,13 @@ def test_parent_map_matches_oracle():
             pos = torch.randperm(N, generator=g)[:k]
             rows[i, pos] = torch.randint(5, 9, (k,), generator=g)
         assert FoldedVerifyB200._build_parent_map(rows) == orc.parent_map(rows)
+
+
+def test_preallocated_kv_cache_is_device_only():
+    """The cache appends with a CUDA kernel; there is no host fallback."""
+    import torch
+    from specfold_b200.kv_cache import PreallocatedKVCache
+    with pytest.raises(ValueError):
+        PreallocatedKVCache(2, 4, 128, 64, dtype=torch.bfloat16, device="cpu")
+    with pytest.raises(ValueError):
+        PreallocatedKVCache(0, 4, 128, 64, dtype=torch.bfloat16, device="cuda")
