@@ -174,6 +174,17 @@ int sf_kv_append(int dtype, void* cache_k, void* cache_v, int64_t cache_head_str
                  const void* new_k, const void* new_v, int64_t new_head_stride, int Hkv,
                  int hd, int P, int n_new, void* stream);
 
+/* Greedy top-p sampling of logits rows (temperature 0): tokens[r] = the argmax token,
+ * conf[r] = its probability after top-p filtering, in the logits' dtype -- what the
+ * decode loops take from FastDLLMModelExecutor.sample_with_top_p
+ * (fastdllm_model_executor.py:130-155; used at fastdllm_v2_generation.py:346-351) --
+ * computed per row by a radix select of the nucleus boundary instead of a vocabulary
+ * sort.  logits [rows][row_stride] (row_stride >= V elements), tokens int64 [rows],
+ * conf [rows]; 0 < top_p. */
+int sf_sample_top_p_greedy(int dtype, const void* logits, int64_t rows, int V,
+                           int64_t row_stride, float top_p, int64_t* tokens, void* conf,
+                           void* stream);
+
 /* ------------------------------------------------------------ whole forward -------
  * The full per-layer loop of SpecFoldTritonFastDLLMV2Generation._batched_block_forward
  * (fastdllm_v2_folded.py:296-366) in one call: gate -> QKV -> attention -> chain

@@ -568,6 +568,18 @@ int sf_kv_append(int dtype, void* cache_k, void* cache_v, int64_t cache_head_str
                      "kv_append");
 }
 
+int sf_sample_top_p_greedy(int dtype, const void* logits, int64_t rows, int V,
+                           int64_t row_stride, float top_p, int64_t* tokens, void* conf,
+                           void* stream) {
+  if (!dtype_ok(dtype) || !logits || !tokens || !conf || rows < 0 || V < 1 || row_stride < V ||
+      !(top_p > 0.0f))
+    return fail(SF_ERR_ARG, "bad sample_top_p_greedy arguments");
+  if (rows > 0x7FFFFFFF) return fail(SF_ERR_ARG, "sample_top_p_greedy: too many rows");
+  return cuda_status(launch_sample_top_p(dtype, logits, rows, V, row_stride, top_p, tokens, conf,
+                                         S(stream)),
+                     "sample_top_p_greedy");
+}
+
 size_t sf_verify_workspace_bytes(int dtype, int B1, int N, int D, int H, int Hkv, int hd, int I,
                                  int V, int P) {
   return carve_forward(nullptr, dtype, B1, N, D, H, Hkv, hd, I, V, B1 * N, P).total + 256;

@@ -310,4 +310,8 @@ cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, co
                              const void* nv, int64_t n_stride, int Hkv, int hd, int P, int n,
                              cudaStream_t st);
 
+cudaError_t launch_sample_top_p(int dtype, const void* logits, int64_t rows, int V,
+                                int64_t row_stride, float top_p, int64_t* tokens, void* conf,
+                                cudaStream_t st);
+
 }  // namespace sf

@@ -31,6 +31,7 @@ from typing import Dict, List, Optional, Tuple
 import torch
 
 from . import _lib
+from . import kernels as K
 from .kernels import dtype_code
 
 logger = logging.getLogger(__name__)
@@ -410,6 +411,23 @@ class SpecFoldB200FastDLLMV2Generation(FoldedVerifyB200):
     (replaces SpecFoldTritonFastDLLMV2Generation)."""
 
     family = "fastdllm"
+
+    def _sample_with_top_p(self, logits: torch.Tensor, top_p: float = 0.95,
+                           temperature: float = 0.0):
+        """The decode loops' sampler (fastdllm_v2_generation.py:134-149 ->
+        FastDLLMModelExecutor.sample_with_top_p) on the GPU for greedy decoding: tokens
+        and their top-p filtered probabilities without sorting the vocabulary
+        (sf_sample_top_p_greedy).  The probabilities come back as the tokens'
+        confidence broadcast over the vocabulary dimension (a stride-0 view of shape
+        logits.shape): the loops only gather them at the sampled token (:348-351) and
+        slice positions (:615-616).  Temperature sampling keeps the reference's path."""
+        if temperature > 0 or not logits.is_cuda or logits.dtype not in (torch.bfloat16, torch.float32):
+            parent = super()
+            if hasattr(parent, "_sample_with_top_p"):
+                return parent._sample_with_top_p(logits, top_p=top_p, temperature=temperature)
+            raise NotImplementedError("the GPU sampler is greedy (temperature 0) on CUDA logits")
+        tokens, conf = K.sample_top_p_greedy(logits, top_p)
+        return tokens, conf.unsqueeze(-1).expand(*logits.shape)
 
 
 class SpecFoldB200NLDGeneration(FoldedVerifyB200):

@@ -219,6 +219,26 @@ def final_norm_lm_head(hidden, norm_w, lm_w, B1, N, eps, shift, err=None):
     return logits, err
 
 
+def sample_top_p_greedy(logits: torch.Tensor, top_p: float = 0.95):
+    """Greedy top-p sampling over the last dimension on the GPU: (tokens int64, the
+    tokens' top-p filtered probabilities in the logits' dtype), both shaped
+    logits.shape[:-1] (sf_sample_top_p_greedy; the reference's
+    FastDLLMModelExecutor.sample_with_top_p at temperature 0)."""
+    if not logits.is_cuda:
+        raise ValueError("specfold_b200 kernels take CUDA tensors")
+    V = logits.shape[-1]
+    x = logits.reshape(-1, V)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    rows = x.shape[0]
+    tokens = torch.empty(rows, dtype=torch.int64, device=x.device)
+    conf = torch.empty(rows, dtype=x.dtype, device=x.device)
+    _lib.check(_lib.load().sf_sample_top_p_greedy(
+        dtype_code(x), x.data_ptr(), rows, V, x.stride(0), float(top_p), tokens.data_ptr(),
+        conf.data_ptr(), _stream()), "sample_top_p_greedy")
+    return tokens.view(logits.shape[:-1]), conf.view(logits.shape[:-1])
+
+
 def kv_append(cache_k, cache_v, new_k, new_v, P):
     """cache_{k,v}: [Hkv, cap, hd] (any head stride, inner dims contiguous); new_{k,v}:
     [Hkv, n, hd].  Writes positions [P, P+n)."""

@@ -115,6 +115,18 @@ def bench_lm_head(dims, rows, iters, g):
                    {"rows": B1 * N})
 
 
+def bench_sample(dims, rows, iters, g):
+    """Greedy top-p sampling of a verify step's logits (256 rows x V, bf16) on the GPU
+    sampler; for context, the time of the full-vocabulary torch.sort alone, the first of
+    the reference sampler's five full-size passes (fastdllm_model_executor.py:141)."""
+    V = dims.vocab
+    x = (torch.randn(rows, V, generator=g) * 2.0).to(torch.bfloat16).cuda()
+    ms = _events(lambda: K.sample_top_p_greedy(x, 0.95), iters)
+    sort_ms = _events(lambda: torch.sort(x, descending=True, dim=-1), iters)
+    return _report("sample", ms, rows * V * 2, 0, {"rows": rows, "vocab": V,
+                                                   "torch_sort_ms": round(sort_ms, 4)})
+
+
 def bench_forward(dims, args):
     """Whole verify forward (main + 7 drafts, configuration-0 noise, fold ~0.6) with
     ``--layers`` decoder layers of the named shape; per-kernel times from the library's
@@ -148,7 +160,7 @@ def bench_forward(dims, args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
-                    choices=["qkv", "o_proj", "ffn", "lm_head", "all_gemm", "forward"])
+                    choices=["qkv", "o_proj", "ffn", "lm_head", "all_gemm", "forward", "sample"])
     ap.add_argument("--shape", default="qwen7b", choices=sorted(SHAPES))
     ap.add_argument("--rows", type=int, default=122)
     ap.add_argument("--iters", type=int, default=20)
@@ -165,6 +177,9 @@ def main():
     g = torch.Generator().manual_seed(args.seed)
     if args.kernel == "forward":
         bench_forward(dims, args)
+        return
+    if args.kernel == "sample":
+        bench_sample(dims, 256 if args.rows == 122 else args.rows, args.iters, g)
         return
     todo = ["qkv", "o_proj", "ffn", "lm_head"] if args.kernel == "all_gemm" else [args.kernel]
     for k in todo:

@@ -52,3 +52,16 @@ def test_src_chain():
     rec = torch.tensor([[1, 1, 1], [0, 1, 0], [0, 0, 1]], dtype=torch.bool)
     src = orc.nearest_recomputing_ancestor(rec, [None, 0, 1])
     assert src.tolist() == [[0, 0, 0], [0, 1, 0], [0, 1, 2]]
+
+
+def test_sampling_oracle_matches_reference():
+    """oracle/sampling.py reproduces the reference's greedy top-p sampler
+    (fastdllm_model_executor.py:109-155) bit for bit on the CPU fixtures."""
+    import os
+    from oracle import sampling
+    path = os.path.join(os.path.dirname(__file__), "golden", "sampling.pt")
+    data = torch.load(path)
+    for name, case in data.items():
+        tok, conf = sampling.greedy_confidence(case["logits"], case["top_p"])
+        assert torch.equal(tok, case["tokens"]), name
+        assert torch.equal(conf, case["conf"]), name
