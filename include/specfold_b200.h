@@ -185,6 +185,26 @@ int sf_sample_top_p_greedy(int dtype, const void* logits, int64_t rows, int V,
                            int64_t row_stride, float top_p, int64_t* tokens, void* conf,
                            void* stream);
 
+/* Draft blocks from the calibration graph (FastDLLMV2SpeculativeGeneration.
+ * get_draft_blocks, fastdllm_v2_generation.py:387-474; NLDDiffusionGeneration.
+ * get_draft_blocks, nld_generation.py:108-151): confidence of each of the n_pos
+ * positions = its maximal softmax probability (conf_fp32 = 1: fp32, as NLD; 0: in the
+ * logits' dtype, as Fast-dLLM); for node k with pairs[node_off[k]..node_off[k+1]) of
+ * (pos_rank, vocab_rank), drafts[k] = block with block[pos_offset + p] = the
+ * vocab_rank-th most likely token of p, p = the pos_rank-th most confident masked
+ * position; valid[k] = 0 when the node needs more masked positions than there are
+ * (the reference skips it).  Ties rank the larger value, then the smaller index first.
+ * logits [n_pos][row_stride] (>= V), mask uint8 [n_pos], pairs int32 [n_pairs][2],
+ * node_off int32 [n_nodes + 1], block int64 [block_len], drafts int64
+ * [n_nodes][block_len], valid int32 [n_nodes], all on the device; K = largest
+ * vocab_rank + 1 (<= 16), n_pos <= 1024; ws: sf_draft_workspace_bytes(n_pos, K) bytes. */
+size_t sf_draft_workspace_bytes(int n_pos, int K);
+int sf_draft_blocks(int dtype, const void* logits, int64_t row_stride, int n_pos, int V, int K,
+                    int conf_fp32, const uint8_t* mask, const int32_t* pairs,
+                    const int32_t* node_off, int n_nodes, const int64_t* block, int block_len,
+                    int pos_offset, int64_t* drafts, int32_t* valid, void* ws, size_t ws_bytes,
+                    void* stream);
+
 /* ------------------------------------------------------------ whole forward -------
  * The full per-layer loop of SpecFoldTritonFastDLLMV2Generation._batched_block_forward
  * (fastdllm_v2_folded.py:296-366) in one call: gate -> QKV -> attention -> chain

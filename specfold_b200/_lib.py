@@ -87,6 +87,10 @@ _SIGS = {
                              c_int, c_int, c_int, c_int, c_void_p]),
     "sf_sample_top_p_greedy": (c_int, [c_int, c_void_p, c_int64, c_int, c_int64, c_float,
                                        c_void_p, c_void_p, c_void_p]),
+    "sf_draft_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "sf_draft_blocks": (c_int, [c_int, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p,
+                                c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p,
+                                c_void_p, c_void_p, c_size_t, c_void_p]),
     "sf_weight_tiles_bytes": (c_size_t, [c_int] * 4),
     "sf_parent_map": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "sf_tp_unique_id": (c_int, [c_void_p, c_int]),

@@ -568,6 +568,36 @@ int sf_kv_append(int dtype, void* cache_k, void* cache_v, int64_t cache_head_str
                      "kv_append");
 }
 
+size_t sf_draft_workspace_bytes(int n_pos, int K) {
+  if (n_pos < 0 || K < 1) return 0;
+  return ((static_cast<size_t>(n_pos) * 4 + 255) / 256) * 256 + static_cast<size_t>(n_pos) * K * 8;
+}
+
+int sf_draft_blocks(int dtype, const void* logits, int64_t row_stride, int n_pos, int V, int K,
+                    int conf_fp32, const uint8_t* mask, const int32_t* pairs,
+                    const int32_t* node_off, int n_nodes, const int64_t* block, int block_len,
+                    int pos_offset, int64_t* drafts, int32_t* valid, void* ws, size_t ws_bytes,
+                    void* stream) {
+  if (!dtype_ok(dtype) || (n_pos > 0 && !logits) || !mask || !node_off || !block ||
+      (n_nodes > 0 && (!drafts || !valid)) || n_pos < 0 || V < 1 || row_stride < V || n_nodes < 0 ||
+      block_len < 1)
+    return fail(SF_ERR_ARG, "bad draft_blocks arguments");
+  if (K < 1 || K > draft_max_topk() || K > V)
+    return fail(SF_ERR_ARG, "draft_blocks: K = %d outside [1, %d] or above V", K, draft_max_topk());
+  if (n_pos > draft_max_positions() || pos_offset < 0 || pos_offset + n_pos > block_len)
+    return fail(SF_ERR_ARG, "draft_blocks: positions [%d, %d) outside the block of %d (at most %d)",
+                pos_offset, pos_offset + n_pos, block_len, draft_max_positions());
+  const size_t need = sf_draft_workspace_bytes(n_pos, K);
+  if (!ws || ws_bytes < need) return fail(SF_ERR_WORKSPACE, "draft_blocks: workspace %zu < %zu", ws_bytes, need);
+  float* conf = static_cast<float*>(ws);
+  int64_t* top = reinterpret_cast<int64_t*>(static_cast<char*>(ws) +
+                                            ((static_cast<size_t>(n_pos) * 4 + 255) / 256) * 256);
+  return cuda_status(launch_draft_blocks(dtype, logits, row_stride, n_pos, V, K, conf_fp32, mask,
+                                         pairs, node_off, n_nodes, block, block_len, pos_offset,
+                                         drafts, valid, conf, top, S(stream)),
+                     "draft_blocks");
+}
+
 int sf_sample_top_p_greedy(int dtype, const void* logits, int64_t rows, int V,
                            int64_t row_stride, float top_p, int64_t* tokens, void* conf,
                            void* stream) {

@@ -310,6 +310,15 @@ cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, co
                              const void* nv, int64_t n_stride, int Hkv, int hd, int P, int n,
                              cudaStream_t st);
 
+int draft_max_topk();
+int draft_max_positions();
+cudaError_t launch_draft_blocks(int dtype, const void* logits, int64_t row_stride, int n_pos,
+                                int V, int K, int conf_fp32, const uint8_t* mask,
+                                const int32_t* pairs, const int32_t* node_off, int n_nodes,
+                                const int64_t* block, int block_len, int pos_offset,
+                                int64_t* drafts, int32_t* valid, float* conf, int64_t* top,
+                                cudaStream_t st);
+
 cudaError_t launch_sample_top_p(int dtype, const void* logits, int64_t rows, int V,
                                 int64_t row_stride, float top_p, int64_t* tokens, void* conf,
                                 cudaStream_t st);

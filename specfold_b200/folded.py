@@ -32,6 +32,7 @@ import torch
 
 from . import _lib
 from . import kernels as K
+from .kernels import draft_blocks as K_draft_blocks
 from .kernels import dtype_code
 
 logger = logging.getLogger(__name__)
@@ -405,6 +406,39 @@ class FoldedVerifyB200:
     def _q_scale(self, cfg, P, N, device):
         return None
 
+    # -------------------------------------------------------------- draft construction
+    def _graph_pairs(self, device):
+        """The calibration graph's nodes with a non-empty ij_set and their (pos_rank,
+        vocab_rank) pairs as device tensors, cached per graph object."""
+        graph = getattr(self, "calibration_graph", None)
+        if graph is None:
+            return None
+        key = (id(graph), str(device))
+        cache = self.__dict__.setdefault("_graph_pairs_cache", {})
+        hit = cache.get(key)
+        if hit is not None and hit[0] is graph:
+            return hit[1]
+        nodes = [n for n in graph.get("selected_nodes", []) if n.get("ij_set")]
+        pairs, off = [], [0]
+        for n in nodes:
+            pairs += [(int(i), int(j)) for i, j in n["ij_set"]]
+            off.append(len(pairs))
+        K = 1 + max((j for _, j in pairs), default=0)
+        out = (nodes,
+               torch.tensor(pairs or [(0, 0)], dtype=torch.int32, device=device).reshape(-1, 2),
+               torch.tensor(off, dtype=torch.int32, device=device), K)
+        cache[key] = (graph, out)
+        return out
+
+    def _draft_states(self, block, logits, mask, pos_offset, conf_fp32):
+        """(nodes, drafts [n_nodes, L], valid list) from sf_draft_blocks; one host sync."""
+        g = self._graph_pairs(block.device)
+        if g is None or not g[0]:
+            return [], None, []
+        nodes, pairs, off, K = g
+        drafts, valid = K_draft_blocks(logits, mask, block, pos_offset, pairs, off, K, conf_fp32)
+        return nodes, drafts, valid.tolist()
+
 
 class SpecFoldB200FastDLLMV2Generation(FoldedVerifyB200):
     """Fast-dLLM v2 (Qwen2 backbone): QKV bias, shifted logits
@@ -429,6 +463,33 @@ class SpecFoldB200FastDLLMV2Generation(FoldedVerifyB200):
         tokens, conf = K.sample_top_p_greedy(logits, top_p)
         return tokens, conf.unsqueeze(-1).expand(*logits.shape)
 
+    @torch.no_grad()
+    def get_draft_blocks(self, x: torch.Tensor, p: torch.Tensor,
+                         mask_index: Optional[torch.Tensor] = None, start_pos: Optional[int] = None,
+                         end_pos: Optional[int] = None, small_block_start: Optional[int] = None,
+                         small_block_end: Optional[int] = None, **kwargs) -> List[dict]:
+        """Draft blocks of the calibration graph (fastdllm_v2_generation.py:387-474) on the
+        GPU (sf_draft_blocks): confidences and the needed top-k tokens of the small block's
+        positions in one pass over their logits, every node's draft in one launch, one
+        host sync (the reference runs a vocabulary topk per pair and syncs per node).
+        Same arguments and result: dicts with 'state', 'start_pos', 'end_pos', 'node'."""
+        if getattr(self, "calibration_graph", None) is None or mask_index is None:
+            return []
+        if not (x.is_cuda and p.is_cuda) or p.dtype not in (torch.bfloat16, torch.float32):
+            parent = super()
+            if hasattr(parent, "get_draft_blocks"):
+                return parent.get_draft_blocks(x, p, mask_index, start_pos, end_pos,
+                                               small_block_start, small_block_end, **kwargs)
+            raise NotImplementedError("GPU draft construction takes CUDA bf16 / fp32 logits")
+        if small_block_start is not None and small_block_end is not None:
+            lo, hi = small_block_start, small_block_end
+        else:
+            lo, hi = 0, x.shape[0]
+        # the reference's softmax runs in the logits' dtype (:434)
+        nodes, drafts, valid = self._draft_states(x, p[lo:hi], mask_index[lo:hi], lo, conf_fp32=False)
+        return [{"state": drafts[k], "start_pos": start_pos, "end_pos": end_pos, "node": n}
+                for k, n in enumerate(nodes) if valid[k]]
+
 
 class SpecFoldB200NLDGeneration(FoldedVerifyB200):
     """Nemotron-Labs-Diffusion (Ministral3 / Llama backbone): no QKV bias, unshifted
@@ -436,6 +497,21 @@ class SpecFoldB200NLDGeneration(FoldedVerifyB200):
     (replaces SpecFoldTritonNLDGeneration, nld_folded.py:244-394)."""
 
     family = "nld"
+
+    @torch.no_grad()
+    def get_draft_blocks(self, x_block: torch.Tensor, logits_block: torch.Tensor,
+                         mask_index: torch.Tensor) -> List[dict]:
+        """Draft blocks of the calibration graph over the whole block
+        (nld_generation.py:108-151) on the GPU (sf_draft_blocks; fp32 confidences as the
+        reference's softmax of logits.float()).  Dicts with 'state' and 'node'."""
+        if not (x_block.is_cuda and logits_block.is_cuda) or \
+                logits_block.dtype not in (torch.bfloat16, torch.float32):
+            parent = super()
+            if hasattr(parent, "get_draft_blocks"):
+                return parent.get_draft_blocks(x_block, logits_block, mask_index)
+            raise NotImplementedError("GPU draft construction takes CUDA bf16 / fp32 logits")
+        nodes, drafts, valid = self._draft_states(x_block, logits_block, mask_index, 0, conf_fp32=True)
+        return [{"state": drafts[k], "node": n} for k, n in enumerate(nodes) if valid[k]]
 
     def _q_scale(self, cfg, P, N, device):
         rp = getattr(cfg, "rope_parameters", None) or {}

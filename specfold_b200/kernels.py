@@ -40,6 +40,9 @@ def _check_cuda(*ts):
             raise ValueError("specfold_b200 kernels take contiguous tensors")
 
 
+_DRAFT_WS = {}
+
+
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Zero-initialised scratch shared by the GEMM entry points (split-K partials and
     tile counters; the kernels leave the counters at zero)."""
@@ -237,6 +240,38 @@ def sample_top_p_greedy(logits: torch.Tensor, top_p: float = 0.95):
         dtype_code(x), x.data_ptr(), rows, V, x.stride(0), float(top_p), tokens.data_ptr(),
         conf.data_ptr(), _stream()), "sample_top_p_greedy")
     return tokens.view(logits.shape[:-1]), conf.view(logits.shape[:-1])
+
+
+def draft_blocks(logits: torch.Tensor, mask: torch.Tensor, block: torch.Tensor, pos_offset: int,
+                 pairs: torch.Tensor, node_off: torch.Tensor, K: int, conf_fp32: bool):
+    """Draft blocks from the calibration graph on the GPU (sf_draft_blocks): logits
+    [n_pos, V] of the positions [pos_offset, pos_offset + n_pos) of ``block`` (int64
+    [L]), mask bool [n_pos], pairs int32 [n_pairs, 2] (pos_rank, vocab_rank), node_off
+    int32 [n_nodes + 1].  Returns (drafts int64 [n_nodes, L], valid int32 [n_nodes])."""
+    for t in (logits, mask, block, pairs, node_off):
+        if not t.is_cuda:
+            raise ValueError("specfold_b200 kernels take CUDA tensors")
+    n_pos, V = logits.shape
+    x = logits if logits.stride(-1) == 1 else logits.contiguous()
+    m = mask.contiguous().view(torch.uint8) if mask.dtype == torch.bool else mask.to(torch.uint8)
+    blk = block.contiguous()
+    n_nodes = node_off.numel() - 1
+    drafts = torch.empty(max(n_nodes, 1), blk.numel(), dtype=torch.int64, device=x.device)[:n_nodes]
+    valid = torch.empty(max(n_nodes, 1), dtype=torch.int32, device=x.device)[:n_nodes]
+    lib = _lib.load()
+    nbytes = lib.sf_draft_workspace_bytes(n_pos, K)
+    # scratch of its own: the GEMM workspace's counters must stay zero
+    idx = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    ws = _DRAFT_WS.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=x.device)
+        _DRAFT_WS[idx] = ws
+    _lib.check(lib.sf_draft_blocks(
+        dtype_code(x), x.data_ptr(), x.stride(0), n_pos, V, K, 1 if conf_fp32 else 0,
+        m.data_ptr(), pairs.data_ptr(), node_off.data_ptr(), n_nodes, blk.data_ptr(), blk.numel(),
+        int(pos_offset), drafts.data_ptr(), valid.data_ptr(), ws.data_ptr(), ws.numel(), _stream()),
+        "draft_blocks")
+    return drafts, valid
 
 
 def kv_append(cache_k, cache_v, new_k, new_v, P):

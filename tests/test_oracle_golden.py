@@ -65,3 +65,21 @@ def test_sampling_oracle_matches_reference():
         tok, conf = sampling.greedy_confidence(case["logits"], case["top_p"])
         assert torch.equal(tok, case["tokens"]), name
         assert torch.equal(conf, case["conf"]), name
+
+
+def test_draft_oracle_matches_reference():
+    """oracle/drafts.py reproduces both reference draft constructions
+    (fastdllm_v2_generation.py:387-474, nld_generation.py:108-151) on the fixtures."""
+    import os
+    from oracle import drafts
+    data = torch.load(os.path.join(os.path.dirname(__file__), "golden", "drafts.pt"))
+    graph, nodes = data["graph"], data["graph"]["selected_nodes"]
+    for c in data["cases"]:
+        L = c["x"].shape[0]
+        f = drafts.fastdllm_draft_blocks(graph, c["x"], c["logits"], c["mask"], 64, 64 + L,
+                                         c["small"][0], c["small"][1])
+        n = drafts.nld_draft_blocks(graph, c["x"], c["logits"], c["mask"])
+        for got, ref in ((f, c["fastdllm"]), (n, c["nld"])):
+            assert [nodes.index(d["node"]) for d in got] == [k for _, k in ref]
+            for d, (state, _) in zip(got, ref):
+                assert torch.equal(d["state"], state)
