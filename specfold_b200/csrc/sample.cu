@@ -108,49 +108,159 @@ __global__ void __launch_bounds__(kSampleThreads) sample_top_p_kernel(
   float mx = -INFINITY;
   for (int i = tid; i < V; i += kSampleThreads) mx = fmaxf(mx, Elt<T>::to_f(x[i]));
   const float m = block_max(mx, red);
-  float z = 0.f;
-  for (int i = tid; i < V; i += kSampleThreads) z += expf(Elt<T>::to_f(x[i]) - m);
-  const float Z = block_sum(z, red);
-
-  // ---- select of the crossing logit.  Level 0: bins of 1/128 logit below the maximum
-  // (tokens more than 32 below it share the last bin: their total probability is under
-  // V * e^-32); then, inside the crossing bin's order-key range [klo, khi], bins of
-  // 2^shift keys until one key (one logit value) is left.
-  uint32_t klo = 0, khi = 0xFFFFFFFFu;
-  unsigned long long p_above = 0, e_above = 0;
-  bool crossed = true;
-  int final_bin = -1, lv0_bin = -1;
-  // level-0 bin of a logit: monotone in l (the subtraction and the scaling by 128 are)
+  // level-0 bin of a logit: bins of 1/128 logit below the maximum, the last bin holding
+  // every token more than 32 below it (their total probability is under V * e^-32);
+  // monotone in l (the subtraction and the scaling by 128 are)
   auto bin0 = [&](float l) {
     const float d = (m - l) * 128.0f;
     const int db = d < static_cast<float>(kBins - 1) ? static_cast<int>(d) : kBins - 1;
     return kBins - 1 - db;                     // larger logit -> higher bin
   };
-  for (int lv = 0; lv < 6; ++lv) {
+  // the normaliser and the level-0 bin counts in one pass
+  for (int b = tid; b < kBins; b += kSampleThreads) cnt[b] = 0;
+  __syncthreads();
+  float z = 0.f;
+  for (int i = tid; i < V; i += kSampleThreads) {
+    const float l = Elt<T>::to_f(x[i]);
+    z += expf(l - m);
+    atomicAdd(&cnt[bin0(l)], 1u);
+  }
+  const float Z = block_sum(z, red);
+
+  // ---- select of the crossing logit.  Level 0 (bins of bin0): the bin counts bound the
+  // probability in each bin (p of a bin-d token lies within exp(-(d+1)/128)/Z and
+  // exp(-d/128)/Z, give or take the rounding to T), which brackets the crossing bin;
+  // an exact pass then sums p and exp(l - m) over the bins above the bracket in
+  // registers and histograms only the bracket.  Later levels refine inside the crossing
+  // bin's order-key range [klo, khi] with bins of 2^shift keys until one key is left.
+  uint32_t klo = 0, khi = 0xFFFFFFFFu;
+  unsigned long long p_above = 0, e_above = 0;
+  bool crossed = true;
+  int final_bin = -1, lv0_bin = -1;
+  constexpr int per = kBins / kSampleThreads;
+  {
+    // cumulative bounds from the top bin; thread t owns bins [kBins-1-8t-7, kBins-1-8t]
+    float lo_c[per], hi_c[per], lsum = 0.f, hsum = 0.f;
+#pragma unroll
+    for (int j = 0; j < per; ++j) {
+      const int b = kBins - 1 - (tid * per + j);
+      const int d = kBins - 1 - b;
+      const float c = static_cast<float>(cnt[b]);
+      const float phi = expf(-static_cast<float>(d) / 128.0f) / Z * (1.0f + 1.0f / 64.0f);
+      const float plo = d == kBins - 1 ? 0.f : expf(-static_cast<float>(d + 1) / 128.0f) / Z * (1.0f - 1.0f / 64.0f);
+      lsum += c * plo;
+      hsum += c * phi;
+      lo_c[j] = lsum;
+      hi_c[j] = hsum;
+    }
+    // inclusive prefix over threads (warp shuffles + warps above)
+    float il = lsum, ih = hsum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float vl = __shfl_up_sync(0xffffffffu, il, o), vh = __shfl_up_sync(0xffffffffu, ih, o);
+      if ((tid & 31) >= o) { il += vl; ih += vh; }
+    }
+    __shared__ float wl[kSampleThreads / 32], wh[kSampleThreads / 32];
+    __shared__ int s_start, s_end;
+    if ((tid & 31) == 31) { wl[tid >> 5] = il; wh[tid >> 5] = ih; }
+    if (tid == 0) { s_start = -1; s_end = 0; }
+    __syncthreads();
+    float bl = il - lsum, bh = ih - hsum;
+    for (int w = 0; w < (tid >> 5); ++w) { bl += wl[w]; bh += wh[w]; }
+#pragma unroll
+    for (int j = 0; j < per; ++j) {
+      const int b = kBins - 1 - (tid * per + j);
+      const float cl = bl + lo_c[j], ch = bh + hi_c[j];
+      const float pl = bl + (j ? lo_c[j - 1] : 0.f), ph = bh + (j ? hi_c[j - 1] : 0.f);
+      // first bin (from the top) where the upper / lower cumulative bound crosses
+      if (round_t<T>(ch) > top_p && round_t<T>(ph) <= top_p) s_start = b;
+      if (round_t<T>(cl) > top_p && round_t<T>(pl) <= top_p) s_end = b;
+    }
+    __syncthreads();
+    const int b_start = s_start, b_end = s_end;
+    if (b_start < 0) {
+      crossed = false;                     // even the upper bound never crosses
+    } else {
+      // exact pass: register sums above the bracket, a histogram of the bracket
+      for (int b = tid; b < kBins; b += kSampleThreads) { hp[b] = 0; he[b] = 0; }
+      __syncthreads();
+      unsigned long long rp = 0, re = 0;
+      for (int i = tid; i < V; i += kSampleThreads) {
+        const float l = Elt<T>::to_f(x[i]);
+        const int b = bin0(l);
+        if (b < b_end) continue;
+        const float e = expf(l - m);
+        const unsigned long long fp = to_fix(round_t<T>(__fdiv_rn(e, Z))), fe = to_fix(e);
+        if (b > b_start) {
+          rp += fp;
+          re += fe;
+        } else {
+          atomicAdd(&hp[b], fp);
+          atomicAdd(&he[b], fe);
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        rp += __shfl_xor_sync(0xffffffffu, rp, o);
+        re += __shfl_xor_sync(0xffffffffu, re, o);
+      }
+      if ((tid & 31) == 0) { sp[tid >> 5] = rp; se[tid >> 5] = re; }
+      if (tid == 0) walk.bin = -1;
+      __syncthreads();
+      if (tid == 0) {
+        unsigned long long bp = 0, be = 0;
+        for (int w = 0; w < kSampleThreads / 32; ++w) { bp += sp[w]; be += se[w]; }
+        for (int b = b_start; b >= b_end; --b) {
+          const unsigned long long np = bp + hp[b];
+          if (np != bp && round_t<T>(from_fix(np)) > top_p) {
+            walk.bin = b;
+            walk.p_above = bp;
+            walk.e_above = be;
+            break;
+          }
+          bp = np;
+          be += he[b];
+        }
+      }
+      __syncthreads();
+      if (walk.bin < 0) {
+        crossed = false;
+      } else {
+        const int b = walk.bin;
+        p_above = walk.p_above;
+        e_above = walk.e_above;
+        // a key range holding the bin's logit interval, widened for the rounding of the
+        // bin arithmetic (values of the neighbouring bins inside it are excluded by the
+        // level-0 bin test of the later levels)
+        const int d = kBins - 1 - b;
+        constexpr uint32_t kMargin = 1u << 12;
+        const uint32_t k_hi = order_key(d == 0 ? m : m - static_cast<float>(d) / 128.0f);
+        const uint32_t k_lo = d == kBins - 1 ? 0u : order_key(m - static_cast<float>(d + 1) / 128.0f);
+        klo = k_lo > kMargin ? k_lo - kMargin : 0u;
+        khi = k_hi < 0xFFFFFFFFu - kMargin ? k_hi + kMargin : 0xFFFFFFFFu;
+        lv0_bin = b;
+      }
+      __syncthreads();
+    }
+  }
+  for (int lv = 1; lv < 6 && crossed; ++lv) {
     const uint32_t span = khi - klo;
-    const int shift = lv == 0 ? 0 : max(0, 32 - __clz(span) - 12);
+    const int shift = max(0, 32 - __clz(span) - 12);
     for (int b = tid; b < kBins; b += kSampleThreads) { hp[b] = 0; he[b] = 0; cnt[b] = 0; }
     __syncthreads();
     for (int i = tid; i < V; i += kSampleThreads) {
       const float l = Elt<T>::to_f(x[i]);
       const uint32_t key = order_key(l);
       if (key < klo || key > khi) continue;
-      int b;
-      if (lv == 0) {
-        b = bin0(l);
-      } else {
-        if (bin0(l) != lv0_bin) continue;      // counted in a neighbouring level-0 bin
-        b = static_cast<int>((key - klo) >> shift);
-      }
+      if (bin0(l) != lv0_bin) continue;        // counted in a neighbouring level-0 bin
+      const int b = static_cast<int>((key - klo) >> shift);
       const float e = expf(l - m);
       const float p = round_t<T>(__fdiv_rn(e, Z));
-      if (shift == 0 && lv > 0) atomicAdd(&cnt[b], 1u);   // counts: the exact-key level only
+      if (shift == 0) atomicAdd(&cnt[b], 1u);  // counts: the exact-key level only
       atomicAdd(&hp[b], to_fix(p));
       atomicAdd(&he[b], to_fix(e));
     }
     __syncthreads();
     // suffix sums from the top bin: thread t owns bins [kBins-1-8t-7, kBins-1-8t]
-    constexpr int per = kBins / kSampleThreads;
     unsigned long long mp = 0, me = 0;
 #pragma unroll
     for (int j = 0; j < per; ++j) {
@@ -191,22 +301,9 @@ __global__ void __launch_bounds__(kSampleThreads) sample_top_p_kernel(
     const int b = walk.bin;
     p_above = walk.p_above;
     e_above = walk.e_above;
-    if (lv == 0) {
-      // a key range holding the bin's logit interval, widened for the rounding of the
-      // bin arithmetic (values of the neighbouring bins inside it are excluded by the
-      // level-0 bin test of the later levels)
-      const int d = kBins - 1 - b;
-      constexpr uint32_t kMargin = 1u << 12;
-      const uint32_t k_hi = order_key(d == 0 ? m : m - static_cast<float>(d) / 128.0f);
-      const uint32_t k_lo = d == kBins - 1 ? 0u : order_key(m - static_cast<float>(d + 1) / 128.0f);
-      klo = k_lo > kMargin ? k_lo - kMargin : 0u;
-      khi = k_hi < 0xFFFFFFFFu - kMargin ? k_hi + kMargin : 0xFFFFFFFFu;
-      lv0_bin = b;
-    } else {
-      klo = klo + (static_cast<uint32_t>(b) << shift);
-      khi = min(khi, klo + ((1u << shift) - 1u));
-    }
-    if (lv > 0 && shift == 0) { final_bin = b; break; }
+    klo = klo + (static_cast<uint32_t>(b) << shift);
+    khi = min(khi, klo + ((1u << shift) - 1u));
+    if (shift == 0) { final_bin = b; break; }
     __syncthreads();
   }
   if (final_bin < 0) crossed = false;          // not narrowed to one key: keep every token
