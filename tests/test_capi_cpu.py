@@ -55,6 +55,19 @@ def test_argument_validation_without_device():
                                     256, 256, 1e-6, None, None)
     assert st == 1
     assert lib.sf_kv_append(1, 16, 16, 100, 16, 16, 1024, 4, 128, 0, 32, None) == 1  # capacity
+    # sampler: row stride below V, non-positive top_p
+    assert lib.sf_sample_top_p_greedy(1, 16, 4, 1000, 999, 0.95, 16, 16, None) == 1
+    assert lib.sf_sample_top_p_greedy(1, 16, 4, 1000, 1000, 0.0, 16, 16, None) == 1
+    assert b"sample_top_p_greedy" in lib.sf_last_error()
+    # drafts: top-k depth beyond 16, positions outside the block, short workspace
+    assert lib.sf_draft_blocks(1, 16, 1000, 32, 1000, 17, 0, 16, 16, 16, 2, 16, 32, 0, 16, 16,
+                               16, 1 << 20, None) == 1
+    assert lib.sf_draft_blocks(1, 16, 1000, 32, 1000, 4, 0, 16, 16, 16, 2, 16, 32, 8, 16, 16,
+                               16, 1 << 20, None) == 1
+    need = lib.sf_draft_workspace_bytes(32, 4)
+    assert need >= 32 * 4 + 32 * 4 * 8
+    assert lib.sf_draft_blocks(1, 16, 1000, 32, 1000, 4, 0, 16, 16, 16, 2, 16, 32, 0, 16, 16,
+                               16, need - 1, None) == 4                          # workspace
 
 
 def test_parent_map_matches_oracle():
