@@ -963,8 +963,8 @@ static int num_sms() {
 }
 
 // Tuning, read once from the environment: SF_GEMM_SUB (weight tiles per CTA stage: 0 =
-// chosen per GEMM, or 1 / 2 / 4 wherever TMEM allows) and SF_GEMM_SMEM_KB (shared memory
-// per CTA; below ~113 two CTAs share an SM).
+// chosen per GEMM, or 1 / 2 / 4 wherever TMEM allows), SF_GEMM_SMEM_KB (shared memory
+// per CTA; below ~113 two CTAs share an SM) and SF_QKV_SPLITS (split-K of the QKV GEMM).
 constexpr int kDefaultSmemKb = 170;
 constexpr int kMaxSmemKb = 226;
 struct TcTuning {
@@ -972,6 +972,7 @@ struct TcTuning {
   int smem_kb = kDefaultSmemKb;
   int pf_mb = 0;       // SF_GEMM_PF_MB: L2 prefetch budget for the next GEMM's weights
                        // (off: measured, the step got slower at 40 and 80 MB)
+  int qkv_splits = 0;  // SF_QKV_SPLITS: split-K count of the QKV GEMM (0: chosen)
 };
 static const TcTuning& tc_tuning() {
   static TcTuning t;
@@ -983,6 +984,7 @@ static const TcTuning& tc_tuning() {
     }
     if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(kMaxSmemKb, atoi(v)));
     if (const char* v = getenv("SF_GEMM_PF_MB")) t.pf_mb = std::max(0, std::min(96, atoi(v)));
+    if (const char* v = getenv("SF_QKV_SPLITS")) t.qkv_splits = std::max(0, std::min(16, atoi(v)));
   });
   return t;
 }
@@ -991,7 +993,8 @@ struct TcPlan {
   int n_tiles, sub, n_groups, splits, kb_total, kb_per_split, acc_cols, double_buf, grid;
   int stage_budget, ctas_per_sm;
 };
-static TcPlan tc_plan(int n_out, int K, int mode, int inter, int rows_cap) {
+static TcPlan tc_plan(int n_out, int K, int kind, int inter, int rows_cap) {
+  const int mode = kind == EPI_SWIGLU ? 1 : 0;
   TcPlan pl{};
   pl.n_tiles = mode == 1 ? (inter + 63) / 64 : (n_out + kTileF - 1) / kTileF;
   pl.kb_total = (K + kBK - 1) / kBK;
@@ -1022,6 +1025,10 @@ static TcPlan tc_plan(int n_out, int K, int mode, int inter, int rows_cap) {
   // few tile groups: split K so that groups x splits fills the SMs (one pass of rows)
   if (rows_cap <= kMaxPassRows && pl.n_groups < sms / 2 && pl.n_groups <= kMaxCounterTiles)
     splits = std::max(1, std::min(sms / pl.n_groups, pl.kb_total / 4));
+  // (every split of a group must be resident at once: at most the SMs' CTA slots)
+  if (kind == EPI_QKV && tune.qkv_splits > 0 && splits > 1)
+    splits = std::max(1, std::min(std::min(tune.qkv_splits, pl.kb_total),
+                                  sms * pl.ctas_per_sm / std::max(1, pl.n_groups)));
   pl.kb_per_split = (pl.kb_total + splits - 1) / splits;
   pl.splits = (pl.kb_total + pl.kb_per_split - 1) / pl.kb_per_split;  // no empty split
   const int n_units = pl.n_groups * pl.splits;
@@ -1035,8 +1042,7 @@ static TcPlan tc_plan(int n_out, int K, int mode, int inter, int rows_cap) {
 WPrefetch gemm_prefetch_plan(const GemmArgs& a) {
   WPrefetch f{};
   if (a.dtype != BF16 || !a.w_tiled || a.W == nullptr) return f;
-  const int mode = a.epi.kind == EPI_SWIGLU ? 1 : 0;
-  const TcPlan pl = tc_plan(a.n_out, a.K, mode, a.epi.inter, a.rows_cap);
+  const TcPlan pl = tc_plan(a.n_out, a.K, a.epi.kind, a.epi.inter, a.rows_cap);
   const int64_t per_kb = static_cast<int64_t>(pl.n_groups) * pl.splits * pl.sub * kWBytes;
   const int64_t budget = static_cast<int64_t>(tc_tuning().pf_mb) << 20;
   const int npf = static_cast<int>(std::min<int64_t>(pl.kb_per_split, per_kb > 0 ? budget / per_kb : 0));
@@ -1055,8 +1061,7 @@ WPrefetch gemm_prefetch_plan(const GemmArgs& a) {
 static int wave_tail_tiles0(int n_out, int K, int kind, int rows_cap, int* splits1);
 
 size_t gemm_tc_ws_need(int rows_cap, int n_out, int K, int kind, int inter) {
-  const int mode = kind == EPI_SWIGLU ? 1 : 0;
-  const TcPlan pl = tc_plan(n_out, K, mode, inter, rows_cap);
+  const TcPlan pl = tc_plan(n_out, K, kind, inter, rows_cap);
   if (pl.splits <= 1) {
     int s1 = 0;
     const int tiles0 = wave_tail_tiles0(n_out, K, kind, rows_cap, &s1);
@@ -1076,7 +1081,7 @@ static cudaError_t make_phase(const GemmArgs& a, int* counters, TcParams* out, T
   const int mode = a.epi.kind == EPI_SWIGLU ? 1 : 0;
   const int inter = a.epi.inter;
   if (a.n_out % 8 != 0 || (mode == 1 && inter % 8 != 0)) return cudaErrorInvalidValue;
-  const TcPlan pl = tc_plan(a.n_out, a.K, mode, inter, a.rows_cap);
+  const TcPlan pl = tc_plan(a.n_out, a.K, a.epi.kind, inter, a.rows_cap);
   TcParams p{};
   p.n_out = a.n_out;
   p.K = a.K;
@@ -1288,13 +1293,13 @@ cudaError_t gemm_chain(const GemmArgs* g, int n, const PreNormArgs* const* norms
 // tiles of the full rounds (0: no tail split) and the tail phase's split count
 static int wave_tail_tiles0(int n_out, int K, int kind, int rows_cap, int* splits1) {
   if ((kind != EPI_LOGITS && kind != EPI_RAW) || rows_cap > kMaxPassRows) return 0;
-  const TcPlan pl = tc_plan(n_out, K, 0, 0, rows_cap);
+  const TcPlan pl = tc_plan(n_out, K, kind, 0, rows_cap);
   if (pl.splits > 1) return 0;
   const int n_units = pl.n_groups * pl.splits;
   const int rem = n_units % pl.grid;
   if (rem == 0 || rem * 4 > pl.grid) return 0;
   const int tiles0 = (n_units - rem) * pl.sub;
-  const TcPlan p1 = tc_plan(n_out - tiles0 * kTileF, K, 0, 0, rows_cap);
+  const TcPlan p1 = tc_plan(n_out - tiles0 * kTileF, K, kind, 0, rows_cap);
   if (p1.splits <= 1 || p1.n_groups * p1.splits > pl.grid) return 0;
   *splits1 = p1.splits;
   return tiles0;
@@ -1305,7 +1310,7 @@ static bool split_wave_tail(const GemmArgs& a, GemmArgs* g) {
   int s1 = 0;
   const int tiles0 = wave_tail_tiles0(a.n_out, a.K, a.epi.kind, a.rows_cap, &s1);
   if (tiles0 <= 0) return false;
-  const TcPlan pl = tc_plan(a.n_out, a.K, 0, 0, a.rows_cap);
+  const TcPlan pl = tc_plan(a.n_out, a.K, a.epi.kind, 0, a.rows_cap);
   const int n1 = a.n_out - tiles0 * kTileF;
   const size_t need = kGemmCounterBytes + static_cast<size_t>(s1) * a.rows_cap * n1 * 4;
   if (a.ws == nullptr || a.ws_bytes < need) return false;

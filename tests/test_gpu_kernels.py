@@ -162,6 +162,50 @@ def test_qkv_rope_scatter(name):
         assert_close(kv_buf[rows.cuda()].cpu(), kv_ref, dtype, f"layer {li} kv")
 
 
+def _rope_ref(x, cos, sin, pos):
+    """x [n, heads, hd] fp32; the rotate-half RoPE at block positions pos."""
+    c, s_ = cos[pos].float().unsqueeze(1), sin[pos].float().unsqueeze(1)
+    h = x.shape[-1] // 2
+    rot = torch.cat([-x[..., h:], x[..., :h]], -1)
+    return x * c + rot * s_
+
+
+@pytest.mark.parametrize("count", [1, 122, 128, 129, 256])
+def test_qkv_rope_scatter_7b_shape(count):
+    """The QKV GEMM at the Qwen2.5-7B shape (D = 3584 -> 4608 outputs), split over K and
+    with its k-steps spread over independent TMEM accumulators (four at <= 128 rows, two
+    above), against a torch fp32 GEMM + bias + RoPE + scatter on the same bf16 inputs."""
+    D, H, Hkv, hd, N, BN = 3584, 28, 4, 128, 32, 256
+    g = torch.Generator().manual_seed(11 + count)
+    n_out = (H + 2 * Hkv) * hd
+    xn = torch.randn(BN, D, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n_out, D, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n_out, generator=g) * 0.02).to(torch.bfloat16)
+    ang = torch.rand(N, hd // 2, generator=g) * 6.0
+    cos = torch.cat([ang.cos(), ang.cos()], -1).to(torch.bfloat16)
+    sin = torch.cat([ang.sin(), ang.sin()], -1).to(torch.bfloat16)
+    rows = torch.randperm(BN, generator=g)[:count].sort().values
+    q_buf = torch.zeros(BN + 1, H * hd, dtype=torch.bfloat16, device="cuda")
+    kv_buf = torch.zeros(BN + 1, 2 * Hkv * hd, dtype=torch.bfloat16, device="cuda")
+    cnt = torch.tensor([count], dtype=torch.int32, device="cuda")
+    err = K.fused_ln_qkv_rope_scatter(xn.cuda(), w.cuda(), b.cuda(), rows.cuda(), cnt, cos.cuda(),
+                                      sin.cuda(), q_buf, kv_buf, N, BN, H, Hkv, hd)
+    torch.cuda.synchronize()
+    K.raise_device_error(err)
+    y = xn[:count].float() @ w.float().t() + b.float()
+    pos = rows % N
+    q = _rope_ref(y[:, :H * hd].reshape(count, H, hd), cos, sin, pos).reshape(count, -1)
+    k = _rope_ref(y[:, H * hd:(H + Hkv) * hd].reshape(count, Hkv, hd), cos, sin, pos).reshape(count, -1)
+    v = y[:, (H + Hkv) * hd:]
+    assert_close(q_buf[rows.cuda()].cpu(), q, torch.bfloat16, f"q at {count} rows")
+    assert_close(kv_buf[rows.cuda()].cpu(), torch.cat([k, v], 1), torch.bfloat16, f"kv at {count} rows")
+    # rows that were not recomputed stay untouched
+    keep = torch.ones(BN + 1, dtype=torch.bool)
+    keep[rows] = False
+    keep[BN] = False                                  # the sink row of padded slots
+    assert not q_buf.cpu()[keep].any() and not kv_buf.cpu()[keep].any()
+
+
 # --------------------------------------------------------------------------- attention + merge
 @pytest.mark.parametrize("name", CASES)
 def test_attention_and_chain_correction(name):
