@@ -108,6 +108,91 @@ __device__ __forceinline__ void st8(void* base, int64_t i, const float* v) {
   if (Elt<T>::kVec == 4) store_vec<T>(reinterpret_cast<T*>(base) + i + 4, v + 4);
 }
 
+// The operands of a QKV output group that do not depend on the GEMM: the bias at the
+// group's features f and at its RoPE partner's fp, cos / sin at (n, f % hd) (q and k
+// features only) and, with `both`, at (n, fp % hd) for the partner's own group; bf16 x 8.
+struct QkvOps {
+  uint4 b, bp, c, s, cp, sp;
+  float qs;
+};
+__device__ __forceinline__ void qkv_ops_load(const EpiParams& e, int64_t row, int f, int fp,
+                                             bool both, QkvOps& o) {
+  using T = __nv_bfloat16;
+  const int n = static_cast<int>(row % e.N);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  const T* bias = reinterpret_cast<const T*>(e.bias);
+  o.b = bias ? *reinterpret_cast<const uint4*>(bias + f) : z;
+  o.bp = bias ? *reinterpret_cast<const uint4*>(bias + fp) : z;
+  o.c = o.s = o.cp = o.sp = z;
+  if (f < e.q_dim + e.kv_dim) {
+    const int64_t base = static_cast<int64_t>(n) * e.hd;
+    o.c = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(e.cos) + base + f % e.hd);
+    o.s = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(e.sin) + base + f % e.hd);
+    if (both) {
+      o.cp = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(e.cos) + base + fp % e.hd);
+      o.sp = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(e.sin) + base + fp % e.hd);
+    }
+  }
+  o.qs = (f < e.q_dim && e.q_scale) ? e.q_scale[n] : 1.0f;
+}
+__device__ __forceinline__ void bf16x8_get(const uint4& u, float* out) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+// QKV output group f0..f0+7 of activation row j (block row `row`): + bias, bf16, RoPE with
+// the partner values vp, q scale, scatter (q rows, the query-major q copy, k / v rows).
+__device__ __forceinline__ void qkv_emit8(const EpiParams& e, int j, int64_t row, int f0,
+                                          const float* v, const float* vp, const uint4& braw,
+                                          const uint4& bpraw, const uint4& craw,
+                                          const uint4& sraw, float qs_raw) {
+  using T = __nv_bfloat16;
+  float x[8], xp[8], o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { x[i] = v[i]; xp[i] = vp[i]; }
+  if (e.bias) {
+    float b[8], bp[8];
+    bf16x8_get(braw, b);
+    bf16x8_get(bpraw, bp);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { x[i] = __fadd_rn(x[i], b[i]); xp[i] = __fadd_rn(xp[i], bp[i]); }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { o[i] = Elt<T>::rnd(x[i]); xp[i] = Elt<T>::rnd(xp[i]); }
+  if (f0 < e.q_dim + e.kv_dim) {
+    const int d0 = f0 % e.hd;
+    float c[8], s[8];
+    bf16x8_get(craw, c);
+    bf16x8_get(sraw, s);
+    const bool first = d0 < (e.hd >> 1);
+    const float qs = (f0 < e.q_dim && e.q_scale) ? Elt<T>::rnd(qs_raw) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float rot = first ? -xp[i] : xp[i];
+      float r = Elt<T>::rnd(__fadd_rn(Elt<T>::rnd(__fmul_rn(o[i], c[i])),
+                                      Elt<T>::rnd(__fmul_rn(rot, s[i]))));
+      if (f0 < e.q_dim && e.q_scale) r = Elt<T>::rnd(__fmul_rn(r, qs));
+      o[i] = r;
+    }
+  }
+  if (f0 < e.q_dim) {
+    st8<T>(e.out, row * e.q_dim + f0, o);
+    if (e.q_comp) {   // query-major copy per kv head for the tensor-core attention
+      const int G = e.q_dim / e.kv_dim;
+      const int h = f0 / e.hd;
+      st8<T>(e.q_comp,
+             ((static_cast<int64_t>(h / G) * e.q_comp_rows + static_cast<int64_t>(j) * G +
+               h % G) * e.hd) + f0 % e.hd, o);
+    }
+  } else {
+    st8<T>(e.out2, row * (2 * e.kv_dim) + (f0 - e.q_dim), o);
+  }
+}
+
 // Epilogue of 8 consecutive tile-local weight rows l0..l0+7 for activation row j:
 // v = their accumulators, vp = the partner rows' (RoPE pair / SwiGLU up half).  The kind
 // is a template parameter: one kernel per epilogue keeps each kernel's code small (the
@@ -127,48 +212,9 @@ __device__ __forceinline__ void epi_group8(const TcParams& p, int tile, int j, i
       return;
     case EPI_QKV: {
       const int64_t row = e.rows[j];
-      const int n = static_cast<int>(row % e.N);
-      const int fp0 = f0 ^ (e.hd >> 1);
-      float x[8], xp[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) { x[i] = v[i]; xp[i] = vp[i]; }
-      if (e.bias) {
-        float b[8], bp[8];
-        ld8<T>(e.bias, f0, b);
-        ld8<T>(e.bias, fp0, bp);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { x[i] = __fadd_rn(x[i], b[i]); xp[i] = __fadd_rn(xp[i], bp[i]); }
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) { o[i] = Elt<T>::rnd(x[i]); xp[i] = Elt<T>::rnd(xp[i]); }
-      if (f0 < e.q_dim + e.kv_dim) {
-        const int d0 = f0 % e.hd;
-        float c[8], s[8];
-        ld8<T>(e.cos, static_cast<int64_t>(n) * e.hd + d0, c);
-        ld8<T>(e.sin, static_cast<int64_t>(n) * e.hd + d0, s);
-        const bool first = d0 < (e.hd >> 1);
-        const float qs = (f0 < e.q_dim && e.q_scale) ? Elt<T>::rnd(e.q_scale[n]) : 1.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float rot = first ? -xp[i] : xp[i];
-          float r = Elt<T>::rnd(__fadd_rn(Elt<T>::rnd(__fmul_rn(o[i], c[i])),
-                                          Elt<T>::rnd(__fmul_rn(rot, s[i]))));
-          if (f0 < e.q_dim && e.q_scale) r = Elt<T>::rnd(__fmul_rn(r, qs));
-          o[i] = r;
-        }
-      }
-      if (f0 < e.q_dim) {
-        st8<T>(e.out, row * e.q_dim + f0, o);
-        if (e.q_comp) {   // query-major copy per kv head for the tensor-core attention
-          const int G = e.q_dim / e.kv_dim;
-          const int h = f0 / e.hd;
-          st8<T>(e.q_comp,
-                 ((static_cast<int64_t>(h / G) * e.q_comp_rows + static_cast<int64_t>(j) * G +
-                   h % G) * e.hd) + f0 % e.hd, o);
-        }
-      } else {
-        st8<T>(e.out2, row * (2 * e.kv_dim) + (f0 - e.q_dim), o);
-      }
+      QkvOps ops;
+      qkv_ops_load(e, row, f0, f0 ^ (e.hd >> 1), false, ops);
+      qkv_emit8(e, j, row, f0, v, vp, ops.b, ops.bp, ops.c, ops.s, ops.qs);
       return;
     }
     case EPI_RESID: {
@@ -272,6 +318,45 @@ __device__ __forceinline__ void sum_splits8(const float* partial, int splits, in
     const float4 a1 = __ldcg(reinterpret_cast<const float4*>(q + 4));
     acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w;
     acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
+  }
+}
+
+// sum_splits8 of two groups at once (both groups' loads in flight together; each sum in
+// split order, as sum_splits8)
+__device__ __forceinline__ void sum_splits8_pair(const float* partial, int splits,
+                                                 int64_t split_stride, int64_t off_a,
+                                                 int64_t off_b, float* acc_a, float* acc_b) {
+  int s = 0;
+  for (; s + 2 <= splits; s += 2) {
+    float4 a[8];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float* qa = partial + (s + u) * split_stride + off_a;
+      const float* qb = partial + (s + u) * split_stride + off_b;
+      a[4 * u] = __ldcg(reinterpret_cast<const float4*>(qa));
+      a[4 * u + 1] = __ldcg(reinterpret_cast<const float4*>(qa + 4));
+      a[4 * u + 2] = __ldcg(reinterpret_cast<const float4*>(qb));
+      a[4 * u + 3] = __ldcg(reinterpret_cast<const float4*>(qb + 4));
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float va[8], vb[8];
+      vec_get(a[4 * u], va); vec_get(a[4 * u + 1], va + 4);
+      vec_get(a[4 * u + 2], vb); vec_get(a[4 * u + 3], vb + 4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { acc_a[i] += va[i]; acc_b[i] += vb[i]; }
+    }
+  }
+  for (; s < splits; ++s) {
+    float va[8], vb[8];
+    const float* qa = partial + s * split_stride + off_a;
+    const float* qb = partial + s * split_stride + off_b;
+    vec_get(__ldcg(reinterpret_cast<const float4*>(qa)), va);
+    vec_get(__ldcg(reinterpret_cast<const float4*>(qa + 4)), va + 4);
+    vec_get(__ldcg(reinterpret_cast<const float4*>(qb)), vb);
+    vec_get(__ldcg(reinterpret_cast<const float4*>(qb + 4)), vb + 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { acc_a[i] += va[i]; acc_b[i] += vb[i]; }
   }
 }
 
@@ -442,6 +527,15 @@ __device__ __forceinline__ void epi_unit(const TcParams& p, const EpiCtx& x, int
     // every split of this tile group publishes, then each reduces its slice of rows
     __threadfence();
     bool go = epi_vote_all(!*x.abort_flag);
+    // QKV: the block row of this thread's first item does not depend on the GEMM; loaded
+    // while the other splits finish, it leaves one round of loads after the wait (bias,
+    // cos / sin and the partials together) where each item chained several
+    int64_t pre_row = -1;
+    if constexpr (KIND == EPI_QKV) {
+      const int sl = (rows + p.splits - 1) / p.splits;
+      const int pr = split * sl + x.et / 8;
+      if (go && x.et / 8 < sl && pr < rows) pre_row = p.epi.rows[pr];
+    }
     if (x.et == 0 && go) {
       atomicAdd(&p.counters[2 * grp], 1);
       const uint64_t t0 = globaltimer();
@@ -474,6 +568,20 @@ __device__ __forceinline__ void epi_unit(const TcParams& p, const EpiCtx& x, int
       }
       const int tile = grp * p.sub + t;
       if (tile >= p.n_tiles) continue;
+      if constexpr (KIND == EPI_QKV) {
+        const int fa = tc_feature(p, tile, l0);
+        const int fb = tc_feature(p, tile, tc_partner_l<KIND>(p, l0));
+        if (item == x.et && t == 0 && pre_row >= 0 && fa >= 0 && fb >= 0 && fb != fa) {
+          QkvOps ops;
+          qkv_ops_load(p.epi, pre_row, fa, fb, true, ops);
+          float va[8] = {}, vb[8] = {};
+          const int64_t row_off = static_cast<int64_t>(r) * p.n_out;
+          sum_splits8_pair(p.partial, p.splits, split_stride, row_off + fa, row_off + fb, va, vb);
+          qkv_emit8(p.epi, r, pre_row, fa, va, vb, ops.b, ops.bp, ops.c, ops.s, ops.qs);
+          qkv_emit8(p.epi, r, pre_row, fb, vb, va, ops.bp, ops.b, ops.cp, ops.sp, ops.qs);
+          continue;
+        }
+      }
       const int fa = tc_feature(p, tile, l0);
       if (fa < 0) continue;
       const int lp = tc_partner_l<KIND>(p, l0);
