@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Workload ("Qwen2.5-7B shape"): 28 layers, hidden 3584,
+Workload (the benchmark's Qwen2.5-7B-shape configuration): 28 layers, hidden 3584,
 28 q / 4 kv heads, head_dim 128, MLP 18944, vocab 152064, bf16, random-init N(0, 0.02);
 one verify step = ``_batched_block_forward`` over the main block + 7 drafts (B1 = 8,
 N = 32) against a 1024-token prefix cache, delta = 0.1.  Draft rows follow the
@@ -398,7 +398,7 @@ def run_reference(args):
 
 
 def run_tp(args):
-    """The 14B configuration (SURVEY config C4): a Llama-style 14B-shape model, tensor
+    """The 14B tensor-parallel configuration: a Llama-style 14B-shape model, tensor
     parallel over all torchrun ranks (heads and the intermediate dimension sharded, o_proj
     and down all-reduced over NVLink), one verify stream, prefix 2048.  Strong scaling:
     the whole group serves one stream; value = verify steps/s of that stream."""

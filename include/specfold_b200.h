@@ -78,7 +78,9 @@ int sf_src_resolve(const int64_t* f, int64_t* src, int B1, int N, int* err, void
  * bytes of device memory (split-K partial sums and tile counters; tile counters must
  * be zero on the first use and are left zero by every call).                        */
 size_t sf_workspace_bytes(int BN, int D, int H, int Hkv, int hd, int I, int V);
-/* zero the tile counters inside a fresh workspace */
+/* zero the tile counters inside a fresh workspace.  A call that set a device error
+ * bit (SF_DEV_TIMEOUT in particular) may leave counters nonzero: run sf_workspace_init
+ * on the workspace again before reusing it after any device error. */
 int sf_workspace_init(void* ws, size_t ws_bytes, void* stream);
 
 /* fused_ln_qkv_rope_scatter_kernel (triton_kernels.py:29-87, launched at
@@ -144,6 +146,8 @@ int sf_fused_ffn_scatter(int dtype, const void* hp_all, const void* ln_w, const 
  * process exits.  It calls no cudaMalloc/cudaFree.
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress, that device current): make it before any stream capture.
+ *    The address is kept for the life of the process; after cudaDeviceReset on that
+ *    device it is stale, so do not call this entry point again after a reset.
  *  - Shapes needing more than 32 MiB of scratch return SF_ERR_ARG.
  *  - All calls share the array and it keeps the last call's contents (the split-K
  *    counters are cleared at each call); calls that overlap on the GPU race and must be

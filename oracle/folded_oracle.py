@@ -99,11 +99,18 @@ class Capture:
 
 
 def folded_forward(model, batched_input: torch.Tensor, past_key_values, delta: float,
-                   family: str = "fastdllm", capture: Optional[Capture] = None) -> torch.Tensor:
+                   family: str = "fastdllm", capture: Optional[Capture] = None,
+                   rec_override: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Logits of the folded B1 x N verify forward (Fast-dLLM: shifted, NLD: unshifted).
 
     ``model`` is the object the reference reads as ``self.model_executor.model``;
     ``past_key_values`` offers ``get_seq_length``, ``len`` and ``[li] -> (k, v)``.
+
+    ``rec_override`` ([L, B1, N] bool, optional) replaces the gate's decisions of the
+    draft branches with the given masks (the main branch always recomputes).  Parity
+    tests use it to re-run the oracle with the fold decisions a GPU run took where a
+    near-tie landed on the other side of the threshold, so that every branch can be
+    compared.  The recorded margins still describe the oracle's own inputs.
     """
     if family == "fastdllm":
         base = model.model
@@ -153,6 +160,8 @@ def folded_forward(model, batched_input: torch.Tensor, past_key_values, delta: f
                 rbar = torch.arange(N, device=dev)
             else:
                 rbar = gate_rows(x[0], rows[pj][0], delta)
+                if rec_override is not None:
+                    rbar = rec_override[li][i].to(dev).nonzero(as_tuple=True)[0]
                 if capture is not None:
                     capture.positions += N
                     capture.recomputed += int(rbar.numel())

@@ -51,18 +51,26 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         with open(stamp) as f:
             if f.read().strip() == digest:
                 return LIB
-    objs = []
     flags = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
                     "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
     if ptxas_verbose:
         flags += ["-Xptxas", "-v"]
-    for src in SOURCES:
-        obj = os.path.join(LIBDIR, src.replace(".cu", ".o"))
-        cmd = [nvcc(), "-c", os.path.join(CSRC, src), "-o", obj] + flags
-        if verbose:
+    objs = [os.path.join(LIBDIR, src.replace(".cu", ".o")) for src in SOURCES]
+    cmds = [[nvcc(), "-c", os.path.join(CSRC, src), "-o", obj] + flags
+            for src, obj in zip(SOURCES, objs)]
+    if verbose:
+        for cmd in cmds:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+    # translation units compile independently: one nvcc per core
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as pool:
+        for r in list(pool.map(lambda c: subprocess.run(c, capture_output=ptxas_verbose), cmds)):
+            if ptxas_verbose:
+                sys.stdout.write(r.stdout.decode() + r.stderr.decode())
+            if r.returncode != 0:
+                if not ptxas_verbose:
+                    raise subprocess.CalledProcessError(r.returncode, r.args)
+                raise subprocess.CalledProcessError(r.returncode, r.args, r.stdout, r.stderr)
     cmd = [nvcc(), "-shared", "-o", LIB] + objs + ARCH + ["-cudart", "static", "-Xcompiler", "-fPIC",
                                                           "-ldl"]
     if verbose:

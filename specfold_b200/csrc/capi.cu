@@ -692,7 +692,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
   const int qd = H * hd, kvd = Hkv * hd;
   // split-K tile counters (first 16 KB of the GEMM scratch) start at zero
   if (b.gemm_ws_bytes > 0) {
-    s = cuda_status(cudaMemsetAsync(b.gemm_ws, 0, std::min<size_t>(b.gemm_ws_bytes, 16384), st),
+    s = cuda_status(cudaMemsetAsync(b.gemm_ws, 0, std::min<size_t>(b.gemm_ws_bytes, kGemmCounterBytes), st),
                     "memset");
     if (s) return s;
   }

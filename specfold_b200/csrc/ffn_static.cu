@@ -15,7 +15,8 @@
 //    first call on the device.
 //  * The first call on each device resolves the array's device address with
 //    cudaGetSymbolAddress (with that device current); make that first call before any
-//    stream capture.
+//    stream capture.  The address is cached per device index for the life of the
+//    process, so it is stale after cudaDeviceReset: no calls after a reset.
 //  * All calls share the one array and it keeps the previous call's contents: the
 //    split-K counters are cleared at every call; calls that overlap on the GPU (two
 //    streams, or two host threads) race on the array and must be serialised by the caller.
@@ -35,7 +36,9 @@ using namespace sf;
 namespace {
 
 constexpr size_t kScratchBytes = 32ull << 20;
-constexpr size_t kCounterRegion = 16384;   // split-K tile counters at the start of the GEMM scratch
+// split-K tile counters at the start of the GEMM scratch: the same region every GEMM of
+// the library keeps there, so that clearing it here clears every counter a launch reads
+constexpr size_t kCounterRegion = kGemmCounterBytes;
 constexpr int kMaxDevices = 64;
 
 // In host code this name is only a stand-in: the kernels get the address that
@@ -74,6 +77,13 @@ extern "C" int sf_fused_ffn_scatter_static(int dtype, const void* hp_all, const 
       !w_up || !w_down || !rows || !count || !ffn_buf || D <= 0 || I <= 0 || D % 64 ||
       I % 64 || bucket < 1)
     return report_error(SF_ERR_ARG, "bad ffn arguments");
+  // the tensor-core GEMMs stream the weights through TMA, which needs 16-byte aligned
+  // bases; checked here, before anything is queued, as sf_fused_ffn_scatter does
+  if (dtype == SF_DTYPE_BF16) {
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (!a16(w_gate) || !a16(w_up) || !a16(w_down))
+      return report_error(SF_ERR_ARG, "ffn (static scratch): weights must be 16-byte aligned");
+  }
   const size_t es = dtype == SF_DTYPE_BF16 ? 2 : 4;
   // scratch layout: [GEMM scratch (counters first)] [xn bucket x D] [act bucket x I] [rstd]
   const size_t g_gu = gemm_ws_need(dtype, bucket, 2 * I, D, EPI_SWIGLU, I);

@@ -60,6 +60,11 @@ class FoldedVerifyB200:
         self._ws: Dict[Tuple, torch.Tensor] = {}
         self.last_rec_masks: Optional[torch.Tensor] = None
         self.record_masks = False
+        # True: every call returns logits of its own (a copy of the library's output
+        # buffer), which the decode loop may keep across calls -- it caches draft logits
+        # for later hits (fastdllm_v2_generation.py:640-643).  False: the returned tensor
+        # is the output buffer itself, valid until the next call with the same shapes.
+        self.copy_logits = True
 
     # -------------------------------------------------------------- reference API
     @property
@@ -274,7 +279,7 @@ class FoldedVerifyB200:
         st["args"].stream = stream.cuda_stream
         st["args"].delta = self.delta if delta is None else float(delta)
         _lib.check(lib.sf_folded_verify_forward(st["args"]), "folded verify forward")
-        logits = st["logits"].clone()
+        logits = st["logits"].clone() if self.copy_logits else st["logits"]
         rec = st["rec"].clone() if st["rec"] is not None else None
 
         # one sync for the fold counters and the device error word (the reference's :363)
@@ -454,12 +459,12 @@ class SpecFoldB200FastDLLMV2Generation(FoldedVerifyB200):
         (sf_sample_top_p_greedy).  The probabilities come back as the tokens'
         confidence broadcast over the vocabulary dimension (a stride-0 view of shape
         logits.shape): the loops only gather them at the sampled token (:348-351) and
-        slice positions (:615-616).  Temperature sampling keeps the reference's path."""
+        slice positions (:615-616).  There is no fallback to the reference's sampler:
+        temperature sampling, CPU logits and other dtypes raise NotImplementedError."""
         if temperature > 0 or not logits.is_cuda or logits.dtype not in (torch.bfloat16, torch.float32):
-            parent = super()
-            if hasattr(parent, "_sample_with_top_p"):
-                return parent._sample_with_top_p(logits, top_p=top_p, temperature=temperature)
-            raise NotImplementedError("the GPU sampler is greedy (temperature 0) on CUDA logits")
+            raise NotImplementedError("the GPU sampler is greedy (temperature 0) on CUDA bf16 / "
+                                      f"fp32 logits (got temperature {temperature}, "
+                                      f"{logits.dtype} on {logits.device})")
         tokens, conf = K.sample_top_p_greedy(logits, top_p)
         return tokens, conf.unsqueeze(-1).expand(*logits.shape)
 
@@ -476,11 +481,8 @@ class SpecFoldB200FastDLLMV2Generation(FoldedVerifyB200):
         if getattr(self, "calibration_graph", None) is None or mask_index is None:
             return []
         if not (x.is_cuda and p.is_cuda) or p.dtype not in (torch.bfloat16, torch.float32):
-            parent = super()
-            if hasattr(parent, "get_draft_blocks"):
-                return parent.get_draft_blocks(x, p, mask_index, start_pos, end_pos,
-                                               small_block_start, small_block_end, **kwargs)
-            raise NotImplementedError("GPU draft construction takes CUDA bf16 / fp32 logits")
+            raise NotImplementedError("GPU draft construction takes CUDA bf16 / fp32 logits "
+                                      f"(got {p.dtype} on {p.device})")
         if small_block_start is not None and small_block_end is not None:
             lo, hi = small_block_start, small_block_end
         else:
@@ -506,10 +508,8 @@ class SpecFoldB200NLDGeneration(FoldedVerifyB200):
         reference's softmax of logits.float()).  Dicts with 'state' and 'node'."""
         if not (x_block.is_cuda and logits_block.is_cuda) or \
                 logits_block.dtype not in (torch.bfloat16, torch.float32):
-            parent = super()
-            if hasattr(parent, "get_draft_blocks"):
-                return parent.get_draft_blocks(x_block, logits_block, mask_index)
-            raise NotImplementedError("GPU draft construction takes CUDA bf16 / fp32 logits")
+            raise NotImplementedError("GPU draft construction takes CUDA bf16 / fp32 logits "
+                                      f"(got {logits_block.dtype} on {logits_block.device})")
         nodes, drafts, valid = self._draft_states(x_block, logits_block, mask_index, 0, conf_fp32=True)
         return [{"state": drafts[k], "node": n} for k, n in enumerate(nodes) if valid[k]]
 

@@ -78,7 +78,16 @@ CASES = {
     "tiny_nld_bf16_inject": ("nld", "tiny", torch.bfloat16, 16, 0.1, "inject"),
     # configuration 0: one Qwen2.5-1.5B-shape layer, fp32, P = 256, delta 0.1
     "config0": ("fastdllm", "qwen1.5b-1layer", torch.float32, 256, 0.1, "inject"),
+    # NLD with a non-unit llama-4 query scale: original_max_position_embeddings is set to 8
+    # so that block positions [24, 56) get scale 1 + beta * log(1 + floor(pos / 8))
+    # (nld_folded.py:37-53); the reference's own fused class falls back to its PyTorch
+    # path for this case (nld_folded.py:275-278)
+    "tiny_nld_fp32_qscale": ("nld", "tiny", torch.float32, 24, 0.1, "tree+qscale"),
+    "tiny_nld_bf16_qscale": ("nld", "tiny", torch.bfloat16, 24, 0.1, "tree+qscale"),
 }
+
+# llama-4 query-scale parameters of the "+qscale" cases
+QSCALE_BETA, QSCALE_OMAX = 0.1, 8
 
 
 def build_case(name):
@@ -87,6 +96,11 @@ def build_case(name):
     model = syn.build_model(dims, family=family, dtype=dtype, seed=0)
     cache = syn.random_prefix_cache(dims, P, dtype=dtype, seed=1)
     B1, N = 8, 32
+    if kind.endswith("+qscale"):
+        kind = kind[:-len("+qscale")]
+        model.config.rope_parameters = dict(model.config.rope_parameters,
+                                            llama_4_scaling_beta=QSCALE_BETA,
+                                            original_max_position_embeddings=QSCALE_OMAX)
     if kind in ("tree", "chain"):
         ids = syn.tree_block_input(dims.vocab, N=N, edits_per_level=3 if kind == "tree" else 1,
                                    seed=2)
@@ -98,9 +112,12 @@ def build_case(name):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SPECFOLD_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SPECFOLD_REFERENCE"),
+                    help="checkout of the reference (or set SPECFOLD_REFERENCE)")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference or set SPECFOLD_REFERENCE")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     fd_cls, nd_cls = import_reference(args.reference)
     for name in (args.only or CASES):

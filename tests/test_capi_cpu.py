@@ -91,3 +91,24 @@ def test_preallocated_kv_cache_is_device_only():
         PreallocatedKVCache(2, 4, 128, 64, dtype=torch.bfloat16, device="cpu")
     with pytest.raises(ValueError):
         PreallocatedKVCache(0, 4, 128, 64, dtype=torch.bfloat16, device="cuda")
+
+
+def test_no_fallback_to_the_reference_sampler_or_drafts():
+    """The generator hooks never hand work to a CPU or reference path: temperature
+    sampling, CPU tensors and other dtypes raise before anything runs."""
+    from specfold_b200 import SpecFoldB200FastDLLMV2Generation, SpecFoldB200NLDGeneration
+    gen = SpecFoldB200FastDLLMV2Generation(model_executor=None)
+    logits = torch.zeros(1, 4, 16)
+    with pytest.raises(NotImplementedError):
+        gen._sample_with_top_p(logits, top_p=0.95, temperature=0.0)      # CPU logits
+    with pytest.raises(NotImplementedError):
+        gen._sample_with_top_p(logits, top_p=0.95, temperature=0.7)      # temperature
+    gen.calibration_graph = {"selected_nodes": [{"ij_set": [[0, 0]]}]}
+    with pytest.raises(NotImplementedError):
+        gen.get_draft_blocks(torch.zeros(8, dtype=torch.int64), torch.zeros(8, 16),
+                             torch.ones(8, dtype=torch.bool), 0, 8, 0, 8)
+    nld = SpecFoldB200NLDGeneration(model_executor=None)
+    nld.calibration_graph = gen.calibration_graph
+    with pytest.raises(NotImplementedError):
+        nld.get_draft_blocks(torch.zeros(8, dtype=torch.int64), torch.zeros(8, 16),
+                             torch.ones(8, dtype=torch.bool))

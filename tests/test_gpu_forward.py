@@ -98,6 +98,12 @@ EXTRA = {
     "mid_bf16_qwen_vocab": ("fastdllm", ModelDims(hidden=512, heads=4, kv_heads=2, head_dim=128,
                                                   inter=1408, layers=1, vocab=152064), 64, "tree"),
 }
+# long prefixes of the Llama-8B microbenchmark sweep (GQA group 4, RoPE theta 5e5): the
+# prefix attention caps its key splits at 16, so each split streams P / 16 keys
+_LONG = ModelDims(hidden=1024, heads=8, kv_heads=2, head_dim=128, inter=1024, layers=1,
+                  vocab=512, eps=1e-5, theta=5e5)
+for _p in (4096, 16384, 32768):
+    EXTRA[f"long_prefix_{_p // 1024}k"] = ("nld", _LONG, _p, "tree")
 
 
 @pytest.mark.parametrize("name", sorted(EXTRA))

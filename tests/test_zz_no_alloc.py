@@ -29,8 +29,9 @@ def _inputs(seed, dtype, BN=256, D=512, I=1408, count=122):
     return [t.cuda() for t in (hp, ln, wg, wu, wd, rows)] + [count]
 
 
-def _static_call(hp, ln, wg, wu, wd, rows, count, eps=1e-6):
+def _static_call(hp, ln, wg, wu, wd, rows, count, eps=1e-6, bucket=None):
     BN, D = hp.shape
+    bucket = BN if bucket is None else bucket
     I = wg.shape[0]
     ffn = torch.zeros(BN + 1, D, dtype=hp.dtype, device="cuda")
     cnt = torch.tensor([count], dtype=torch.int32, device="cuda")
@@ -38,7 +39,7 @@ def _static_call(hp, ln, wg, wu, wd, rows, count, eps=1e-6):
     lib = _lib.load()
     st = lib.sf_fused_ffn_scatter_static(
         K.dtype_code(hp), hp.data_ptr(), ln.data_ptr(), wg.data_ptr(), wu.data_ptr(),
-        wd.data_ptr(), rows.data_ptr(), cnt.data_ptr(), ffn.data_ptr(), BN, ctypes.c_float(eps),
+        wd.data_ptr(), rows.data_ptr(), cnt.data_ptr(), ffn.data_ptr(), bucket, ctypes.c_float(eps),
         D, I, err.data_ptr(), torch.cuda.current_stream().cuda_stream)
     _lib.check(st, "sf_fused_ffn_scatter_static")
     torch.cuda.synchronize()
@@ -46,11 +47,12 @@ def _static_call(hp, ln, wg, wu, wd, rows, count, eps=1e-6):
     return ffn
 
 
-def _scratch_call(hp, ln, wg, wu, wd, rows, count, eps=1e-6):
+def _scratch_call(hp, ln, wg, wu, wd, rows, count, eps=1e-6, bucket=None):
     BN, D = hp.shape
+    bucket = BN if bucket is None else bucket
     ffn = torch.zeros(BN + 1, D, dtype=hp.dtype, device="cuda")
     cnt = torch.tensor([count], dtype=torch.int32, device="cuda")
-    out = K.fused_ffn_scatter(hp, ln, wg, wu, wd, rows, cnt, ffn, BN, eps)
+    out = K.fused_ffn_scatter(hp, ln, wg, wu, wd, rows, cnt, ffn, bucket, eps)
     torch.cuda.synchronize()
     K.raise_device_error(out["err"])
     return ffn
@@ -67,6 +69,18 @@ def test_static_scratch_matches_allocating_entry_point(dtype):
         untouched = torch.ones(got.shape[0], dtype=torch.bool, device="cuda")
         untouched[rows] = False
         assert got[untouched].abs().max().item() == 0.0
+
+
+def test_static_scratch_7b_shape():
+    """The Qwen2.5-7B FFN (D = 3584, I = 18944) at a 160-row bucket, which fits the fixed
+    scratch with the GEMMs split over K (gate/up and down both run several splits whose
+    fp32 partials and tile counters live in the static array), two calls in a row."""
+    for seed, count in ((3, 122), (4, 160)):
+        args = _inputs(seed, torch.bfloat16, BN=256, D=3584, I=18944, count=count)
+        hp, ln, wg, wu, wd, rows, cnt = args
+        got = _static_call(hp, ln, wg, wu, wd, rows, cnt, bucket=160)
+        want = _scratch_call(hp, ln, wg, wu, wd, rows, cnt, bucket=160)
+        assert_close(got[rows], want[rows], torch.bfloat16, f"7B static-scratch ffn (seed {seed})")
 
 
 def test_static_scratch_rejects_oversized_shapes():
