@@ -90,9 +90,54 @@ def build_workload(device, dtype=torch.bfloat16, layers=None, seed=0):
     cache = syn.random_prefix_cache(dims, P_PREFIX, dtype=dtype, seed=seed + 1, device=str(device))
     hidden = syn.config0_hidden(dims, B1, N, dtype=dtype, seed=seed + 3,
                                 frac_recompute=FRAC_RECOMPUTE)
+    model.token_embedding = model.model.embed_tokens      # kept for the decode leg
     syn.inject_hidden(model, hidden.to(device))
     ids = torch.zeros(B1, N, dtype=torch.int64)
     return dims, model, cache, ids
+
+
+# decode leg: the end-to-end configuration of the 7B shape -- 1024-token random prompts,
+# 512 generated tokens each, block length 32, draft graph B=7 D=8 S=3, delta 0.1,
+# threshold 0.9 -- on random-init weights with the seeded per-position logit bias that
+# stands in for a trained model's confidence (specfold_b200.synthetic.decode_bias)
+DECODE_PROMPT, DECODE_NEW = 1024, 512
+MASK_ID, STOP_ID = 151665, 151645
+
+
+def decode_leg(gen, model, dims, streams, rank, device):
+    """Decode `streams` independent sequences on this rank; returns the stats of the
+    timed ones (after one short warm-up sequence) and their device time in ms."""
+    from specfold_b200 import synthetic as syn
+    from specfold_b200.decode import FastDLLMV2Decoder
+    model.model.embed_tokens = model.token_embedding
+    total = DECODE_PROMPT + DECODE_NEW + 2 * N
+    graph = syn.synthetic_draft_graph()
+
+    def decoder(seed, new):
+        bias = syn.decode_bias(dims.vocab, DECODE_PROMPT, total, seed=1000 + seed,
+                               frac_strong=0.6, exclude=(MASK_ID, STOP_ID))
+        return FastDLLMV2Decoder(gen, block_length=N, small_block_size=8, threshold=0.9,
+                                 top_p=0.95, max_new_tokens=new, mask_id=MASK_ID,
+                                 stop_token=STOP_ID, calibration_graph=graph, logit_bias=bias,
+                                 capacity=total)
+
+    def prompt(seed):
+        return syn.decode_prompt(dims.vocab, DECODE_PROMPT, seed=2000 + seed,
+                                 exclude=(MASK_ID, STOP_ID)).tolist()
+
+    decoder(-1, 2 * N).generate_with_draft_speculation(prompt(-1), device=device)   # warm-up
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    runs = []
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for k in range(streams):
+        seed = rank * 1000 + k
+        _, st = decoder(seed, DECODE_NEW).generate_with_draft_speculation(prompt(seed), device=device)
+        runs.append(st)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    return runs, e0.elapsed_time(e1)
 
 
 def profiled_traffic(kind):
@@ -253,8 +298,36 @@ def run_b200(args):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
+    # ---- decode tok/s: whole sequences through the decode loop (prefill, verify steps,
+    # draft construction, sampling, block commits), device-timed, max over ranks
+    decode = None
+    dec_ms = 0.0
+    if args.decode_streams > 0:
+        barrier()
+        runs, dec_ms = decode_leg(gen, model, dims, args.decode_streams, rank, dev)
+        barrier()
     # ---- max over ranks
-    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dev)
+    ms, e2e_ms, dec_ms = max_over_ranks([ms, e2e_ms, dec_ms], dev)
+    if args.decode_streams > 0:
+        tok = sum(r["tokens_generated"] for r in runs)
+        calls = sum(r["model_calls"] for r in runs)
+        verify = sum(sum(1 for k, _ in r["steps"] if k == "forward") for r in runs)
+        hits = sum(r["draft_hits"] for r in runs)
+        fr = [r["fold_ratio"] for r in runs]
+        decode = {"tok_s": round(ws * tok / (dec_ms / 1e3), 2), "unit": "tok/s",
+                  "streams": ws * args.decode_streams, "prompt": DECODE_PROMPT,
+                  "new_tokens": DECODE_NEW, "tokens_per_stream": tok / len(runs),
+                  "ms_per_stream": round(dec_ms / len(runs), 2),
+                  "model_calls_per_stream": calls / len(runs),
+                  "verify_calls_per_stream": verify / len(runs),
+                  "draft_hits_per_stream": hits / len(runs),
+                  "tokens_per_verify_call": round(tok / max(verify, 1), 3),
+                  "fold_ratio": round(sum(fr) / len(fr), 4),
+                  "timing": "CUDA events around whole sequences on the launching stream "
+                            "(the loop synchronises every step), max over ranks",
+                  "workload": "1024-token random prompt, 512 new tokens, block 32, small "
+                              "block 8, graph B=7 D=8 S=3, delta 0.1, threshold 0.9, seeded "
+                              "per-position logit bias (60% strong)"}
     step_ms = ms / args.steps
     value = weak_scaling_value(ws, args.steps, ms)
     e2e_value = weak_scaling_value(ws, args.steps, e2e_ms)
@@ -303,6 +376,7 @@ def run_b200(args):
                    "recomputed_rows_per_layer": round(recomputed_rows, 1),
                    "parallelism": f"dp{ws} (independent streams, no collectives)",
                    "l2": "inputs larger than L2 (15 GB of weights streamed per step)"},
+        "decode": decode,
         "e2e": {"value": round(e2e_value, 4), "unit": UNIT,
                 "ms_per_step": round(e2e_ms / args.steps, 4),
                 "h2d_bytes_per_step": B1 * N * 8, "d2h_bytes_per_step": B1 * N * 8},
@@ -479,6 +553,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-streams", type=int, default=2,
+                    help="sequences each rank decodes for the decode tok/s figure (0: skip)")
     ap.add_argument("--tp", action="store_true",
                     help="the 14B tensor-parallel configuration over all ranks instead")
     args = ap.parse_args()

@@ -262,6 +262,20 @@ typedef struct sf_verify_args {
    * tp_comm comes from sf_tp_comm_init; o_proj and down are all-reduced in fp32. */
   void* tp_comm;
   int tp_size;
+  /* Decode-loop support (both optional; zero / NULL = off).
+   * P_dev: device int32 holding the prefix length actually used, read when the
+   *   launches run (0 <= *P_dev <= P; a larger value sets SF_DEV_INDEX and is clamped).
+   *   P then only bounds it: it sizes the grids and the workspace, and the prefix heads
+   *   must hold kv_head_stride >= P * hd elements.  The launches no longer depend on the
+   *   prefix length, so the captured graph of one argument set serves every block of a
+   *   decode.  cos / sin (and q_scale) must hold the rows of positions [*P_dev, +N).
+   * commit: the block commit forward (B1 == 1): every layer also writes its block rows'
+   *   keys (after RoPE) and values into prefix_k / prefix_v at positions [P', P' + N),
+   *   P' = *P_dev or P -- the append of the reference's cache update
+   *   (fastdllm_v2_generation.py:562-568 -> DynamicCache.update); the prefix tensors are
+   *   then written, and kv_head_stride must be >= (P + N) * hd. */
+  const int32_t* P_dev;
+  int commit;
 } sf_verify_args;
 
 /* Tensor-parallel communicator (NCCL, loaded at run time).  Rank 0 calls

@@ -100,8 +100,11 @@ class Capture:
 
 def folded_forward(model, batched_input: torch.Tensor, past_key_values, delta: float,
                    family: str = "fastdllm", capture: Optional[Capture] = None,
-                   rec_override: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Logits of the folded B1 x N verify forward (Fast-dLLM: shifted, NLD: unshifted).
+                   rec_override: Optional[torch.Tensor] = None,
+                   shift: Optional[bool] = None) -> torch.Tensor:
+    """Logits of the folded B1 x N verify forward (Fast-dLLM: shifted, NLD: unshifted;
+    ``shift=False`` returns the model's unshifted Fast-dLLM logits, as its executor
+    forward does).
 
     ``model`` is the object the reference reads as ``self.model_executor.model``;
     ``past_key_values`` offers ``get_seq_length``, ``len`` and ``[li] -> (k, v)``.
@@ -271,6 +274,8 @@ def folded_forward(model, batched_input: torch.Tensor, past_key_values, delta: f
     final = base.norm(torch.cat(rows, dim=0))
     if family == "fastdllm":
         logits = model.lm_head(final)
+        if shift is False:
+            return logits
         return torch.cat([logits[:, :1, :], logits[:, :-1, :]], dim=1)   # generation.py:121-126
     return model.diffusion_head(final)
 

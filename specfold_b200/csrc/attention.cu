@@ -11,6 +11,8 @@
 //   in-block keys are added here.  On the fp32 path it covers every key.
 //
 // kv_append_kernel: cache[h, P + t, :] = new[h, t, :] with 16-byte vectors.
+// kv_commit_kernel: the same append from the forward's own kv_buf (branch 0's rows), at a
+//   prefix length read on the device (the block commit forward of a decode loop).
 //
 // The chain-correction merge of the folded rows lives in merge.cu.
 #include "sf_kernels.cuh"
@@ -41,6 +43,7 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, const floa
   if (r < 0 || r >= BN) { flag_error(p.err, SF_DEV_ERR_INDEX); return; }
   const int64_t b = r / p.N;
   const int G = p.H / p.Hkv;
+  const int P = prefix_len(p.P_dev, p.P, p.err);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qd = p.H * HD, kvd = 2 * p.Hkv * HD;
   const T* qb = reinterpret_cast<const T*>(p.q_buf);
@@ -89,15 +92,15 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, const floa
       }
     }
   }
-  const int total = p.P + p.N;
-  const int key_begin = part_O != nullptr ? p.P : 0;
+  const int total = P + p.N;
+  const int key_begin = part_O != nullptr ? P : 0;
   for (int k0 = key_begin; k0 < total; k0 += kAttnKeys) {
     __syncthreads();
     if (threadIdx.x < kAttnKeys) {
       const int key = k0 + threadIdx.x;
       int64_t kr = -1;
-      if (key >= p.P && key < total) {
-        const int j = key - p.P;
+      if (key >= P && key < total) {
+        const int j = key - P;
         int64_t s = p.src[b * p.N + j];
         if (s < 0 || s >= p.B1) { flag_error(p.err, SF_DEV_ERR_INDEX); s = 0; }
         kr = s * p.N + j;
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, const floa
       const int idx = threadIdx.x + 128 * u;
       const int t = idx / VPR, d0 = (idx % VPR) * V;
       const int key = k0 + t;
-      if (key < p.P) {
+      if (key < P) {
         const int64_t o = kvh * p.kv_head_stride + static_cast<int64_t>(key) * HD + d0;
         load_vec<T>(pk + o, kv[u]);
         load_vec<T>(pv + o, vv[u]);
@@ -246,8 +249,9 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
   }
   __syncthreads();
 
-  const int key_begin = part_O != nullptr ? p.P : 0;
-  const int total = p.P + p.N;
+  const int P = prefix_len(p.P_dev, p.P, p.err);
+  const int key_begin = part_O != nullptr ? P : 0;
+  const int total = P + p.N;
   float kv[TILE_VEC][V], vv[TILE_VEC][V];
   // keys [k0, k0 + 32) into registers: prefix cache, then branch b's block keys
   auto load_tile = [&](int k0) {
@@ -256,12 +260,12 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
       const int idx = threadIdx.x + 256 * u;
       const int t = idx / VPR, d0 = (idx % VPR) * V;
       const int key = k0 + t;
-      if (t < kAttnKeys && key < p.P) {
+      if (t < kAttnKeys && key < P) {
         const int64_t o = kvh * p.kv_head_stride + static_cast<int64_t>(key) * HD + d0;
         load_vec<T>(pk + o, kv[u]);
         load_vec<T>(pv + o, vv[u]);
       } else if (t < kAttnKeys && key < total) {
-        const int j = key - p.P;
+        const int j = key - P;
         const int64_t o = (static_cast<int64_t>(s_src[j]) * p.N + j) * kvd;
         load_vec<T>(kvb + o + kvh * HD + d0, kv[u]);
         load_vec<T>(kvb + o + (p.Hkv + kvh) * HD + d0, vv[u]);
@@ -441,6 +445,30 @@ __global__ void kv_append_kernel(T* ck, T* cv, int64_t cs, const T* nk, const T*
   }
 }
 
+// cache[h, P' + n, :] = kv_buf[n][(h | Hkv + h) * hd : ...] for the block's N rows of
+// branch 0, P' read on the device: the commit forward's append of the committed block
+template <typename T>
+__global__ void kv_commit_kernel(const T* kvb, T* ck, T* cv, int64_t cs, const int32_t* P_dev,
+                                 int P_max, int N, int Hkv, int hd, int* err) {
+  constexpr int V = Elt<T>::kVec;
+  const int P = prefix_len(P_dev, P_max, err);
+  const int vecs_row = hd / V;
+  const int64_t per_head = static_cast<int64_t>(N) * vecs_row;
+  const int64_t total = static_cast<int64_t>(Hkv) * per_head;
+  const int64_t kvd = 2LL * Hkv * hd;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int h = static_cast<int>(i / per_head);
+    const int rem = static_cast<int>(i % per_head);
+    const int n = rem / vecs_row, d0 = (rem % vecs_row) * V;
+    const int64_t src = n * kvd + static_cast<int64_t>(h) * hd + d0;
+    const int64_t dst = h * cs + static_cast<int64_t>(P + n) * hd + d0;
+    *reinterpret_cast<uint4*>(ck + dst) = *reinterpret_cast<const uint4*>(kvb + src);
+    *reinterpret_cast<uint4*>(cv + dst) =
+        *reinterpret_cast<const uint4*>(kvb + src + static_cast<int64_t>(Hkv) * hd);
+  }
+}
+
 // ------------------------------------------------------------------------ launchers
 template <typename T>
 static cudaError_t attn_t(const AttnParams& p, const float* part_O, const float* part_ml,
@@ -534,6 +562,24 @@ cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, co
     kv_append_kernel<float><<<blocks, 256, 0, st>>>(
         static_cast<float*>(ck), static_cast<float*>(cv), c_stride, static_cast<const float*>(nk),
         static_cast<const float*>(nv), n_stride, Hkv, hd, P, n);
+  return launched();
+}
+
+cudaError_t launch_kv_commit(int dtype, const void* kv_buf, void* ck, void* cv, int64_t c_stride,
+                             const int32_t* P_dev, int P, int N, int Hkv, int hd, int* err,
+                             cudaStream_t st) {
+  const int vec = dtype == BF16 ? 8 : 4;
+  if (hd % vec != 0 || N <= 0) return cudaErrorInvalidValue;
+  const int64_t total = static_cast<int64_t>(Hkv) * N * hd / vec;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 592));
+  if (dtype == BF16)
+    kv_commit_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(kv_buf), static_cast<__nv_bfloat16*>(ck),
+        static_cast<__nv_bfloat16*>(cv), c_stride, P_dev, P, N, Hkv, hd, err);
+  else
+    kv_commit_kernel<float><<<blocks, 256, 0, st>>>(
+        static_cast<const float*>(kv_buf), static_cast<float*>(ck), static_cast<float*>(cv),
+        c_stride, P_dev, P, N, Hkv, hd, err);
   return launched();
 }
 

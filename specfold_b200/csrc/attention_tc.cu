@@ -40,7 +40,21 @@ struct AttnTcParams {
   const int64_t* rows;
   int part_rows;
   int* err;
+  // device prefix length (nullptr: P).  P is then the bound the grid was sized for
+  // (splits = kv_splits(P)); the kernel derives the split layout of the actual length the
+  // way the host does, and the splits beyond it write empty partials (m = -inf, l = 0).
+  const int32_t* P_dev;
 };
+
+// key splits of a prefix of P keys: at least kKeysPerSplit keys each, at most kMaxKvSplits
+__host__ __device__ __forceinline__ int kv_splits_of(int P) {
+  if (P <= 0) return 0;
+  const int s = (P + kKeysPerSplit - 1) / kKeysPerSplit;
+  return s < 1 ? 1 : (s > kMaxKvSplits ? kMaxKvSplits : s);
+}
+__host__ __device__ __forceinline__ int keys_per_split_of(int P, int S) {
+  return S > 0 ? ((P + S - 1) / S + kKB - 1) / kKB * kKB : 0;
+}
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -102,8 +116,13 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   const int Mq = count * p.G;
   const int q0 = qt * kQT;
   if (q0 >= Mq) return;                        // uniform per CTA
-  const int k_begin = split * p.keys_per_split;
-  const int k_end = min(p.P, k_begin + p.keys_per_split);
+  int P = p.P, kps = p.keys_per_split;
+  if (p.P_dev != nullptr) {
+    P = prefix_len(p.P_dev, p.P, p.err);
+    kps = keys_per_split_of(P, kv_splits_of(P));
+  }
+  const int k_begin = split * kps;
+  const int k_end = min(P, k_begin + kps);
   const int nb = k_end > k_begin ? (k_end - k_begin + kKB - 1) / kKB : 0;
 
   if (threadIdx.x == 0) {
@@ -349,10 +368,7 @@ static bool att_tmap(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t co
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static int kv_splits(int P) {
-  if (P <= 0) return 0;
-  return std::max(1, std::min(kMaxKvSplits, (P + kKeysPerSplit - 1) / kKeysPerSplit));
-}
+static int kv_splits(int P) { return kv_splits_of(P); }
 
 static size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
@@ -412,7 +428,8 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
   p.P = a.P;
   p.kv_rows = static_cast<int>(a.kv_head_stride / HD);
   p.splits = S;
-  p.keys_per_split = ((a.P + S - 1) / S + kKB - 1) / kKB * kKB;
+  p.keys_per_split = keys_per_split_of(a.P, S);
+  p.P_dev = a.P_dev;
   p.Hkv = a.Hkv;
   p.scale = a.scale;
   p.part_rows = std::max(a.bucket, rows_total) * G;

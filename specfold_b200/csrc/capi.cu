@@ -647,6 +647,9 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     return fail(SF_ERR_ARG, "prefix length / stride mismatch");
   if (a->tp_size > 1 && (a->tp_comm == nullptr || D % 4 != 0))
     return fail(SF_ERR_ARG, "tensor parallel forward needs a communicator (sf_tp_comm_init)");
+  if (a->commit && (B1 != 1 || a->kv_head_stride < static_cast<int64_t>(a->P + N) * hd ||
+                    hd % 8 != 0))
+    return fail(SF_ERR_ARG, "commit forward needs B1 == 1 and kv_head_stride >= (P + N) * hd");
   FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket, a->P);
   if (b.total > a->ws_bytes)
     return fail(SF_ERR_WORKSPACE, "workspace %zu < %zu bytes", a->ws_bytes, b.total);
@@ -654,7 +657,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     const sf_layer& ly = a->layers[li];
     if (!ly.w_qkv || !ly.ln1_w || !ly.w_o || !ly.ln2_w || !ly.w_gate ||
         (!ly.w_up && !a->weights_tiled) || !ly.w_down ||
-        (a->P > 0 && (!ly.prefix_k || !ly.prefix_v)))
+        ((a->P > 0 || a->commit) && (!ly.prefix_k || !ly.prefix_v)))
       return fail(SF_ERR_ARG, "layer %d: null weight", li);
   }
   if (g_prof.on || !graphs_enabled()) return forward_launches(a, b, S(a->stream));
@@ -799,10 +802,20 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     at.scratch = b.attn_ws;
     at.scratch_bytes = b.attn_ws_bytes;
     at.rec = rec;
+    at.P_dev = a->P_dev;
     // every row: recomputed rows attend with their own query, folded rows are rebuilt
     // from their recomputing ancestor's query and retained prefix state
     if ((s = timed(K_ATTN, st, [&] { return cuda_status(launch_attention_rows(dtype, at, st), "attention"); })))
       return s;
+    if (a->commit) {
+      // the committed block's keys and values join the prefix cache (its rows [P', P' + N)
+      // are not read by this layer's attention, which covers [0, P'))
+      if ((s = cuda_status(launch_kv_commit(dtype, b.kv_buf, const_cast<void*>(ly.prefix_k),
+                                            const_cast<void*>(ly.prefix_v), a->kv_head_stride,
+                                            a->P_dev, a->P, N, Hkv, hd, a->err, st),
+                           "kv commit")))
+        return s;
+    }
 
     GemmArgs o{};
     o.dtype = dtype;

@@ -256,7 +256,22 @@ struct AttnParams {
   const void* q_comp;
   void* scratch;
   size_t scratch_bytes;
+  // prefix length read on the device when the kernel runs (decode loops: one captured
+  // launch serves every prefix length); nullptr = P.  P then bounds it and sizes the grid.
+  const int32_t* P_dev;
 };
+
+// The prefix length a kernel attends to: *P_dev when given, clamped to the bound P the
+// launch was sized for (a larger value flags SF_DEV_ERR_INDEX and is clamped).
+__device__ __forceinline__ int prefix_len(const int32_t* P_dev, int P, int* err) {
+  if (P_dev == nullptr) return P;
+  const int v = *P_dev;
+  if (v < 0 || v > P) {
+    flag_error(err, SF_DEV_ERR_INDEX);
+    return v < 0 ? 0 : P;
+  }
+  return v;
+}
 // rows_total > 0: room for partials indexed by flat block row (launch_attention_rows)
 size_t attn_scratch_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P,
                           bool need_q_comp, int rows_total = 0);
@@ -306,6 +321,11 @@ cudaError_t launch_scatter_rows(int dtype, const float* sum, const int64_t* rows
                                 const int32_t* count, int n, int D, int64_t n_out_rows, void* out,
                                 int* err, cudaStream_t st);
 
+// Block commit inside the forward: the first N rows of kv_buf (branch 0's keys and values)
+// appended to the prefix cache at positions [P', P' + N), P' = prefix_len(P_dev, P).
+cudaError_t launch_kv_commit(int dtype, const void* kv_buf, void* ck, void* cv, int64_t c_stride,
+                             const int32_t* P_dev, int P, int N, int Hkv, int hd, int* err,
+                             cudaStream_t st);
 cudaError_t launch_kv_append(int dtype, void* ck, void* cv, int64_t c_stride, const void* nk,
                              const void* nv, int64_t n_stride, int Hkv, int hd, int P, int n,
                              cudaStream_t st);

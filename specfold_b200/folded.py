@@ -60,6 +60,10 @@ class FoldedVerifyB200:
         self._ws: Dict[Tuple, torch.Tensor] = {}
         self.last_rec_masks: Optional[torch.Tensor] = None
         self.record_masks = False
+        # True: the fold counters and the device error word of a call are read at the next
+        # settle_stats() (or the next call with the same configuration) instead of a host
+        # sync at the end of every call; used by decode loops, which synchronise anyway
+        self.defer_stats = False
         # True: every call returns logits of its own (a copy of the library's output
         # buffer), which the decode loop may keep across calls -- it caches draft logits
         # for later hits (fastdllm_v2_generation.py:640-643).  False: the returned tensor
@@ -223,7 +227,7 @@ class FoldedVerifyB200:
         B1, N = batched_input.shape
         bucket = B1 * N if self.fold_bucket is None else max(1, min(self.fold_bucket, B1 * N))
         logits, stats = self._run(batched_input, past_key_values, bucket)
-        if stats["max_count"] > bucket:
+        if stats["max_count"] is not None and stats["max_count"] > bucket:
             # the reference re-runs its PyTorch path on overflow (fastdllm_v2_folded.py:367-369);
             # here the same kernels run again with room for every row
             logger.warning("SpecFold bucket overflow (%d > %d); re-running with bucket %d",
@@ -250,7 +254,29 @@ class FoldedVerifyB200:
         logits, _ = self._run(batched_input, past_key_values, B1 * N, count_stats=False, delta=-1.0)
         return logits
 
-    def _run(self, batched_input, past_key_values, bucket, count_stats=True, delta=None):
+    @torch.no_grad()
+    def commit_block_forward(self, block: torch.Tensor, cache) -> torch.Tensor:
+        """The block commit forward of the decoding loops on the same kernels: the dense
+        forward of one block [1, N] against the running prefix with every layer's keys
+        and values of the block appended to ``cache`` (a PreallocatedKVCache) at
+        positions [P, P + N) -- the executor call with update_past_key_values=True
+        (fastdllm_v2_generation.py:562-568; nld_generation.py:283-289), which the
+        reference runs as the model's dense forward plus DynamicCache.update.  Returns
+        the model's unshifted logits [1, N, V] (the loop reads the last position's)."""
+        from .kv_cache import PreallocatedKVCache
+        if not isinstance(cache, PreallocatedKVCache):
+            raise TypeError("the commit forward appends to a PreallocatedKVCache")
+        if block.dim() != 2 or block.shape[0] != 1:
+            raise ValueError(f"the commit forward takes one block [1, N], got {tuple(block.shape)}")
+        N = block.shape[1]
+        cache.reserve(N)
+        logits, _ = self._run(block, cache, N, count_stats=False, delta=-1.0, commit=True,
+                              shift=False)
+        cache.advance(N)
+        return logits
+
+    def _run(self, batched_input, past_key_values, bucket, count_stats=True, delta=None,
+             commit=False, shift=None):
         lib = _lib.load()
         m_ = self.model_executor.model
         base = self._base()
@@ -265,8 +291,20 @@ class FoldedVerifyB200:
         P = int(past_key_values.get_seq_length()) if past_key_values is not None else 0
         stream = torch.cuda.current_stream(dev)
         hidden = base.embed_tokens(batched_input)
-        st = self._static_state(batched_input, past_key_values, hidden.dtype, P, bucket)
+        shift = (self.family == "fastdllm") if shift is None else bool(shift)
+        st = self._static_state(batched_input, past_key_values, hidden.dtype, P, bucket,
+                                commit=commit, shift=shift)
         L = st["L"]
+        if st["P_dev"] is not None:
+            # one state (and captured graph) for every prefix length of the cache: the
+            # length and its RoPE rows go to the device, the launches stay the same
+            if P + N > st["cap"]:
+                raise ValueError(f"prefix {P} + block {N} exceeds the cache capacity {st['cap']}")
+            st["P_dev"].fill_(P)
+            st["cos"].copy_(st["cos_all"][P:P + N])
+            st["sin"].copy_(st["sin_all"][P:P + N])
+            if st["q_scale"] is not None:
+                st["q_scale"].copy_(st["q_scale_all"][P:P + N])
 
         # per call: parent map on the device (the reference's :263-265 host round trip),
         # embeddings into the fixed input buffer, then the forward (a CUDA graph replay
@@ -282,8 +320,20 @@ class FoldedVerifyB200:
         logits = st["logits"].clone() if self.copy_logits else st["logits"]
         rec = st["rec"].clone() if st["rec"] is not None else None
 
-        # one sync for the fold counters and the device error word (the reference's :363)
+        if rec is not None:
+            self.last_rec_masks = rec.view(L, B1, N)
         host = st["host_slab"]
+        if self.defer_stats and bucket >= BN:
+            # decode loops: no overflow is possible (every row fits the bucket), so the fold
+            # counters and the error word are read at the caller's next synchronisation
+            # (settle_stats) instead of a sync of their own per call
+            self._settle(st)
+            host.copy_(st["slab"], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            st["pending"] = (ev, count_stats, B1, N, L)
+            return logits, {"max_count": None, "sum_count": None}
+        # one sync for the fold counters and the device error word (the reference's :363)
         host.copy_(st["slab"], non_blocking=True)
         stream.synchronize()
         counts = host[:L].tolist()
@@ -292,17 +342,48 @@ class FoldedVerifyB200:
             raise _lib.SpecFoldError("folded verify forward: " + _lib.describe_device_error(bits))
         mx, sm = max(counts), sum(counts)
         if count_stats:
-            self._fold_draft_positions = getattr(self, "_fold_draft_positions", 0) + (B1 - 1) * N * L
-            self._fold_draft_recomputed = getattr(self, "_fold_draft_recomputed", 0) + int(sm) - L * N
-        if rec is not None:
-            self.last_rec_masks = rec.view(L, B1, N)
+            self._count_folds(B1, N, L, sm)
         return logits, {"max_count": int(mx), "sum_count": int(sm)}
 
-    def _static_state(self, batched_input, past_key_values, dtype, P, bucket) -> dict:
+    def _count_folds(self, B1, N, L, recomputed_rows):
+        self._fold_draft_positions = getattr(self, "_fold_draft_positions", 0) + (B1 - 1) * N * L
+        self._fold_draft_recomputed = (getattr(self, "_fold_draft_recomputed", 0)
+                                       + int(recomputed_rows) - L * N)
+
+    def _settle(self, st) -> None:
+        pend = st.get("pending")
+        if pend is None:
+            return
+        st["pending"] = None
+        ev, count_stats, B1, N, L = pend
+        ev.synchronize()
+        host = st["host_slab"]
+        bits = int(host[-1])
+        if bits:
+            raise _lib.SpecFoldError("folded verify forward: " + _lib.describe_device_error(bits))
+        if count_stats:
+            self._count_folds(B1, N, L, sum(host[:L].tolist()))
+
+    def settle_stats(self) -> None:
+        """Read the fold counters and device error words of calls made with
+        ``defer_stats`` (waits for them); raises SpecFoldError on a device error."""
+        for st in list(self.__dict__.get("_statics", {}).values()):
+            self._settle(st)
+
+    def _static_state(self, batched_input, past_key_values, dtype, P, bucket, commit=False,
+                      shift=True) -> dict:
         """Buffers and the C argument struct of one configuration (shape, prefix cache
         tensors, bucket), kept at fixed addresses across calls so that the library
         replays its CUDA graph of the forward.  RoPE tables and the query scale depend
-        only on the prefix length and are filled once here."""
+        only on the prefix length and are filled once here.
+
+        With a PreallocatedKVCache the prefix length is not part of the configuration:
+        it is handed to the kernels in device memory (sf_verify_args.P_dev), bounded by
+        the cache capacity, and the RoPE rows of the current positions are copied from
+        tables over the whole capacity at each call, so one state and one captured graph
+        serve every block of a decode."""
+        from .kv_cache import PreallocatedKVCache
+        prealloc = isinstance(past_key_values, PreallocatedKVCache)
         lib = _lib.load()
         base = self._base()
         cfg = self.model_executor.model.config
@@ -315,7 +396,18 @@ class FoldedVerifyB200:
         H, Hkv = cfg.num_attention_heads // tp_size, cfg.num_key_value_heads // tp_size
         hd = layers[0].self_attn.head_dim
         kv, keep, kv_stride = [], [], 0
-        if P > 0:
+        if prealloc:
+            # the cache's whole buffers (capacity rows per head): their addresses do not
+            # change with the prefix length
+            for li in range(L):
+                k0, v0 = past_key_values.buffers(li)
+                if tp_size > 1 and k0.shape[0] == Hkv * tp_size:   # this rank's kv heads
+                    k0, v0 = k0[tp_rank * Hkv:(tp_rank + 1) * Hkv], v0[tp_rank * Hkv:(tp_rank + 1) * Hkv]
+                keep += [k0, v0]
+                kv.append((k0.data_ptr(), v0.data_ptr()))
+            kv_stride = keep[0].stride(0)
+            cap = past_key_values.capacity
+        elif P > 0:
             for li in range(L):
                 k, v = past_key_values[li]
                 k0, v0 = self._prefix_view(k), self._prefix_view(v)
@@ -327,8 +419,9 @@ class FoldedVerifyB200:
                     raise ValueError("prefix cache layers must share one head stride")
                 keep += [k0, v0]
                 kv.append((k0.data_ptr(), v0.data_ptr()))
-        key = (dev.index, dtype, B1, N, P, bucket, bool(self.record_masks), kv_stride, tuple(kv),
-               tp_size, tp_comm)
+        key = (dev.index, dtype, B1, N, "cap" if prealloc else P, cap if prealloc else None,
+               bucket, bool(self.record_masks), kv_stride, tuple(kv), tp_size, tp_comm,
+               bool(commit), bool(shift))
         statics = self.__dict__.setdefault("_statics", {})
         st = statics.get(key)
         if st is not None:
@@ -341,17 +434,30 @@ class FoldedVerifyB200:
         probe = torch.zeros(1, N, D, dtype=dtype, device=dev)
         pos = torch.arange(P, P + N, device=dev).unsqueeze(0)
         cos, sin = base.rotary_emb(probe, pos)
-        st = {"L": L, "keep": keep}
+        st = {"L": L, "keep": keep, "P_dev": None, "pending": None}
         st["cos"] = cos[0].to(dtype).contiguous()
         st["sin"] = sin[0].to(dtype).contiguous()
         st["q_scale"] = self._q_scale(cfg, P, N, dev)
+        P_bound = P
+        if prealloc:
+            P_bound = cap - N
+            st["cap"] = cap
+            st["P_dev"] = torch.full((1,), P, dtype=torch.int32, device=dev)
+            probe_all = torch.zeros(1, cap, D, dtype=dtype, device=dev)
+            cos_all, sin_all = base.rotary_emb(probe_all, torch.arange(cap, device=dev).unsqueeze(0))
+            st["cos_all"] = cos_all[0].to(dtype).contiguous()
+            st["sin_all"] = sin_all[0].to(dtype).contiguous()
+            qs_all = self._q_scale(cfg, 0, cap, dev, force=True)
+            st["q_scale_all"] = qs_all
+            st["q_scale"] = None if qs_all is None else qs_all[P:P + N].clone()
         st["hidden"] = torch.empty(BN, D, dtype=dtype, device=dev)
         st["par"] = torch.zeros(B1, dtype=torch.int64, device=dev)
         st["logits"] = torch.empty(B1, N, V, dtype=dtype, device=dev)
         st["slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32, device=dev)
         st["host_slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32).pin_memory()
         st["rec"] = torch.zeros(L * BN, dtype=torch.int8, device=dev) if self.record_masks else None
-        need = lib.sf_verify_workspace_bytes(dtype_code(st["hidden"]), B1, N, D, H, Hkv, hd, I, V, P)
+        need = lib.sf_verify_workspace_bytes(dtype_code(st["hidden"]), B1, N, D, H, Hkv, hd, I, V,
+                                             P_bound)
         st["ws"] = torch.empty(need, dtype=torch.uint8, device=dev)
 
         layer_arr = (_lib.SfLayer * L)()
@@ -363,19 +469,21 @@ class FoldedVerifyB200:
             sl.b_qkv = None if w[1] is None else w[1].data_ptr()
             sl.w_gate, sl.w_down = w[5].data_ptr(), w[7].data_ptr()
             sl.w_up = None if w[6] is None else w[6].data_ptr()
-            if P > 0:
+            if kv:
                 sl.prefix_k, sl.prefix_v = kv[li]
         slab = st["slab"]
         args = _lib.SfVerifyArgs()
         args.dtype = dtype_code(st["hidden"])
         args.B1, args.N, args.D, args.H, args.Hkv, args.hd = B1, N, D, H, Hkv, hd
-        args.I, args.V, args.L, args.P = I, V, L, P
+        args.I, args.V, args.L, args.P = I, V, L, P_bound
         args.kv_head_stride = kv_stride
+        args.P_dev = None if st["P_dev"] is None else st["P_dev"].data_ptr()
+        args.commit = 1 if commit else 0
         args.bucket = bucket
         args.delta = self.delta
         args.eps = float(getattr(cfg, "rms_norm_eps", 1e-6))
         args.scale = scale
-        args.shift_logits = 1 if self.family == "fastdllm" else 0
+        args.shift_logits = 1 if shift else 0
         args.weights_tiled = 1 if self._tiled else 0
         args.layers = layer_arr
         args.final_norm_w = base.norm.weight.data_ptr()
@@ -395,8 +503,8 @@ class FoldedVerifyB200:
         args.tp_size = tp_size
         st["layer_arr"] = layer_arr
         st["args"] = args
-        if len(statics) >= 4:
-            statics.pop(next(iter(statics)))
+        if len(statics) >= 12:      # a decode keeps one state per branch count + the commit
+            self._settle(statics.pop(next(iter(statics))))
         statics[key] = st
         return st
 
@@ -408,7 +516,7 @@ class FoldedVerifyB200:
             t0 = t0.contiguous()
         return t0
 
-    def _q_scale(self, cfg, P, N, device):
+    def _q_scale(self, cfg, P, N, device, force=False):
         return None
 
     # -------------------------------------------------------------- draft construction
@@ -434,6 +542,16 @@ class FoldedVerifyB200:
                torch.tensor(off, dtype=torch.int32, device=device), K)
         cache[key] = (graph, out)
         return out
+
+    def _draft_states_async(self, block, logits, mask, pos_offset, conf_fp32=False):
+        """(nodes, drafts [n_nodes, L], valid [n_nodes]) from sf_draft_blocks, left on the
+        device (no host sync); nodes == [] when the graph has no usable node."""
+        g = self._graph_pairs(block.device)
+        if g is None or not g[0]:
+            return [], None, None
+        nodes, pairs, off, K = g
+        drafts, valid = K_draft_blocks(logits, mask, block, pos_offset, pairs, off, K, conf_fp32)
+        return nodes, drafts, valid
 
     def _draft_states(self, block, logits, mask, pos_offset, conf_fp32):
         """(nodes, drafts [n_nodes, L], valid list) from sf_draft_blocks; one host sync."""
@@ -513,7 +631,10 @@ class SpecFoldB200NLDGeneration(FoldedVerifyB200):
         nodes, drafts, valid = self._draft_states(x_block, logits_block, mask_index, 0, conf_fp32=True)
         return [{"state": drafts[k], "node": n} for k, n in enumerate(nodes) if valid[k]]
 
-    def _q_scale(self, cfg, P, N, device):
+    def _q_scale(self, cfg, P, N, device, force=False):
+        """llama-4 query scale of block positions [P, P + N) (nld_folded.py:37-53); None
+        when it is identically 1, unless ``force`` (a table over a cache's capacity,
+        copied from per call, must exist whenever the model has the parameters)."""
         rp = getattr(cfg, "rope_parameters", None) or {}
         beta = rp.get("llama_4_scaling_beta")
         omax = rp.get("original_max_position_embeddings")
@@ -521,6 +642,6 @@ class SpecFoldB200NLDGeneration(FoldedVerifyB200):
             return None
         pos = torch.arange(P, P + N, device=device, dtype=torch.float32)
         scale = 1.0 + beta * torch.log(1.0 + torch.floor(pos / omax))
-        if bool((scale == 1.0).all()):
+        if not force and bool((scale == 1.0).all()):
             return None
         return scale.contiguous()

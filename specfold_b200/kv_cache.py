@@ -85,7 +85,28 @@ class PreallocatedKVCache:
     def __iter__(self) -> Iterator[Tuple[torch.Tensor, torch.Tensor]]:
         return (self[li] for li in range(self.num_layers))
 
+    def buffers(self, layer_idx: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Layer ``layer_idx``'s whole key and value buffers [Hkv, capacity, hd]: the
+        addresses the forward keys its state on (they change only when the cache grows)."""
+        return self._store[layer_idx, 0], self._store[layer_idx, 1]
+
     # ---------------------------------------------------------------- write side
+    def reserve(self, n: int) -> None:
+        """Make room for ``n`` more rows in every layer (grows by doubling)."""
+        need = max(self._len) + n
+        if need > self.capacity:
+            cap = self.capacity
+            while cap < need:
+                cap *= 2
+            self._grow(cap)
+
+    def advance(self, n: int) -> None:
+        """Count ``n`` rows that a commit forward wrote in place (at the current length of
+        every layer, within the reserved capacity) as part of the prefix."""
+        if any(x + n > self.capacity for x in self._len):
+            raise ValueError("advance past the cache capacity")
+        self._len = [x + n for x in self._len]
+
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
                cache_kwargs=None) -> Tuple[torch.Tensor, torch.Tensor]:
         """Append ``key_states`` / ``value_states`` [1, Hkv, n, hd] to layer

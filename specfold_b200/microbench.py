@@ -157,10 +157,74 @@ def bench_forward(dims, args):
     print(json.dumps(out), flush=True)
 
 
+def bench_sweep(args):
+    """The folded-attention / fused-QKV sweep at the Llama-style 8B shape (hidden 4096,
+    32 q / 8 kv heads, head_dim 128, RoPE theta 5e5, bf16): prefix length x fold ratio x
+    branch budget B (B1 = B + 1 branches of N = 32), configuration-0 noise (a 1 - fold
+    share of the draft rows gets the large noise and is recomputed).  One decoder layer
+    per configuration; per-kernel CUDA-event times from the library's profiler, with the
+    algorithmic bytes and FLOPs of each kernel:
+
+    * qkv: weights + the recomputed rows' input and output; 2 R (H + 2 Hkv) hd D FLOPs;
+    * attention (prefix pass + rows pass): the prefix K/V once + the block's q / k / v;
+      4 R H hd (P + N) FLOPs for the R recomputed rows plus 4 (BN - R) H hd N for the
+      folded rows' in-block keys;
+    * gate: the layer input, the parents' rows and the normalised recomputed rows."""
+    import dataclasses
+    from .folded import SpecFoldB200NLDGeneration
+    from . import synthetic as syn
+    dims = dataclasses.replace(SHAPES["llama8b"], layers=1)
+    D, H, Hkv, hd = dims.hidden, dims.heads, dims.kv_heads, dims.head_dim
+    N = 32
+    model = syn.build_model(dims, family="nld", dtype=torch.bfloat16, seed=0, device="cuda")
+    gen = SpecFoldB200NLDGeneration(model_executor=syn.StandinExecutor(model), delta=0.1)
+    prefixes = [int(x) for x in args.sweep_prefix.split(",")]
+    folds = [float(x) for x in args.sweep_fold.split(",")]
+    budgets = [int(x) for x in args.sweep_b.split(",")]
+    for P in prefixes:
+        cache = syn.random_prefix_cache(dims, P, dtype=torch.bfloat16, seed=1, device="cuda")
+        for B in budgets:
+            B1 = B + 1
+            for fold in folds:
+                syn.inject_hidden(model, syn.config0_hidden(
+                    dims, B1, N, dtype=torch.bfloat16, frac_recompute=1.0 - fold).cuda())
+                ids = torch.zeros(B1, N, dtype=torch.int64, device="cuda")
+                for _ in range(3):
+                    gen._batched_block_forward(ids, cache)
+                torch.cuda.synchronize()
+                gen._fold_draft_positions = gen._fold_draft_recomputed = 0
+                _lib.profile_begin(args.iters * 16)
+                for _ in range(args.iters):
+                    gen._batched_block_forward(ids, cache)
+                torch.cuda.synchronize()
+                prof = _lib.profile_end()
+                BN = B1 * N
+                R = (gen._fold_draft_recomputed + args.iters * N) / args.iters
+                n_out = (H + 2 * Hkv) * hd
+                work = {
+                    "qkv": (n_out * D * 2 + R * D * 2 + R * n_out * 2, 2 * R * n_out * D),
+                    "attention": (2 * P * Hkv * hd * 2 + BN * (H + 2 * Hkv) * hd * 2 + BN * H * hd * 2,
+                                  4 * R * H * hd * (P + N) + 4 * (BN - R) * H * hd * N),
+                    "gate": (2 * BN * D * 2 + R * D * 2, 0),
+                }
+                out = {"sweep": "llama8b", "prefix": P, "B": B, "B1": B1, "fold_target": fold,
+                       "fold_ratio": round(gen.fold_ratio, 4) if B > 0 else None,
+                       "recomputed_rows": round(R, 1)}
+                for k, (nb, nf) in work.items():
+                    t_ms, calls = prof.get(k, (0.0, 0))
+                    if not calls:
+                        continue
+                    per = t_ms / calls / 1e3
+                    out[k] = {"us": round(per * 1e6, 2), "gbs": round(nb / per / 1e9, 1),
+                              "tflops": round(nf / per / 1e12, 2)}
+                print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
-                    choices=["qkv", "o_proj", "ffn", "lm_head", "all_gemm", "forward", "sample"])
+                    choices=["qkv", "o_proj", "ffn", "lm_head", "all_gemm", "forward", "sample",
+                             "sweep"])
     ap.add_argument("--shape", default="qwen7b", choices=sorted(SHAPES))
     ap.add_argument("--rows", type=int, default=122)
     ap.add_argument("--iters", type=int, default=20)
@@ -171,8 +235,14 @@ def main():
     ap.add_argument("--branches", type=int, default=8, help="forward: B1 (main + drafts)")
     ap.add_argument("--untiled", action="store_true",
                     help="forward: plain row-major weights instead of the tile layout")
+    ap.add_argument("--sweep-prefix", default="1024,4096,16384,32768")
+    ap.add_argument("--sweep-fold", default="0,0.3,0.6,0.9")
+    ap.add_argument("--sweep-b", default="1,4,7")
     args = ap.parse_args()
     _lib.check(_lib.load().sf_check_device(), "device")
+    if args.kernel == "sweep":
+        bench_sweep(args)
+        return
     dims = SHAPES[args.shape]
     g = torch.Generator().manual_seed(args.seed)
     if args.kernel == "forward":

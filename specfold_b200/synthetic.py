@@ -273,3 +273,104 @@ def config0_hidden(dims: ModelDims, B1: int = 8, N: int = 32, dtype=torch.float3
     gen = torch.Generator().manual_seed(seed + 1000)
     x0 = torch.randn(N, dims.hidden, generator=gen)
     return noise_hidden(x0, B1, frac_recompute=frac_recompute, seed=seed).to(dtype)
+
+
+# ----------------------------------------------------------------------------- decoding
+# The end-to-end decode configurations generate from random-init models, whose logits
+# carry no signal.  A seeded per-position logit bias stands in for a trained model's
+# confidence: for every generated position q it names a target token and a strength, and
+# the model's output row that predicts q (Fast-dLLM: the row before q, which the logit
+# shift moves onto q; fastdllm_v2_generation.py:121-126) gets the strength added at the
+# target's column.  "strong" positions reach a top-p confidence of 1 and are committed by
+# the threshold test in the first step they are masked; "weak" ones stay below it and are
+# committed one per step by the max-confidence rule (fastdllm_v2_generation.py:673-676),
+# their strengths spaced so that the order of commits is set by the bias rather than by
+# rounding noise; "free" positions (no bias) take the model's own argmax.
+
+
+@dataclasses.dataclass
+class DecodeBias:
+    """target[q] (int64, -1 = free) and strength[q] (float32) per absolute position q."""
+    target: torch.Tensor
+    strength: torch.Tensor
+
+    def _on(self, device):
+        cache = self.__dict__.setdefault("_dev", {})
+        key = str(device)
+        if key not in cache:
+            cache[key] = (self.target.to(device), self.strength.to(device))
+        return cache[key]
+
+    def apply(self, logits: torch.Tensor, pred_positions: torch.Tensor) -> torch.Tensor:
+        """In place on logits [..., R, V]: row r gets strength[q_r] added at column
+        target[q_r], q_r = pred_positions[r] (positions outside the table, or free, get
+        nothing), rounded once to the logits' dtype -- the bf16 / fp32 add torch performs
+        on the model's output.  No host synchronisation: every row is gathered and
+        written back, unbiased rows unchanged."""
+        target, strength = self._on(logits.device)
+        q = pred_positions.to(device=logits.device, dtype=torch.int64)
+        ok = (q >= 0) & (q < target.numel())
+        qc = q.clamp(0, target.numel() - 1)
+        tok = torch.where(ok, target[qc], torch.full_like(qc, -1))
+        r = torch.arange(q.numel(), device=logits.device)
+        col = tok.clamp(min=0)
+        cur = logits[..., r, col]
+        new = (cur.float() + strength[qc]).to(logits.dtype)
+        logits[..., r, col] = torch.where(tok >= 0, new, cur)
+        return logits
+
+
+def decode_bias(vocab: int, start: int, total: int, seed: int = 7, frac_strong: float = 0.6,
+                frac_free: float = 0.0, strong: float = 20.0, weak_base: float = 6.0,
+                weak_step: float = 0.5, exclude: Sequence[int] = ()) -> DecodeBias:
+    """Bias table over positions [0, total): positions [start, total) are the generated
+    ones (the prompt's own positions are free).  Each is strong with probability
+    ``frac_strong``, free with ``frac_free``, else weak with strength weak_base +
+    weak_step * ((q * 10) mod 11) -- distinct within any 8 consecutive positions."""
+    gen = torch.Generator().manual_seed(seed)
+    target = torch.full((total,), -1, dtype=torch.int64)
+    strength = torch.zeros(total, dtype=torch.float32)
+    n = total - start
+    if n <= 0:
+        return DecodeBias(target, strength)
+    bad = torch.tensor(sorted(set(int(x) for x in exclude)), dtype=torch.int64)
+    tok = torch.randint(0, vocab - len(bad), (n,), generator=gen)
+    for b in bad.tolist():                         # skip the excluded ids (ascending)
+        tok = tok + (tok >= b).to(torch.int64)
+    u = torch.rand(n, generator=gen)
+    q = torch.arange(start, total)
+    weak = weak_base + weak_step * ((q * 10) % 11).float()
+    kind_strong = u < frac_strong
+    kind_free = (u >= frac_strong) & (u < frac_strong + frac_free)
+    s = torch.where(kind_strong, torch.full_like(weak, strong), weak)
+    target[start:] = torch.where(kind_free, torch.full_like(tok, -1), tok)
+    strength[start:] = torch.where(kind_free, torch.zeros_like(s), s)
+    return DecodeBias(target, strength)
+
+
+def decode_prompt(vocab: int, length: int, seed: int = 5,
+                  exclude: Sequence[int] = ()) -> torch.Tensor:
+    """[length] uniform-random prompt token ids (seeded), avoiding ``exclude``."""
+    gen = torch.Generator().manual_seed(seed)
+    bad = sorted(set(int(x) for x in exclude))
+    tok = torch.randint(0, vocab - len(bad), (length,), generator=gen)
+    for b in bad:
+        tok = tok + (tok >= b).to(torch.int64)
+    return tok
+
+
+def synthetic_draft_graph() -> dict:
+    """A draft graph in the calibration output format (specfold/calibration/
+    calibration.py:246-264): 7 nodes (budget B = 7) over three levels, at most three per
+    level (S = 3), depth within D = 8.  ij_set pairs are (pos_rank, vocab_rank): fill the
+    pos_rank-th most confident masked position with its vocab_rank-th most likely token."""
+    sets = [[(0, 0)], [(1, 0)], [(0, 1)],
+            [(0, 0), (1, 0)], [(0, 0), (2, 0)], [(0, 1), (1, 0)],
+            [(0, 0), (1, 0), (2, 0)]]
+    parents = [None, None, None, 1, 1, 1, 2]
+    nodes = []
+    for k, ij in enumerate(sets):
+        nodes.append({"L": len(ij), "ij_set": sorted(ij), "frequency": 100 - 10 * k,
+                      "score": float(100 - 10 * k),
+                      "parent_L": parents[k]})
+    return {"selected_nodes": nodes, "tree_roots": []}
