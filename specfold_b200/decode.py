@@ -158,10 +158,13 @@ class FastDLLMV2Decoder:
         if self.logit_bias is not None:
             N = batched.shape[1]
             # shifted row n holds the prediction of position P + n (row 0: a copy of the
-            # row predicting P + 1)
-            pred = torch.arange(P, P + N, device=logits.device)
-            pred[0] = P + 1
-            self.logit_bias.apply(logits, pred)
+            # row predicting P + 1); offsets kept on the device, no host round trip
+            off = self.__dict__.get("_pred_off")
+            if off is None or off.numel() != N or off.device != logits.device:
+                off = torch.arange(N, device=logits.device)
+                off[0] = 1
+                self._pred_off = off
+            self.logit_bias.apply(logits, off + P)
         return logits
 
     def _to_device(self, rows: List[List[int]], dev) -> torch.Tensor:
@@ -205,16 +208,26 @@ class FastDLLMV2Decoder:
 
     def _unmask(self, x: List[int], s0: int, s1: int, small_mask: List[bool], tokens, conf):
         """The commit rule of fastdllm_v2_generation.py:667-700 on the host: positions
-        whose confidence exceeds the threshold, plus the most confident masked one."""
-        bl = self.block_length
-        small = torch.tensor(small_mask)
-        x1_p = torch.where(small, conf, torch.tensor(float("-inf"), dtype=conf.dtype))
-        unmask = x1_p > self._threshold_in(conf.dtype)
-        unmask[int(x1_p.argmax())] = True
-        unmask &= small
-        base = len(x) - bl
-        for j in unmask.nonzero(as_tuple=True)[0].tolist():
-            x[base + s0 + j] = int(tokens[j])
+        whose confidence exceeds the threshold, plus the most confident masked one (the
+        first of equal maxima, as torch.argmax).  The confidences are the logits dtype's
+        values, exactly representable as Python floats, and the threshold is that dtype's
+        rounding of it, so the comparisons are the reference's."""
+        thr = float(self._threshold_in(conf.dtype))
+        c = conf.tolist()
+        tk = tokens.tolist()
+        best, best_j = float("-inf"), 0
+        pick = []
+        for j, m in enumerate(small_mask):
+            v = c[j] if m else float("-inf")
+            if v > best:
+                best, best_j = v, j
+            if m and v > thr:
+                pick.append(j)
+        if small_mask[best_j] and best_j not in pick:
+            pick.append(best_j)
+        base = len(x) - self.block_length + s0
+        for j in pick:
+            x[base + j] = int(tk[j])
 
     def _finish(self, x, orig_len, t0, model_calls, drafts, hits, steps, fold0, dev):
         self.gen.settle_stats()

@@ -290,9 +290,12 @@ class FoldedVerifyB200:
             self._pack_layer_weights(base.layers)
         P = int(past_key_values.get_seq_length()) if past_key_values is not None else 0
         stream = torch.cuda.current_stream(dev)
-        hidden = base.embed_tokens(batched_input)
+        emb = base.embed_tokens
+        table = isinstance(emb, torch.nn.Embedding) and emb.max_norm is None
+        hidden = None if table else emb(batched_input)
+        dtype = emb.weight.dtype if table else hidden.dtype
         shift = (self.family == "fastdllm") if shift is None else bool(shift)
-        st = self._static_state(batched_input, past_key_values, hidden.dtype, P, bucket,
+        st = self._static_state(batched_input, past_key_values, dtype, P, bucket,
                                 commit=commit, shift=shift)
         L = st["L"]
         if st["P_dev"] is not None:
@@ -313,7 +316,10 @@ class FoldedVerifyB200:
         ids = ids.contiguous()
         _lib.check(lib.sf_parent_map(ids.data_ptr(), B1, N, st["par"].data_ptr(),
                                      stream.cuda_stream), "parent map")
-        st["hidden"].copy_(hidden.reshape(BN, -1))
+        if table:   # the embedding lookup written straight into the fixed input buffer
+            torch.index_select(emb.weight, 0, ids.view(-1), out=st["hidden"])
+        else:
+            st["hidden"].copy_(hidden.reshape(BN, -1))
         st["args"].stream = stream.cuda_stream
         st["args"].delta = self.delta if delta is None else float(delta)
         _lib.check(lib.sf_folded_verify_forward(st["args"]), "folded verify forward")
@@ -396,9 +402,17 @@ class FoldedVerifyB200:
         H, Hkv = cfg.num_attention_heads // tp_size, cfg.num_key_value_heads // tp_size
         hd = layers[0].self_attn.head_dim
         kv, keep, kv_stride = [], [], 0
+        statics = self.__dict__.setdefault("_statics", {})
         if prealloc:
             # the cache's whole buffers (capacity rows per head): their addresses do not
-            # change with the prefix length
+            # change with the prefix length, and the store's address stands for all of
+            # them (looked up first: a decode step skips the per-layer walk)
+            fast = (dev.index, dtype, B1, N, "store", past_key_values._store.data_ptr(),
+                    past_key_values.capacity, bucket, bool(self.record_masks), tp_size, tp_comm,
+                    bool(commit), bool(shift))
+            st = statics.get(fast)
+            if st is not None:
+                return st
             for li in range(L):
                 k0, v0 = past_key_values.buffers(li)
                 if tp_size > 1 and k0.shape[0] == Hkv * tp_size:   # this rank's kv heads
@@ -419,13 +433,14 @@ class FoldedVerifyB200:
                     raise ValueError("prefix cache layers must share one head stride")
                 keep += [k0, v0]
                 kv.append((k0.data_ptr(), v0.data_ptr()))
-        key = (dev.index, dtype, B1, N, "cap" if prealloc else P, cap if prealloc else None,
-               bucket, bool(self.record_masks), kv_stride, tuple(kv), tp_size, tp_comm,
-               bool(commit), bool(shift))
-        statics = self.__dict__.setdefault("_statics", {})
-        st = statics.get(key)
-        if st is not None:
-            return st
+        if prealloc:
+            key = fast
+        else:
+            key = (dev.index, dtype, B1, N, P, bucket, bool(self.record_masks), kv_stride,
+                   tuple(kv), tp_size, tp_comm, bool(commit), bool(shift))
+            st = statics.get(key)
+            if st is not None:
+                return st
 
         D = layers[0].self_attn.q_proj.weight.shape[1]
         I = layers[0].mlp.gate_proj.weight.shape[0] // tp_size
