@@ -401,49 +401,72 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def cpu_model_name() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 class CpuReference:
     """Reference PyTorch folded forward (oracle restatement) on the host cores: one
-    decoder layer of the 7B shape at the bench inputs plus the LM head, the per-step
-    time extrapolated to the full layer count."""
+    decoder layer of the 7B shape at the bench inputs plus the LM head.  A step is
+    extrapolated as layers x (t(layer + head) - t(head)) + t(head), each term the median
+    of the same number of samples after one warm-up, at a given thread count -- the same
+    procedure in both arms of the benchmark."""
 
     def __init__(self):
         from specfold_b200 import synthetic as syn
-        self.threads = os.cpu_count() or 1
-        torch.set_num_threads(self.threads)
+        self.all_threads = os.cpu_count() or 1
         self.layers_full = syn.SHAPES[SHAPE].layers
         self.dims, self.model, self.cache, self.ids = build_workload("cpu", layers=1)
-        x = torch.randn(B1 * N, self.dims.hidden).to(torch.bfloat16)
-        with torch.no_grad():
-            self.model.lm_head(self.model.model.norm(x))       # warm
-            t = time.time()
-            self.model.lm_head(self.model.model.norm(x))
-            self.t_head = time.time() - t
+        self.x = torch.randn(B1 * N, self.dims.hidden).to(torch.bfloat16)
 
-    def step_seconds(self) -> float:
+    def _full(self):
         from oracle import folded_oracle as orc
-        with torch.no_grad():
-            t = time.time()
-            orc.folded_forward(self.model, self.ids, self.cache, DELTA)
-            one = time.time() - t
-        per_layer = max(one - self.t_head, 1e-6)
-        return self.layers_full * per_layer + self.t_head
+        t = time.perf_counter()
+        orc.folded_forward(self.model, self.ids, self.cache, DELTA)
+        return time.perf_counter() - t
 
-    def describe(self, step_s, n):
-        return {"value": round(1.0 / step_s, 6), "unit": UNIT, "cores": self.threads,
-                "kind": "port", "step_s_extrapolated": round(step_s, 3),
-                "lm_head_s": round(self.t_head, 4),
-                "sample": f"1 decoder layer + LM head of the 7B shape at the bench inputs "
-                          f"(bf16, P={P_PREFIX}), median of {n}, extrapolated to "
-                          f"{self.layers_full} layers"}
+    def _head(self):
+        t = time.perf_counter()
+        self.model.lm_head(self.model.model.norm(self.x))
+        return time.perf_counter() - t
+
+    @torch.no_grad()
+    def measure(self, threads: int, samples: int, budget_s: float):
+        torch.set_num_threads(threads)
+        self._full(), self._head()                                  # warm
+        full, head, start = [], [], time.perf_counter()
+        while len(full) < samples and (not full or time.perf_counter() - start < budget_s):
+            full.append(self._full())
+            head.append(self._head())
+        f, h = statistics.median(full), statistics.median(head)
+        step = self.layers_full * max(f - h, 1e-6) + h
+        return {"step_s": round(step, 4), "value": round(1.0 / step, 6), "threads": threads,
+                "samples": len(full), "layer_s": round(f - h, 5), "lm_head_s": round(h, 5)}
+
+    def describe(self, allc, one=None):
+        out = {"value": allc["value"], "unit": UNIT, "cores": allc["threads"], "kind": "port",
+               "cpu_model": cpu_model_name(), "step_s_extrapolated": allc["step_s"],
+               "all_threads": allc,
+               "sample": f"1 decoder layer + LM head of the 7B shape at the bench inputs "
+                         f"(bf16, P={P_PREFIX}), medians of {allc['samples']} samples each "
+                         f"after one warm-up, extrapolated to {self.layers_full} layers"}
+        if one is not None:
+            out["one_thread"] = one
+        return out
 
 
 def cpu_baseline(budget_s=30.0):
     ref = CpuReference()
-    samples, start = [], time.time()
-    ref.step_seconds()                                          # warm
-    while len(samples) < 3 and time.time() - start < budget_s:
-        samples.append(ref.step_seconds())
-    return ref.describe(statistics.median(samples), len(samples))
+    allc = ref.measure(ref.all_threads, 5, budget_s / 2)
+    one = ref.measure(1, 3, budget_s / 2)
+    torch.set_num_threads(ref.all_threads)
+    return ref.describe(allc, one)
 
 
 def run_reference(args):
@@ -451,11 +474,10 @@ def run_reference(args):
     if rank != 0:
         return
     ref = CpuReference()
-    for _ in range(max(1, min(args.warmup, 2))):
-        ref.step_seconds()
-    steps = [ref.step_seconds() for _ in range(args.steps)]
-    step_s = statistics.median(steps)
-    cpu = ref.describe(step_s, len(steps))
+    allc = ref.measure(ref.all_threads, max(args.steps, 5), args.cpu_budget)
+    one = ref.measure(1, 3, args.cpu_budget)
+    cpu = ref.describe(allc, one)
+    step_s = allc["step_s"]
     line = {
         "metric": METRIC, "value": cpu["value"], "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
@@ -469,6 +491,79 @@ def run_reference(args):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _import_reference(root):
+    """The reference's folded generators from an installed copy (baseline/_ref): the
+    package __init__ modules import the vendored NLD model and the executors, which the
+    folded forwards do not use, so the packages are registered as bare namespaces first
+    and the two NLD modules nld_folded imports are stubbed."""
+    import importlib
+    import types
+    for name in ("specfold", "specfold.generate", "specfold.model_cache",
+                 "specfold.model_cache.nemotron_labs_diffusion"):
+        mod = types.ModuleType(name)
+        mod.__path__ = [os.path.join(root, *name.split("."))]
+        sys.modules[name] = mod
+    ex = types.ModuleType("specfold.generate.nld_model_executor")
+    ex.NLDModelExecutor = object
+    sys.modules[ex.__name__] = ex
+    mdl = types.ModuleType("specfold.model_cache.nemotron_labs_diffusion.modeling_nemotron_labs_diffusion")
+    mdl._get_num_transfer_tokens = mdl._get_transfer_index = None
+    sys.modules[mdl.__name__] = mdl
+    sys.path.insert(0, root)
+    return importlib.import_module("specfold.generate.fastdllm_v2_folded")
+
+
+def run_triton_reference(args):
+    """The reference's own fused generator, SpecFoldTritonFastDLLMV2Generation
+    (specfold/generate/fastdllm_v2_folded.py:226-370, its Triton kernels JIT-compiled for
+    this GPU), timed at the benchmark workload on one GPU: the kernel-level bar for the
+    B200 path.  Needs the reference installed under baseline/_ref (pip --target); prints
+    an "unavailable" line otherwise.  Not the driver's reference arm (that is the CPU
+    path, --impl reference)."""
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "specfold")):
+        print(json.dumps({"impl": "reference-triton", "unavailable": "baseline/_ref not installed"}))
+        return
+    fd = _import_reference(root)
+    from specfold_b200.synthetic import StandinExecutor
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dims, model, cache, ids = build_workload(dev)
+    gen = object.__new__(fd.SpecFoldTritonFastDLLMV2Generation)
+    gen.model_executor = StandinExecutor(model)
+    gen.delta = DELTA
+    gen.fold_bucket = None
+    gen._fold_stats = []
+    ids = ids.to(dev)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            gen._batched_block_forward(ids, cache)
+        torch.cuda.synchronize()
+        gen._fold_draft_positions = gen._fold_draft_recomputed = 0
+        stream = torch.cuda.current_stream(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            torch.cuda.synchronize()
+            t0.record(stream)
+            for _ in range(args.steps):
+                gen._batched_block_forward(ids, cache)
+            t1.record(stream)
+            torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference-triton", "value": round(args.steps / (ms / 1e3), 4),
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "dtype": "bf16",
+        "fold_ratio": round(gen.fold_ratio, 4),
+        "config": {"workload": "folded verify step, Qwen2.5-7B shape, B1=8 (main + 7 drafts), "
+                               "N=32, prefix 1024, delta 0.1",
+                   "generator": "SpecFoldTritonFastDLLMV2Generation (reference, Triton)"},
+        "clocks": clk.summary()}), flush=True)
 
 
 def run_tp(args):
@@ -550,7 +645,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--impl", choices=["b200", "reference", "reference-triton"], default="b200")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-streams", type=int, default=2,
@@ -564,6 +659,8 @@ def main():
         run_tp(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-triton":
+        run_triton_reference(args)
     else:
         run_b200(args)
 
