@@ -19,7 +19,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libspecfold_b200.so")
 SOURCES = ["gate.cu", "gemm.cu", "gemm_tc.cu", "attention.cu", "attention_tc.cu",
-           "attention_rows_mma.cu", "merge.cu", "tp.cu", "capi.cu", "ffn_static.cu", "sample.cu",
+           "attention_rows_mma.cu", "attention_rows_tc.cu", "merge.cu", "tp.cu", "capi.cu", "ffn_static.cu", "sample.cu",
            "draft.cu"]
 HEADERS = ["sf_common.cuh", "sf_kernels.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

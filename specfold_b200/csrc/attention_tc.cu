@@ -475,6 +475,15 @@ static bool rows_mma_enabled() {
   return on;
 }
 
+// SF_ROWS_TC=0: the rows pass on mma.sync tiles instead of tcgen05 (read once)
+static bool rows_tc_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SF_ROWS_TC");
+    return v == nullptr || atoi(v) != 0;
+  }();
+  return on;
+}
+
 static bool prefix_on_tc(int dtype, const AttnParams& p) {
   return dtype == BF16 && p.P > 0 && p.pk != nullptr;
 }
@@ -499,6 +508,8 @@ cudaError_t launch_attention_rows(int dtype, const AttnParams& p, cudaStream_t s
   PrefixPartials pp{};
   cudaError_t e = prefix_partials_hd(p, st, &pp, true);
   if (e != cudaSuccess) return e;
+  if (attention_rows_tc_ok(dtype, p, pp.splits) && rows_tc_enabled())
+    return launch_attention_rows_tc(p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
   if (attention_rows_mma_ok(dtype, p, pp.splits) && rows_mma_enabled())
     return launch_attention_rows_mma(p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);
   return launch_attention_rows_partials(BF16, p, pp.part_O, pp.part_ml, pp.splits, pp.q_rows, st);

@@ -289,6 +289,12 @@ bool attention_rows_mma_ok(int dtype, const AttnParams& p, int splits);
 cudaError_t launch_attention_rows_mma(const AttnParams& p, const float* part_O,
                                       const float* part_ml, int splits, int part_rows,
                                       cudaStream_t st);
+// the same rows pass with S and O on tcgen05 (TMEM accumulators): bf16, head_dim 128,
+// N <= 32 block keys, <= 16 prefix splits
+bool attention_rows_tc_ok(int dtype, const AttnParams& p, int splits);
+cudaError_t launch_attention_rows_tc(const AttnParams& p, const float* part_O,
+                                     const float* part_ml, int splits, int part_rows,
+                                     cudaStream_t st);
 
 struct MergeParams {
   const void* q_buf;
