@@ -610,6 +610,15 @@ def run_tp(args):
         if ws > 1:
             dist.barrier()
     ms = max_over_ranks([t0.elapsed_time(t1)], dev)[0]
+    # per-kernel breakdown (direct launches with CUDA events around each, outside the timed
+    # region; the all-reduces and their residual / scatter kernels are "tp_reduce")
+    _lib.profile_begin(args.steps * (dims.layers * 12 + 4))
+    for _ in range(args.steps):
+        gen._batched_block_forward(ids, cache)
+    torch.cuda.synchronize()
+    prof = _lib.profile_end()
+    kernels = {k: {"ms_per_step": round(v[0] / args.steps, 4), "calls_per_step": v[1] / args.steps}
+               for k, v in prof.items() if v[1]}
     step_ms = ms / args.steps
     hbm, _, src = peaks()
     wbytes, kvbytes = algorithmic_bytes(dims, P)
@@ -630,6 +639,7 @@ def run_tp(args):
                      "achieved": round(per_gpu / (step_ms / 1e3) / 1e9, 1), "peak": hbm,
                      "unit": "GB/s", "peak_source": src,
                      "frac": round(per_gpu / (step_ms / 1e3) / 1e9 / hbm, 4)},
+        "kernels": kernels,
         "clocks": clk.summary(),
     }
     if rank == 0:

@@ -276,6 +276,10 @@ typedef struct sf_verify_args {
    *   then written, and kv_head_stride must be >= (P + N) * hd. */
   const int32_t* P_dev;
   int commit;
+  /* tensor parallelism over peer memory (sf_tp_peers_init) instead of tp_comm: the
+   * o_proj and down partial sums stay in each rank's exchange buffer and the kernels
+   * that consume them read every rank's partial over NVLink (no NCCL on the layer path). */
+  void* tp_peers;
 } sf_verify_args;
 
 /* Tensor-parallel communicator (NCCL, loaded at run time).  Rank 0 calls
@@ -285,6 +289,18 @@ typedef struct sf_verify_args {
 int sf_tp_unique_id(void* id_out, int bytes);
 int sf_tp_comm_init(const void* id, int nranks, int rank, void** comm_out);
 int sf_tp_comm_destroy(void* comm);
+/* Tensor parallelism over peer memory.  Each rank allocates an exchange buffer of
+ * sf_tp_exchange_bytes(B1*N, D) bytes of device memory, zero-filled, maps every other
+ * rank's buffer into its address space (CUDA IPC; NVLink peers) and passes the table of
+ * device pointers -- xbufs[q] = rank q's buffer as seen from this process, its own at
+ * xbufs[rank], a HOST array of `size` pointers -- to sf_tp_peers_init; the returned
+ * handle goes into sf_verify_args.tp_peers.  Every rank must run the same sequence of
+ * forwards; a missing peer makes the waiting kernels give up after a bounded time with
+ * SF_DEV_TIMEOUT.  (No counterpart in the reference, which is single-GPU; this replaces
+ * the NCCL all-reduce of sf_tp_comm_init for the two reductions per layer.) */
+size_t sf_tp_exchange_bytes(int BN, int D);
+int sf_tp_peers_init(int rank, int size, void* const* xbufs, int BN, int D, void** peers_out);
+int sf_tp_peers_destroy(void* peers);
 /* Destroys every CUDA graph the forward captured (all devices). */
 int sf_release_graphs(void);
 

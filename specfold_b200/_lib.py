@@ -41,7 +41,7 @@ class SfVerifyArgs(C.Structure):
         ("segcnt_slab", c_void_p), ("rec_slab", c_void_p), ("ws", c_void_p),
         ("ws_bytes", c_size_t), ("err", c_void_p), ("stream", c_void_p),
         ("tp_comm", c_void_p), ("tp_size", c_int),
-        ("P_dev", c_void_p), ("commit", c_int),
+        ("P_dev", c_void_p), ("commit", c_int), ("tp_peers", c_void_p),
     ]
 
 
@@ -97,6 +97,10 @@ _SIGS = {
     "sf_tp_unique_id": (c_int, [c_void_p, c_int]),
     "sf_tp_comm_init": (c_int, [c_void_p, c_int, c_int, C.POINTER(c_void_p)]),
     "sf_tp_comm_destroy": (c_int, [c_void_p]),
+    "sf_tp_exchange_bytes": (c_size_t, [c_int, c_int]),
+    "sf_tp_peers_init": (c_int, [c_int, c_int, C.POINTER(c_void_p), c_int, c_int,
+                                 C.POINTER(c_void_p)]),
+    "sf_tp_peers_destroy": (c_int, [c_void_p]),
     "sf_release_graphs": (c_int, []),
     "sf_pack_weight_tiles": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                      c_void_p]),

@@ -76,11 +76,11 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 // only; one host thread at a time.
 enum ProfKind {
   K_GATE = 0, K_COMPACT, K_QKV, K_ATTN, K_MERGE, K_OPROJ, K_FFN_NORM, K_GATEUP, K_DOWN,
-  K_COMBINE, K_FINAL_NORM, K_LM_HEAD, K_FFN, K_NUM
+  K_COMBINE, K_FINAL_NORM, K_LM_HEAD, K_FFN, K_TP_REDUCE, K_NUM
 };
 const char* kProfNames[K_NUM] = {"gate", "compact", "qkv", "attention", "merge", "o_proj",
                                  "ffn_norm", "gate_up", "down", "combine", "final_norm",
-                                 "lm_head", "ffn"};
+                                 "lm_head", "ffn", "tp_reduce"};
 struct Profiler {
   bool on = false;
   std::vector<cudaEvent_t> ev;
@@ -645,8 +645,16 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
     return fail(SF_ERR_ARG, "null pointer in verify args");
   if (a->P < 0 || (a->P > 0 && a->kv_head_stride < static_cast<int64_t>(a->P) * hd))
     return fail(SF_ERR_ARG, "prefix length / stride mismatch");
-  if (a->tp_size > 1 && (a->tp_comm == nullptr || D % 4 != 0))
-    return fail(SF_ERR_ARG, "tensor parallel forward needs a communicator (sf_tp_comm_init)");
+  if (a->tp_size > 1 && ((a->tp_comm == nullptr && a->tp_peers == nullptr) || D % 4 != 0))
+    return fail(SF_ERR_ARG, "tensor parallel forward needs a communicator (sf_tp_comm_init) "
+                            "or a peer table (sf_tp_peers_init)");
+  if (a->tp_size > 1 && a->tp_peers != nullptr) {
+    const TpPeers* tp = static_cast<const TpPeers*>(a->tp_peers);
+    if (tp->size != a->tp_size || tp->part_elems < static_cast<int64_t>(BN) * D)
+      return fail(SF_ERR_ARG, "peer table: %d ranks / %lld partial elements, the forward needs "
+                              "%d / %lld", tp->size, static_cast<long long>(tp->part_elems),
+                  a->tp_size, static_cast<long long>(BN) * D);
+  }
   if (a->commit && (B1 != 1 || a->kv_head_stride < static_cast<int64_t>(a->P + N) * hd ||
                     hd % 8 != 0))
     return fail(SF_ERR_ARG, "commit forward needs B1 == 1 and kv_head_stride >= (P + N) * hd");
@@ -709,6 +717,8 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     s = cuda_status(cudaMemsetAsync(a->err, 0, sizeof(int32_t), st), "memset");
     if (s) return s;
   }
+  const TpPeers* peers = a->tp_size > 1 ? static_cast<const TpPeers*>(a->tp_peers) : nullptr;
+  if (peers && (s = cuda_status(launch_tp_epoch(*peers, st), "tp epoch"))) return s;
 
   for (int li = 0; li < L; ++li) {
     const sf_layer& ly = a->layers[li];
@@ -838,15 +848,21 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
       // hp = T(x + T(sum)) as the unsharded epilogue does
       GemmArgs op = o;
       op.epi.kind = EPI_RAW;
-      op.epi.out = b.tp_sum;
+      op.epi.out = peers ? peers->part[peers->rank] : b.tp_sum;
       op.epi.resid = nullptr;
       op.epi.ld_out = D;
       op.next_pf = WPrefetch{};
       if ((s = timed(K_OPROJ, st, [&] { return run_gemm(op, st, "o_proj (tp)"); }))) return s;
-      if ((s = tp_status(tp_allreduce_f32(a->tp_comm, b.tp_sum, static_cast<size_t>(BN) * D, st))))
-        return s;
-      if ((s = cuda_status(launch_resid_add(dtype, b.tp_sum, Hf, b.hp, static_cast<int64_t>(BN) * D, st),
-                           "residual add")))
+      if ((s = timed(K_TP_REDUCE, st, [&] {
+             if (peers)
+               return cuda_status(launch_tp_reduce_resid(dtype, *peers, li, L, Hf, b.hp,
+                                                         static_cast<int64_t>(BN) * D, a->err, st),
+                                  "tp reduce (o_proj)");
+             int r = tp_status(tp_allreduce_f32(a->tp_comm, b.tp_sum, static_cast<size_t>(BN) * D, st));
+             if (r) return r;
+             return cuda_status(launch_resid_add(dtype, b.tp_sum, Hf, b.hp, static_cast<int64_t>(BN) * D, st),
+                                "residual add");
+           })))
         return s;
     }
     const bool chained = dtype == SF_DTYPE_BF16 && a->weights_tiled && chain_level() > 0 &&
@@ -895,7 +911,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
       // this rank's intermediate shard: gate/up + down partial sums, all-reduce, scatter
       GemmArgs dp = dn;
       dp.epi.kind = EPI_RAW;
-      dp.epi.out = b.tp_sum;
+      dp.epi.out = peers ? peers->part[peers->rank] + peers->part_elems : b.tp_sum;
       dp.epi.rows = nullptr;
       dp.epi.ld_out = D;
       dp.next_pf = WPrefetch{};
@@ -936,11 +952,17 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
         if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, st, "gate/up"); }))) return s;
         if ((s = timed(K_DOWN, st, [&] { return run_gemm(dp, st, "down (tp)"); }))) return s;
       }
-      if ((s = tp_status(tp_allreduce_f32(a->tp_comm, b.tp_sum, static_cast<size_t>(bucket) * D, st))))
-        return s;
-      if ((s = cuda_status(launch_scatter_rows(dtype, b.tp_sum, b.rows, count, bucket, D, BN + 1,
-                                               b.ffn, a->err, st),
-                           "ffn scatter")))
+      if ((s = timed(K_TP_REDUCE, st, [&] {
+             if (peers)
+               return cuda_status(launch_tp_reduce_scatter(dtype, *peers, li, L, b.rows, count,
+                                                           bucket, D, BN + 1, b.ffn, a->err, st),
+                                  "tp reduce (down)");
+             int r = tp_status(tp_allreduce_f32(a->tp_comm, b.tp_sum, static_cast<size_t>(bucket) * D, st));
+             if (r) return r;
+             return cuda_status(launch_scatter_rows(dtype, b.tp_sum, b.rows, count, bucket, D, BN + 1,
+                                                    b.ffn, a->err, st),
+                                "ffn scatter");
+           })))
         return s;
       continue;
     }
@@ -1165,6 +1187,38 @@ int sf_tp_comm_init(const void* id, int nranks, int rank, void** comm_out) {
   const int r = tp_comm_init(id, nranks, rank, comm_out);
   if (r == -1) return fail(SF_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
   return r ? fail(SF_ERR_CUDA, "ncclCommInitRank: %s", tp_error_string(r)) : 0;
+}
+
+size_t sf_tp_exchange_bytes(int BN, int D) {
+  if (BN < 1 || D < 1) return 0;
+  return kTpHeader + 2 * static_cast<size_t>(BN) * D * sizeof(float);
+}
+
+int sf_tp_peers_init(int rank, int size, void* const* xbufs, int BN, int D, void** peers_out) {
+  if (!xbufs || !peers_out || size < 2 || size > kMaxTp || rank < 0 || rank >= size || BN < 1 ||
+      D < 1 || D % 4 != 0)
+    return fail(SF_ERR_ARG, "peer table: bad arguments");
+  TpPeers* t = new TpPeers{};
+  t->rank = rank;
+  t->size = size;
+  t->part_elems = static_cast<int64_t>(BN) * D;
+  for (int q = 0; q < size; ++q) {
+    if (!xbufs[q] || !aligned16(xbufs[q])) {
+      delete t;
+      return fail(SF_ERR_ARG, "peer table: exchange buffer %d null or unaligned", q);
+    }
+    char* base = static_cast<char*>(xbufs[q]);
+    t->flags[q] = reinterpret_cast<int*>(base);
+    t->part[q] = reinterpret_cast<float*>(base + kTpHeader);
+  }
+  t->epoch = reinterpret_cast<unsigned*>(static_cast<char*>(xbufs[rank]) + 2 * kMaxTp * sizeof(int));
+  *peers_out = t;
+  return SF_OK;
+}
+
+int sf_tp_peers_destroy(void* peers) {
+  delete static_cast<TpPeers*>(peers);
+  return SF_OK;
 }
 
 int sf_tp_comm_destroy(void* comm) {

@@ -321,6 +321,26 @@ int tp_unique_id(void* out, int bytes);
 int tp_comm_init(const void* id, int nranks, int rank, void** comm);
 int tp_comm_destroy(void* comm);
 int tp_allreduce_f32(void* comm, float* buf, size_t n, cudaStream_t st);
+
+// Tensor parallelism over peer memory (tp.cu): every rank's exchange buffer, as mapped in
+// this process (own one included), laid out as [flags: kMaxTp x 2 int32][epoch][pad to
+// kTpHeader bytes][o_proj partials: part_elems fp32][down partials: part_elems fp32].
+constexpr int kMaxTp = 8;
+constexpr size_t kTpHeader = 512;
+struct TpPeers {
+  float* part[kMaxTp];       // each rank's partial regions (o_proj, then down)
+  int* flags[kMaxTp];        // each rank's flag array: [rank q][kind] = last seq of q
+  unsigned* epoch;           // this rank's forward counter
+  int64_t part_elems;        // fp32 elements of one partial region
+  int rank, size;
+};
+cudaError_t launch_tp_epoch(const TpPeers& t, cudaStream_t st);
+cudaError_t launch_tp_reduce_resid(int dtype, const TpPeers& t, int layer, int L,
+                                   const void* resid, void* out, int64_t n, int* err,
+                                   cudaStream_t st);
+cudaError_t launch_tp_reduce_scatter(int dtype, const TpPeers& t, int layer, int L,
+                                     const int64_t* rows, const int32_t* count, int n, int D,
+                                     int64_t n_out_rows, void* out, int* err, cudaStream_t st);
 cudaError_t launch_resid_add(int dtype, const float* sum, const void* resid, void* out, int64_t n,
                              cudaStream_t st);
 cudaError_t launch_scatter_rows(int dtype, const float* sum, const int64_t* rows,

@@ -153,4 +153,159 @@ cudaError_t launch_scatter_rows(int dtype, const float* sum, const int64_t* rows
   return launched();
 }
 
+// ------------------------------------------------------------------ peer-memory reduce
+// The NCCL all-reduce of a 5 MB fp32 partial costs ~40 us per call on two B200s; the two
+// per layer made the tensor-parallel step slower than one GPU.  Instead every rank keeps
+// its partial sums in an exchange buffer that every other rank has mapped (CUDA IPC over
+// NVLink), and the kernel that consumes the sum -- the residual add after o_proj, the row
+// scatter after down -- reads all ranks' partials straight from their memory:
+//   * at its start, one thread publishes "my partial of (layer, kind) is complete" into
+//     every peer's flag slot for this rank (a release store at system scope after a
+//     system fence; the partial was written by the previous kernel on this stream);
+//   * one thread per CTA waits (bounded) until every peer's slot in the local flags
+//     shows the same sequence number, then the CTA sums the ranks' partials in rank
+//     order (identical on every rank: the gate that follows decides the same folds) and
+//     applies the epilogue arithmetic of the unsharded forward.
+// Sequence numbers grow monotonically: seq = epoch * 2L + 2 * layer + kind with a per-rank
+// epoch bumped by one kernel at the start of every forward (both ranks run the same
+// forwards), so a captured graph replays with fresh numbers.  Reuse of a partial region is
+// safe without a second handshake: a rank overwrites its o_proj (down) partial of the
+// next layer only after its own down (o_proj) reduce, which waited for every peer to
+// have started -- hence, in stream order, finished -- the reduce that reads it.
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// publish this rank's partial (thread 0 of CTA 0) and wait for every peer's (thread 0 of
+// every CTA); false after a timeout (SF_DEV_ERR_TIMEOUT set)
+__device__ bool tp_handshake(const TpPeers& t, int kind, int seq, int* err) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int q = 0; q < t.size; ++q)
+        if (q != t.rank) st_release_sys(t.flags[q] + 2 * t.rank + kind, seq);
+    }
+    bool ok = true;
+    const uint64_t t0 = globaltimer();
+    for (int q = 0; q < t.size && ok; ++q) {
+      if (q == t.rank) continue;
+      const int* f = t.flags[t.rank] + 2 * q + kind;
+      while (ld_acquire_sys(f) - seq < 0) {
+        if (globaltimer() - t0 > kWaitNs) {
+          flag_error(err, SF_DEV_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+__global__ void tp_epoch_kernel(unsigned* epoch) { *epoch += 1u; }
+
+// hp[i] = T(resid[i] + T(sum_q part_q[i])), i < n (the EPI_RESID arithmetic)
+template <typename T>
+__global__ void __launch_bounds__(256) tp_reduce_resid_kernel(TpPeers t, int layer, int L,
+                                                              const T* __restrict__ resid,
+                                                              T* out, int64_t n, int* err) {
+  const int seq = static_cast<int>(*t.epoch) * 2 * L + 2 * layer;
+  if (!tp_handshake(t, 0, seq, err)) return;
+  for (int64_t i = (blockIdx.x * 256ll + threadIdx.x) * 4; i < n; i += 256ll * gridDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < t.size; ++q) {
+      const float4 v = __ldcv(reinterpret_cast<const float4*>(t.part[q] + i));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const float sv[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      out[i + k] = Elt<T>::from_f(__fadd_rn(Elt<T>::to_f(resid[i + k]), Elt<T>::rnd(sv[k])));
+  }
+}
+
+// out[rows[j]][:] = T(sum_q part_q[j][:]) for j < min(*count, n) (the EPI_SCATTER
+// arithmetic); the down partials sit after the o_proj ones in every exchange buffer
+template <typename T>
+__global__ void __launch_bounds__(256) tp_reduce_scatter_kernel(TpPeers t, int layer, int L,
+                                                                int64_t part_off,
+                                                                const int64_t* rows,
+                                                                const int32_t* count, int n,
+                                                                int D, int64_t n_out_rows,
+                                                                T* out, int* err) {
+  const int seq = static_cast<int>(*t.epoch) * 2 * L + 2 * layer + 1;
+  if (!tp_handshake(t, 1, seq, err)) return;
+  const int cnt = min(*count, n);
+  const int64_t total = static_cast<int64_t>(cnt) * D;
+  for (int64_t i = (blockIdx.x * 256ll + threadIdx.x) * 4; i < total; i += 256ll * gridDim.x * 4) {
+    const int64_t j = i / D, d = i % D;
+    const int64_t r = rows[j];
+    if (r < 0 || r >= n_out_rows) {
+      flag_error(err, SF_DEV_ERR_INDEX);
+      continue;
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < t.size; ++q) {
+      const float4 v = __ldcv(reinterpret_cast<const float4*>(t.part[q] + part_off + i));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    out[r * D + d] = Elt<T>::from_f(acc.x);
+    out[r * D + d + 1] = Elt<T>::from_f(acc.y);
+    out[r * D + d + 2] = Elt<T>::from_f(acc.z);
+    out[r * D + d + 3] = Elt<T>::from_f(acc.w);
+  }
+}
+
+int reduce_grid(int64_t n) {
+  return static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256, 148 * 2));
+}
+
+}  // namespace
+
+cudaError_t launch_tp_epoch(const TpPeers& t, cudaStream_t st) {
+  tp_epoch_kernel<<<1, 1, 0, st>>>(t.epoch);
+  return launched();
+}
+
+cudaError_t launch_tp_reduce_resid(int dtype, const TpPeers& t, int layer, int L,
+                                   const void* resid, void* out, int64_t n, int* err,
+                                   cudaStream_t st) {
+  if (n % 4 != 0) return cudaErrorInvalidValue;
+  const int blocks = reduce_grid(n);
+  if (dtype == BF16)
+    tp_reduce_resid_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        t, layer, L, static_cast<const __nv_bfloat16*>(resid), static_cast<__nv_bfloat16*>(out),
+        n, err);
+  else
+    tp_reduce_resid_kernel<float><<<blocks, 256, 0, st>>>(t, layer, L, static_cast<const float*>(resid),
+                                                          static_cast<float*>(out), n, err);
+  return launched();
+}
+
+cudaError_t launch_tp_reduce_scatter(int dtype, const TpPeers& t, int layer, int L,
+                                     const int64_t* rows, const int32_t* count, int n, int D,
+                                     int64_t n_out_rows, void* out, int* err, cudaStream_t st) {
+  if (D % 4 != 0 || n <= 0) return n <= 0 ? cudaSuccess : cudaErrorInvalidValue;
+  const int blocks = reduce_grid(static_cast<int64_t>(n) * D);
+  const int64_t off = t.part_elems;
+  if (dtype == BF16)
+    tp_reduce_scatter_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        t, layer, L, off, rows, count, n, D, n_out_rows, static_cast<__nv_bfloat16*>(out), err);
+  else
+    tp_reduce_scatter_kernel<float><<<blocks, 256, 0, st>>>(t, layer, L, off, rows, count, n, D,
+                                                            n_out_rows, static_cast<float*>(out), err);
+  return launched();
+}
+
 }  // namespace sf

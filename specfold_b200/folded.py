@@ -127,35 +127,75 @@ class FoldedVerifyB200:
     # rank, size and the library's communicator of the 14B configuration; size 1 = off
     _tp = (0, 1, None)
 
-    def set_tensor_parallel(self, rank: int, size: int) -> None:
+    def set_tensor_parallel(self, rank: int, size: int, transport: Optional[str] = None,
+                            max_rows: int = 256) -> None:
         """Shard every layer over `size` ranks (attention heads and the intermediate
-        dimension) and all-reduce o_proj and down over NCCL.  Collective over the default
-        torch.distributed group: rank 0 creates the communicator id and broadcasts it."""
+        dimension); o_proj and down produce partial sums that are reduced across the ranks.
+        Collective over the default torch.distributed group.
+
+        transport "p2p" (default; SF_TP_TRANSPORT overrides): each rank's partials stay in
+        an exchange buffer that every other rank maps through CUDA IPC, and the kernels
+        consuming the sums read all ranks' partials over NVLink (sf_tp_peers_init).
+        "nccl": the library's own NCCL communicator all-reduces them (sf_tp_comm_init;
+        rank 0 creates the id and broadcasts it).  `max_rows` bounds B1 * N."""
+        import os
         import torch.distributed as dist
         lib = _lib.load()
+        self.close_tensor_parallel()
         if size <= 1:
-            self._tp = (0, 1, None)
             return
-        uid = (ctypes.c_char * 128)()
-        if rank == 0:
-            _lib.check(lib.sf_tp_unique_id(ctypes.cast(uid, ctypes.c_void_p), 128), "tp id")
-        box = [bytes(uid) if rank == 0 else None]
-        dist.broadcast_object_list(box, src=0)
-        ctypes.memmove(uid, box[0], 128)
-        comm = ctypes.c_void_p()
-        _lib.check(lib.sf_tp_comm_init(ctypes.cast(uid, ctypes.c_void_p), size, rank,
-                                       ctypes.byref(comm)), "tp communicator")
-        self._tp = (rank, size, comm.value)
+        transport = transport or os.environ.get("SF_TP_TRANSPORT", "p2p")
+        if transport == "nccl":
+            uid = (ctypes.c_char * 128)()
+            if rank == 0:
+                _lib.check(lib.sf_tp_unique_id(ctypes.cast(uid, ctypes.c_void_p), 128), "tp id")
+            box = [bytes(uid) if rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            ctypes.memmove(uid, box[0], 128)
+            comm = ctypes.c_void_p()
+            _lib.check(lib.sf_tp_comm_init(ctypes.cast(uid, ctypes.c_void_p), size, rank,
+                                           ctypes.byref(comm)), "tp communicator")
+            self._tp = (rank, size, comm.value)
+        elif transport == "p2p":
+            D = self.model_executor.model.config.hidden_size
+            dev = torch.device("cuda", torch.cuda.current_device())
+            nbytes = lib.sf_tp_exchange_bytes(max_rows, D)
+            xbuf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+            torch.cuda.synchronize(dev)
+            handles = [None] * size
+            dist.all_gather_object(handles, xbuf.untyped_storage()._share_cuda_())
+            mapped, ptrs = [], []
+            for q in range(size):
+                if q == rank:
+                    ptrs.append(xbuf.data_ptr())
+                else:
+                    st = torch.UntypedStorage._new_shared_cuda(*handles[q])
+                    mapped.append(st)
+                    ptrs.append(st.data_ptr())
+            peers = ctypes.c_void_p()
+            _lib.check(lib.sf_tp_peers_init(rank, size, (ctypes.c_void_p * size)(*ptrs), max_rows,
+                                            D, ctypes.byref(peers)), "tp peer table")
+            self._tp_xbuf = (xbuf, mapped)
+            self._tp_peers = peers.value
+            self._tp = (rank, size, None)
+            dist.barrier()          # every rank's buffer is mapped before any forward runs
+        else:
+            raise ValueError(f"tensor-parallel transport {transport!r}")
         self._packed_weights = None
         self.__dict__.pop("_statics", None)
 
     def close_tensor_parallel(self) -> None:
-        """Release the captured graphs (they hold NCCL calls), then the communicator."""
+        """Release the captured graphs (they hold the collective calls), then the
+        communicator or the peer table."""
         lib = _lib.load()
         lib.sf_release_graphs()
         self.__dict__.pop("_statics", None)
         if self._tp[2] is not None:
             _lib.check(lib.sf_tp_comm_destroy(self._tp[2]), "tp communicator")
+        if getattr(self, "_tp_peers", None):
+            _lib.check(lib.sf_tp_peers_destroy(self._tp_peers), "tp peer table")
+            self._tp_peers = None
+            self._tp_xbuf = None
         self._tp = (0, 1, None)
 
     @staticmethod
@@ -409,7 +449,7 @@ class FoldedVerifyB200:
             # them (looked up first: a decode step skips the per-layer walk)
             fast = (dev.index, dtype, B1, N, "store", past_key_values._store.data_ptr(),
                     past_key_values.capacity, bucket, bool(self.record_masks), tp_size, tp_comm,
-                    bool(commit), bool(shift))
+                    getattr(self, "_tp_peers", None), bool(commit), bool(shift))
             st = statics.get(fast)
             if st is not None:
                 return st
@@ -437,7 +477,8 @@ class FoldedVerifyB200:
             key = fast
         else:
             key = (dev.index, dtype, B1, N, P, bucket, bool(self.record_masks), kv_stride,
-                   tuple(kv), tp_size, tp_comm, bool(commit), bool(shift))
+                   tuple(kv), tp_size, tp_comm, getattr(self, "_tp_peers", None), bool(commit),
+                   bool(shift))
             st = statics.get(key)
             if st is not None:
                 return st
@@ -516,6 +557,7 @@ class FoldedVerifyB200:
         args.err = slab[L + L * B1:].data_ptr()
         args.tp_comm = tp_comm
         args.tp_size = tp_size
+        args.tp_peers = getattr(self, "_tp_peers", None) if tp_size > 1 else None
         st["layer_arr"] = layer_arr
         st["args"] = args
         if len(statics) >= 12:      # a decode keeps one state per branch count + the commit

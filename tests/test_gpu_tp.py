@@ -1,8 +1,9 @@
 """Tensor-parallel folded verify forward (the 14B configuration's scheme) on 2 GPUs:
-each rank holds a head / intermediate shard, o_proj and down are all-reduced over NCCL,
-and every rank must return the oracle's logits and fold masks (same tolerances as the
-single-GPU forward).  Runs as two child processes, one per GPU; skipped with fewer than
-two GPUs."""
+each rank holds a head / intermediate shard, the o_proj and down partial sums are reduced
+across the ranks -- by the consuming kernels reading every rank's partials over NVLink
+("p2p", the default) or by NCCL all-reduces ("nccl") -- and every rank must return the
+oracle's logits and fold masks (same tolerances as the single-GPU forward), identical on
+both ranks.  Runs as two child processes, one per GPU; skipped with fewer than two GPUs."""
 import os
 import socket
 import sys
@@ -23,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, ws, port, name, out):
+def _worker(rank, ws, port, name, transport, out):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
@@ -46,7 +47,7 @@ def _worker(rank, ws, port, name, out):
         cls = SpecFoldB200FastDLLMV2Generation if family == "fastdllm" else SpecFoldB200NLDGeneration
         gen = cls(model_executor=StandinExecutor(to_cuda_model(model)), delta=delta)
         gen.record_masks = True
-        gen.set_tensor_parallel(rank, ws)
+        gen.set_tensor_parallel(rank, ws, transport=transport)
         cache_d = None if cache is None else cache.to("cuda")
         last = None
         for _ in range(3):     # direct, captured, replayed
@@ -65,13 +66,14 @@ def _worker(rank, ws, port, name, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("name", CASES)
-def test_tensor_parallel_two_ranks(name):
+def test_tensor_parallel_two_ranks(name, transport):
     ws = 2
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    mp.start_processes(_worker, args=(ws, _free_port(), name, out), nprocs=ws, join=True,
-                       start_method="spawn")
+    mp.start_processes(_worker, args=(ws, _free_port(), name, transport, out), nprocs=ws,
+                       join=True, start_method="spawn")
     for r in range(ws):
         assert out[r][1] == "ok", f"rank {r}: {out[r][1]}"
     assert torch.equal(out[0][0], out[1][0]), "ranks disagree"
