@@ -273,7 +273,9 @@ typedef struct sf_verify_args {
    *   keys (after RoPE) and values into prefix_k / prefix_v at positions [P', P' + N),
    *   P' = *P_dev or P -- the append of the reference's cache update
    *   (fastdllm_v2_generation.py:562-568 -> DynamicCache.update); the prefix tensors are
-   *   then written, and kv_head_stride must be >= (P + N) * hd. */
+   *   then written, and kv_head_stride must be >= (P + N) * hd.  A commit forward may
+   *   pass logits == NULL: the last layer's combine, the final norm and the LM head are
+   *   then skipped (the prompt blocks of a prefill, whose logits are not read). */
   const int32_t* P_dev;
   int commit;
   /* tensor parallelism over peer memory (sf_tp_peers_init) instead of tp_comm: the

@@ -641,7 +641,7 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
   if (static_cast<size_t>(B1) * D * esize(dtype) > static_cast<size_t>(kMaxGateSmem))
     return fail(SF_ERR_ARG, "B1*D too large for the gate");
   if (!a->layers || !a->final_norm_w || !a->lm_w || !a->par_idx || !a->hidden_in || !a->cos ||
-      !a->sin || !a->logits || !a->count_slab || !a->segcnt_slab || !a->ws)
+      !a->sin || (!a->logits && !a->commit) || !a->count_slab || !a->segcnt_slab || !a->ws)
     return fail(SF_ERR_ARG, "null pointer in verify args");
   if (a->P < 0 || (a->P > 0 && a->kv_head_stride < static_cast<int64_t>(a->P) * hd))
     return fail(SF_ERR_ARG, "prefix length / stride mismatch");
@@ -1017,6 +1017,8 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     if ((s = timed(K_GATEUP, st, [&] { return run_gemm(gu, st, "gate/up"); }))) return s;
     if ((s = timed(K_DOWN, st, [&] { return run_gemm(dn, st, "down"); }))) return s;
   }
+  // a commit forward whose logits nobody reads (a prompt block of a prefill) ends here
+  if (a->logits == nullptr) return SF_OK;
   // last layer's combine, final norm, lm_head
   if ((s = timed(K_COMBINE, st, [&] {
          return cuda_status(launch_combine(dtype, b.hp, b.ffn, b.src, b.hbuf, B1, N, D, a->err, st),

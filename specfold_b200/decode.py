@@ -49,11 +49,15 @@ class B200Executor:
     ``generator`` is a ``SpecFoldB200*Generation`` (it owns the packed weights and the
     per-configuration state); ``capacity`` sizes a new cache (rows per layer)."""
 
-    def __init__(self, generator, block: int = 32, capacity: int = 4096, logit_bias=None):
+    def __init__(self, generator, block: int = 32, capacity: int = 4096, logit_bias=None,
+                 all_logits: bool = False):
         self.gen = generator
         self.block = block
         self.capacity = capacity
         self.logit_bias = logit_bias
+        # False: a multi-block prefill returns the logits of its last block only (the rows
+        # the loops read); True: of every block, as the model's forward does
+        self.all_logits = all_logits
         self.model = generator.model_executor.model
 
     def new_cache(self, device) -> PreallocatedKVCache:
@@ -90,11 +94,17 @@ class B200Executor:
             return ExecutorOutput(self._bias(logits, P), past_key_values)
         if T % self.block:
             raise ValueError(f"prefill / commit of {T} tokens: a multiple of {self.block} expected")
+        # every block is committed; the logits of the last one are the ones the loops read
+        # (the next token, fastdllm_v2_generation.py:522-524 / :571), so the earlier blocks
+        # skip the LM head unless all_logits
         outs = []
         for s in range(0, T, self.block):
             P = cache.get_seq_length()
-            lg = self.gen.commit_block_forward(input_seq[:, s:s + self.block], cache)
-            outs.append(self._bias(lg, P))
+            last = s + self.block >= T
+            lg = self.gen.commit_block_forward(input_seq[:, s:s + self.block], cache,
+                                               logits=last or self.all_logits)
+            if lg is not None:
+                outs.append(self._bias(lg, P))
         return ExecutorOutput(outs[0] if len(outs) == 1 else torch.cat(outs, dim=1), cache)
 
 

@@ -295,14 +295,16 @@ class FoldedVerifyB200:
         return logits
 
     @torch.no_grad()
-    def commit_block_forward(self, block: torch.Tensor, cache) -> torch.Tensor:
+    def commit_block_forward(self, block: torch.Tensor, cache, logits: bool = True):
         """The block commit forward of the decoding loops on the same kernels: the dense
         forward of one block [1, N] against the running prefix with every layer's keys
         and values of the block appended to ``cache`` (a PreallocatedKVCache) at
         positions [P, P + N) -- the executor call with update_past_key_values=True
         (fastdllm_v2_generation.py:562-568; nld_generation.py:283-289), which the
         reference runs as the model's dense forward plus DynamicCache.update.  Returns
-        the model's unshifted logits [1, N, V] (the loop reads the last position's)."""
+        the model's unshifted logits [1, N, V] (the loop reads the last position's), or
+        None with ``logits=False``, which skips the final norm and the LM head (the prompt
+        blocks of a prefill)."""
         from .kv_cache import PreallocatedKVCache
         if not isinstance(cache, PreallocatedKVCache):
             raise TypeError("the commit forward appends to a PreallocatedKVCache")
@@ -310,13 +312,13 @@ class FoldedVerifyB200:
             raise ValueError(f"the commit forward takes one block [1, N], got {tuple(block.shape)}")
         N = block.shape[1]
         cache.reserve(N)
-        logits, _ = self._run(block, cache, N, count_stats=False, delta=-1.0, commit=True,
-                              shift=False)
+        out, _ = self._run(block, cache, N, count_stats=False, delta=-1.0, commit=True,
+                           shift=False, want_logits=logits)
         cache.advance(N)
-        return logits
+        return out
 
     def _run(self, batched_input, past_key_values, bucket, count_stats=True, delta=None,
-             commit=False, shift=None):
+             commit=False, shift=None, want_logits=True):
         lib = _lib.load()
         m_ = self.model_executor.model
         base = self._base()
@@ -336,7 +338,7 @@ class FoldedVerifyB200:
         dtype = emb.weight.dtype if table else hidden.dtype
         shift = (self.family == "fastdllm") if shift is None else bool(shift)
         st = self._static_state(batched_input, past_key_values, dtype, P, bucket,
-                                commit=commit, shift=shift)
+                                commit=commit, shift=shift, want_logits=want_logits)
         L = st["L"]
         if st["P_dev"] is not None:
             # one state (and captured graph) for every prefix length of the cache: the
@@ -363,7 +365,9 @@ class FoldedVerifyB200:
         st["args"].stream = stream.cuda_stream
         st["args"].delta = self.delta if delta is None else float(delta)
         _lib.check(lib.sf_folded_verify_forward(st["args"]), "folded verify forward")
-        logits = st["logits"].clone() if self.copy_logits else st["logits"]
+        logits = st["logits"]
+        if logits is not None and self.copy_logits:
+            logits = logits.clone()
         rec = st["rec"].clone() if st["rec"] is not None else None
 
         if rec is not None:
@@ -417,7 +421,7 @@ class FoldedVerifyB200:
             self._settle(st)
 
     def _static_state(self, batched_input, past_key_values, dtype, P, bucket, commit=False,
-                      shift=True) -> dict:
+                      shift=True, want_logits=True) -> dict:
         """Buffers and the C argument struct of one configuration (shape, prefix cache
         tensors, bucket), kept at fixed addresses across calls so that the library
         replays its CUDA graph of the forward.  RoPE tables and the query scale depend
@@ -449,7 +453,8 @@ class FoldedVerifyB200:
             # them (looked up first: a decode step skips the per-layer walk)
             fast = (dev.index, dtype, B1, N, "store", past_key_values._store.data_ptr(),
                     past_key_values.capacity, bucket, bool(self.record_masks), tp_size, tp_comm,
-                    getattr(self, "_tp_peers", None), bool(commit), bool(shift))
+                    getattr(self, "_tp_peers", None), bool(commit), bool(shift),
+                    bool(want_logits))
             st = statics.get(fast)
             if st is not None:
                 return st
@@ -478,7 +483,7 @@ class FoldedVerifyB200:
         else:
             key = (dev.index, dtype, B1, N, P, bucket, bool(self.record_masks), kv_stride,
                    tuple(kv), tp_size, tp_comm, getattr(self, "_tp_peers", None), bool(commit),
-                   bool(shift))
+                   bool(shift), bool(want_logits))
             st = statics.get(key)
             if st is not None:
                 return st
@@ -508,7 +513,7 @@ class FoldedVerifyB200:
             st["q_scale"] = None if qs_all is None else qs_all[P:P + N].clone()
         st["hidden"] = torch.empty(BN, D, dtype=dtype, device=dev)
         st["par"] = torch.zeros(B1, dtype=torch.int64, device=dev)
-        st["logits"] = torch.empty(B1, N, V, dtype=dtype, device=dev)
+        st["logits"] = torch.empty(B1, N, V, dtype=dtype, device=dev) if want_logits else None
         st["slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32, device=dev)
         st["host_slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32).pin_memory()
         st["rec"] = torch.zeros(L * BN, dtype=torch.int8, device=dev) if self.record_masks else None
@@ -548,7 +553,7 @@ class FoldedVerifyB200:
         args.hidden_in = st["hidden"].data_ptr()
         args.cos, args.sin = st["cos"].data_ptr(), st["sin"].data_ptr()
         args.q_scale = None if st["q_scale"] is None else st["q_scale"].data_ptr()
-        args.logits = st["logits"].data_ptr()
+        args.logits = None if st["logits"] is None else st["logits"].data_ptr()
         args.count_slab = slab[:L].data_ptr()
         args.segcnt_slab = slab[L:L + L * B1].data_ptr()
         args.rec_slab = None if st["rec"] is None else st["rec"].data_ptr()
