@@ -44,11 +44,6 @@ struct AttnTcParams {
   // (splits = kv_splits(P)); the kernel derives the split layout of the actual length the
   // way the host does, and the splits beyond it write empty partials (m = -inf, l = 0).
   const int32_t* P_dev;
-  // grid order: 0 = (kv head, split) fastest, query tiles slowest (the live tiles fill the
-  // first wave); 1 = query tiles fastest, so that the tiles sharing a (kv head, split)
-  // run together and re-read its keys and values from L2 (long prefixes, whose K/V
-  // exceed L2)
-  int qt_fastest;
 };
 
 // key splits of a prefix of P keys: at least kKeysPerSplit keys each, at most kMaxKvSplits
@@ -116,9 +111,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   }
   pdl_trigger();
   pdl_wait();
-  const int kvh = p.qt_fastest ? blockIdx.y : blockIdx.x;
-  const int split = p.qt_fastest ? blockIdx.z : blockIdx.y;
-  const int qt = p.qt_fastest ? blockIdx.x : blockIdx.z;
+  const int kvh = blockIdx.x, split = blockIdx.y, qt = blockIdx.z;
   const int count = min(*p.count, p.bucket);
   const int Mq = count * p.G;
   const int q0 = qt * kQT;
@@ -460,14 +453,11 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
     configured = static_cast<int>(smem);
   }
   // (kv head, split) fastest: the CTAs of the live query tiles (count * G rows, known
-  // only on the device) come first in launch order and run in the first wave.  When the
-  // prefix's K/V exceed a quarter of L2, query tiles go fastest instead: the tiles of one
-  // (kv head, split) then read the same key blocks together, once from HBM (measured at
-  // P = 32768 on the 8B shape: 933 MB of DRAM reads for 134 MB of K/V in the first order)
-  const size_t kv_bytes = 2ull * a.P * a.Hkv * HD * 2;
-  p.qt_fastest = kv_bytes > (32ull << 20) ? 1 : 0;
-  const int n_qt = (q_rows + kQT - 1) / kQT;
-  dim3 grid = p.qt_fastest ? dim3(n_qt, a.Hkv, S) : dim3(a.Hkv, S, n_qt);
+  // only on the device) come first in launch order and run in the first wave.  (Query
+  // tiles fastest, so that the tiles of one key split read it from L2 together, cut the
+  // DRAM reads at P = 32768 on the 8B shape from 933 MB but was 5-10 us slower at every
+  // prefix >= 16K: the kernel is not DRAM-bound there, and the dead tiles interleave.)
+  dim3 grid(a.Hkv, S, (q_rows + kQT - 1) / kQT);
   cudaError_t e = launch_ex(attn_prefix_kernel<HD>, grid, dim3(kAttThreads), smem, st, false, tq,
                             tk, tv, p);
   if (e == cudaSuccess) e = launched();
