@@ -303,6 +303,13 @@ int sf_tp_comm_destroy(void* comm);
 size_t sf_tp_exchange_bytes(int BN, int D);
 int sf_tp_peers_init(int rank, int size, void* const* xbufs, int BN, int D, void** peers_out);
 int sf_tp_peers_destroy(void* peers);
+/* CUDA IPC of the exchange buffers (64-byte handles): sf_tp_ipc_export gives the handle
+ * of the allocation holding `ptr` and ptr's offset in it; sf_tp_ipc_open maps a peer's
+ * allocation into the CURRENT device's context (peer access enabled for it), the
+ * buffer is then base + offset; sf_tp_ipc_close unmaps it. */
+int sf_tp_ipc_export(const void* ptr, void* handle_out, int bytes, size_t* offset_out);
+int sf_tp_ipc_open(const void* handle, int bytes, void** base_out);
+int sf_tp_ipc_close(void* base);
 /* Destroys every CUDA graph the forward captured (all devices). */
 int sf_release_graphs(void);
 

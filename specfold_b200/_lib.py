@@ -101,6 +101,9 @@ _SIGS = {
     "sf_tp_peers_init": (c_int, [c_int, c_int, C.POINTER(c_void_p), c_int, c_int,
                                  C.POINTER(c_void_p)]),
     "sf_tp_peers_destroy": (c_int, [c_void_p]),
+    "sf_tp_ipc_export": (c_int, [c_void_p, c_void_p, c_int, C.POINTER(c_size_t)]),
+    "sf_tp_ipc_open": (c_int, [c_void_p, c_int, C.POINTER(c_void_p)]),
+    "sf_tp_ipc_close": (c_int, [c_void_p]),
     "sf_release_graphs": (c_int, []),
     "sf_pack_weight_tiles": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                      c_void_p]),

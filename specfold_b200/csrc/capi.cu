@@ -1,5 +1,6 @@
 // extern "C" entry points of libspecfold_b200 (declared in include/specfold_b200.h) and
 // the whole-forward layer loop.
+#include <cstring>
 #include <cstdarg>
 #include <cstdio>
 #include <atomic>
@@ -1221,6 +1222,57 @@ int sf_tp_peers_init(int rank, int size, void* const* xbufs, int BN, int D, void
 int sf_tp_peers_destroy(void* peers) {
   delete static_cast<TpPeers*>(peers);
   return SF_OK;
+}
+
+// CUDA IPC of an exchange buffer.  The buffer may sit inside a larger allocation (a caching
+// allocator's block): the handle names the allocation and the offset locates the buffer.
+// Opening maps the peer's allocation into the CURRENT device's context, with peer access
+// enabled for it -- the device whose kernels read it.
+namespace {
+using AddrRangeFn = int (*)(unsigned long long*, size_t*, unsigned long long);
+AddrRangeFn addr_range_fn() {
+  static AddrRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddrRangeFn>(ptr);
+  });
+  return fn;
+}
+}  // namespace
+
+int sf_tp_ipc_export(const void* ptr, void* handle_out, int bytes, size_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out || bytes < static_cast<int>(sizeof(cudaIpcMemHandle_t)))
+    return fail(SF_ERR_ARG, "ipc export: bad arguments");
+  AddrRangeFn fn = addr_range_fn();
+  if (!fn) return fail(SF_ERR_UNSUPPORTED, "cuMemGetAddressRange not available");
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<unsigned long long>(ptr)) != 0)
+    return fail(SF_ERR_ARG, "ipc export: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  int s = cuda_status(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle");
+  if (s) return s;
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base);
+  return SF_OK;
+}
+
+int sf_tp_ipc_open(const void* handle, int bytes, void** base_out) {
+  if (!handle || !base_out || bytes < static_cast<int>(sizeof(cudaIpcMemHandle_t)))
+    return fail(SF_ERR_ARG, "ipc open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess),
+                     "cudaIpcOpenMemHandle");
+}
+
+int sf_tp_ipc_close(void* base) {
+  if (!base) return fail(SF_ERR_ARG, "ipc close: null pointer");
+  return cuda_status(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
 }
 
 int sf_tp_comm_destroy(void* comm) {

@@ -162,16 +162,25 @@ class FoldedVerifyB200:
             nbytes = lib.sf_tp_exchange_bytes(max_rows, D)
             xbuf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
             torch.cuda.synchronize(dev)
+            h = (ctypes.c_char * 64)()
+            off = ctypes.c_size_t()
+            _lib.check(lib.sf_tp_ipc_export(xbuf.data_ptr(), ctypes.cast(h, ctypes.c_void_p), 64,
+                                            ctypes.byref(off)), "tp ipc export")
             handles = [None] * size
-            dist.all_gather_object(handles, xbuf.untyped_storage()._share_cuda_())
+            dist.all_gather_object(handles, (bytes(h), off.value))
+            # each peer's buffer mapped into THIS device's context (the kernels reading it
+            # run here)
             mapped, ptrs = [], []
             for q in range(size):
                 if q == rank:
                     ptrs.append(xbuf.data_ptr())
-                else:
-                    st = torch.UntypedStorage._new_shared_cuda(*handles[q])
-                    mapped.append(st)
-                    ptrs.append(st.data_ptr())
+                    continue
+                hq = (ctypes.c_char * 64).from_buffer_copy(handles[q][0])
+                base = ctypes.c_void_p()
+                _lib.check(lib.sf_tp_ipc_open(ctypes.cast(hq, ctypes.c_void_p), 64,
+                                              ctypes.byref(base)), "tp ipc open")
+                mapped.append(base.value)
+                ptrs.append(base.value + handles[q][1])
             peers = ctypes.c_void_p()
             _lib.check(lib.sf_tp_peers_init(rank, size, (ctypes.c_void_p * size)(*ptrs), max_rows,
                                             D, ctypes.byref(peers)), "tp peer table")
@@ -195,6 +204,10 @@ class FoldedVerifyB200:
         if getattr(self, "_tp_peers", None):
             _lib.check(lib.sf_tp_peers_destroy(self._tp_peers), "tp peer table")
             self._tp_peers = None
+            xbuf, mapped = self._tp_xbuf
+            torch.cuda.synchronize()
+            for base in mapped:
+                _lib.check(lib.sf_tp_ipc_close(base), "tp ipc close")
             self._tp_xbuf = None
         self._tp = (0, 1, None)
 
