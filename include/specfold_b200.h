@@ -282,6 +282,14 @@ typedef struct sf_verify_args {
    * o_proj and down partial sums stay in each rank's exchange buffer and the kernels
    * that consume them read every rank's partial over NVLink (no NCCL on the layer path). */
   void* tp_peers;
+  /* prefill != 0 (with commit, a negative delta and shift_logits 0): the B1 "branches"
+   * are B1 consecutive blocks of N prompt tokens at positions [P', P' + B1 * N) -- one
+   * block-causal forward instead of B1 commit forwards.  Every layer appends all B1 * N
+   * rows' keys and values to the cache before its attention; row (b, n) attends to the
+   * cache's first P' + b * N keys and to its own block bidirectionally.  cos / sin (and
+   * q_scale) hold B1 * N rows; logits, when not NULL, are [1, N, V] of the last block;
+   * kv_head_stride must be >= (P + B1 * N) * hd. */
+  int prefill;
 } sf_verify_args;
 
 /* Tensor-parallel communicator (NCCL, loaded at run time).  Rank 0 calls

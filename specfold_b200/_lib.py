@@ -41,7 +41,7 @@ class SfVerifyArgs(C.Structure):
         ("segcnt_slab", c_void_p), ("rec_slab", c_void_p), ("ws", c_void_p),
         ("ws_bytes", c_size_t), ("err", c_void_p), ("stream", c_void_p),
         ("tp_comm", c_void_p), ("tp_size", c_int),
-        ("P_dev", c_void_p), ("commit", c_int), ("tp_peers", c_void_p),
+        ("P_dev", c_void_p), ("commit", c_int), ("tp_peers", c_void_p), ("prefill", c_int),
     ]
 
 

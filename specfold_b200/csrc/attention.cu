@@ -249,7 +249,9 @@ __global__ void __launch_bounds__(256) attn_rows_kernel(AttnParams p, const floa
   }
   __syncthreads();
 
-  const int P = prefix_len(p.P_dev, p.P, p.err);
+  // prefix keys this branch sees: all P' (verify), or P' + b * N (prefill block b)
+  const KeyRange kr = attn_keys(p.P_dev, p.P, p.prefill_rows, p.err);
+  const int P = p.prefill_rows > 0 ? kr.base + b * p.N : kr.keys;
   const int key_begin = part_O != nullptr ? P : 0;
   const int total = P + p.N;
   float kv[TILE_VEC][V], vv[TILE_VEC][V];

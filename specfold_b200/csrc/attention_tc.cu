@@ -44,6 +44,9 @@ struct AttnTcParams {
   // (splits = kv_splits(P)); the kernel derives the split layout of the actual length the
   // way the host does, and the splits beyond it write empty partials (m = -inf, l = 0).
   const int32_t* P_dev;
+  // batched prefill: rows of the prefill blocks (0 = off) and the block length; query
+  // row of flat block row r attends to keys [0, P' + (r / block_N) * block_N)
+  int prefill_rows, block_N;
 };
 
 // key splits of a prefix of P keys: at least kKeysPerSplit keys each, at most kMaxKvSplits
@@ -116,13 +119,23 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   const int Mq = count * p.G;
   const int q0 = qt * kQT;
   if (q0 >= Mq) return;                        // uniform per CTA
-  int P = p.P, kps = p.keys_per_split;
-  if (p.P_dev != nullptr) {
-    P = prefix_len(p.P_dev, p.P, p.err);
+  int P = p.P, kps = p.keys_per_split, P_base = p.P;
+  if (p.P_dev != nullptr || p.prefill_rows > 0) {
+    const KeyRange kr = attn_keys(p.P_dev, p.P, p.prefill_rows, p.err);
+    P = kr.keys;
+    P_base = kr.base;
     kps = keys_per_split_of(P, kv_splits_of(P));
   }
+  // per query row: the keys it may see (prefill: its block's prefix; otherwise all P)
+  auto row_limit = [&](int qi) -> int {
+    if (p.prefill_rows == 0) return P;
+    const int slot = min(qi, Mq - 1) / p.G;
+    const int64_t fr = p.rows != nullptr ? p.rows[slot] : slot;
+    return P_base + static_cast<int>(fr / p.block_N) * p.block_N;
+  };
   const int k_begin = split * kps;
-  const int k_end = min(P, k_begin + kps);
+  // the tile's last row has the largest limit (rows ascend within a tile)
+  const int k_end = min(min(P, row_limit(min(q0 + kQT, Mq) - 1)), k_begin + kps);
   const int nb = k_end > k_begin ? (k_end - k_begin + kKB - 1) / kKB : 0;
 
   if (threadIdx.x == 0) {
@@ -219,12 +232,13 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     const float sl2 = p.scale * 1.4426950408889634f;     // scores in log2 units
     float m = -INFINITY, l = 0.f;                         // m: full row; l: this half's keys
     bool ok = true;
+    const int k_row = min(k_end, row_limit(q0 + r));      // this row's keys end here
     for (int i = 0; i < nb; ++i) {
       ok = softmax_vote(ok && !*abort_flag && mbar_wait(&s_full[i & 1], (i >> 1) & 1, p.err));
       if (!ok) break;
       tc_fence_after();
       const uint32_t tS = tmem + (i & 1) * kKB + hh * HALF_KEYS;
-      const int nv = min(kKB, k_end - (k_begin + i * kKB)) - hh * HALF_KEYS;   // valid keys here
+      const int nv = min(kKB, k_row - (k_begin + i * kKB)) - hh * HALF_KEYS;   // valid keys here
       float v[HALF_KEYS];
 #pragma unroll
       for (int c = 0; c < HALF_KEYS; c += 16) tmem_ld16(tS + lane_off + c, v + c);
@@ -236,7 +250,10 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       s_red[hh * kQT + r] = mx;
       asm volatile("bar.sync 1, 256;" ::: "memory");
       const float mn = fmaxf(m, fmaxf(mx, s_red[(hh ^ 1) * kQT + r]));
-      const float alpha = exp2f(m - mn);
+      // a row with no valid key yet (prefill rows whose limit ends before this block)
+      // keeps m = -inf: exponents then use 0 as the reference, and every term is zero
+      const float mref = mn == -INFINITY ? 0.f : mn;
+      const float alpha = exp2f(m - mref);
       if (i > 0) {
         // P V of the previous block must be done: it reads sP and accumulates into O
         ok = softmax_vote(mbar_wait(pv_done, (i - 1) & 1, p.err));
@@ -267,8 +284,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 #pragma unroll
         for (int h2 = 0; h2 < 4; ++h2) {
           const int j0 = g8 * 8 + 2 * h2;
-          const float e0 = j0 < nv ? exp2f(fmaf(v[j0], sl2, -mn)) : 0.f;
-          const float e1 = j0 + 1 < nv ? exp2f(fmaf(v[j0 + 1], sl2, -mn)) : 0.f;
+          const float e0 = j0 < nv ? exp2f(fmaf(v[j0], sl2, -mref)) : 0.f;
+          const float e1 = j0 + 1 < nv ? exp2f(fmaf(v[j0 + 1], sl2, -mref)) : 0.f;
           sum += e0 + e1;
           const __nv_bfloat162 b2 = __floats2bfloat162_rn(e0, e1);
           pk[h2] = *reinterpret_cast<const uint32_t*>(&b2);
@@ -430,6 +447,8 @@ static cudaError_t prefix_partials(const AttnParams& a, cudaStream_t st, PrefixP
   p.splits = S;
   p.keys_per_split = keys_per_split_of(a.P, S);
   p.P_dev = a.P_dev;
+  p.prefill_rows = a.prefill_rows;
+  p.block_N = a.N;
   p.Hkv = a.Hkv;
   p.scale = a.scale;
   p.part_rows = std::max(a.bucket, rows_total) * G;

@@ -656,10 +656,17 @@ int sf_folded_verify_forward(const sf_verify_args* a) {
                               "%d / %lld", tp->size, static_cast<long long>(tp->part_elems),
                   a->tp_size, static_cast<long long>(BN) * D);
   }
-  if (a->commit && (B1 != 1 || a->kv_head_stride < static_cast<int64_t>(a->P + N) * hd ||
-                    hd % 8 != 0))
-    return fail(SF_ERR_ARG, "commit forward needs B1 == 1 and kv_head_stride >= (P + N) * hd");
-  FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket, a->P);
+  if (a->commit && ((B1 != 1 && !a->prefill) ||
+                    a->kv_head_stride < static_cast<int64_t>(a->P + BN) * hd || hd % 8 != 0))
+    return fail(SF_ERR_ARG, "commit forward needs B1 == 1 (or prefill) and kv_head_stride >= "
+                            "(P + B1 * N) * hd");
+  if (a->prefill && (!a->commit || a->delta >= 0.f || a->shift_logits || a->tp_size > 1))
+    return fail(SF_ERR_ARG, "prefill needs commit, a negative delta (dense), no logit shift "
+                            "and no tensor parallelism");
+  // prefill: the attention covers the prompt blocks' keys as well (its scratch is sized
+  // for P + B1 * N keys; sf_verify_workspace_bytes with that P gives the size)
+  FwdBufs b = carve_forward(a->ws, dtype, B1, N, D, H, Hkv, hd, I, V, bucket,
+                            a->P + (a->prefill ? BN : 0));
   if (b.total > a->ws_bytes)
     return fail(SF_ERR_WORKSPACE, "workspace %zu < %zu bytes", a->ws_bytes, b.total);
   for (int li = 0; li < L; ++li) {
@@ -777,7 +784,8 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     q.epi.q_dim = qd;
     q.epi.kv_dim = kvd;
     q.epi.hd = hd;
-    q.epi.N = N;
+    // prefill: every row has its own position (RoPE tables of B1 * N rows)
+    q.epi.N = a->prefill ? BN : N;
     q.epi.q_comp = b.q_comp;
     q.epi.q_comp_rows = bucket * (H / Hkv);
     q.ws = b.gemm_ws;
@@ -814,11 +822,22 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
     at.scratch_bytes = b.attn_ws_bytes;
     at.rec = rec;
     at.P_dev = a->P_dev;
+    if (a->prefill) {
+      // every block's keys and values join the cache first: block b attends to the
+      // prefix and blocks 0..b-1 there, and to itself from kv_buf
+      if ((s = cuda_status(launch_kv_commit(dtype, b.kv_buf, const_cast<void*>(ly.prefix_k),
+                                            const_cast<void*>(ly.prefix_v), a->kv_head_stride,
+                                            a->P_dev, a->P, BN, Hkv, hd, a->err, st),
+                           "kv commit (prefill)")))
+        return s;
+      at.prefill_rows = BN;
+      at.P = a->P + BN;
+    }
     // every row: recomputed rows attend with their own query, folded rows are rebuilt
     // from their recomputing ancestor's query and retained prefix state
     if ((s = timed(K_ATTN, st, [&] { return cuda_status(launch_attention_rows(dtype, at, st), "attention"); })))
       return s;
-    if (a->commit) {
+    if (a->commit && !a->prefill) {
       // the committed block's keys and values join the prefix cache (its rows [P', P' + N)
       // are not read by this layer's attention, which covers [0, P'))
       if ((s = cuda_status(launch_kv_commit(dtype, b.kv_buf, const_cast<void*>(ly.prefix_k),
@@ -1027,9 +1046,12 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
        })))
     return s;
   RmsRowsParams r{};
-  r.x = b.hbuf;
-  r.n = BN;
-  r.n_src = BN;
+  // prefill: the logits of the last block only ([1, N, V], the rows a decode loop reads)
+  const int lm_rows = a->prefill ? N : BN;
+  const size_t lm_off = static_cast<size_t>(BN - lm_rows) * D * esize(dtype);
+  r.x = static_cast<const char*>(b.hbuf) + lm_off;
+  r.n = lm_rows;
+  r.n_src = lm_rows;
   r.w = a->final_norm_w;
   r.out = b.xn;
   r.D = D;
@@ -1044,7 +1066,7 @@ static int forward_launches(const sf_verify_args* a, const FwdBufs& b, cudaStrea
   lm.w_tiled = a->weights_tiled;
   lm.n_out = V;
   lm.K = D;
-  lm.rows_cap = BN;
+  lm.rows_cap = lm_rows;
   lm.epi.kind = EPI_LOGITS;
   lm.epi.out = a->logits;
   lm.epi.ld_out = V;

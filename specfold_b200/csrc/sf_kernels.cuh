@@ -259,6 +259,12 @@ struct AttnParams {
   // prefix length read on the device when the kernel runs (decode loops: one captured
   // launch serves every prefix length); nullptr = P.  P then bounds it and sizes the grid.
   const int32_t* P_dev;
+  // batched prefill (block-causal): the B1 branches are consecutive blocks of N tokens
+  // whose keys and values are already in the cache after the prefix; P (and *P_dev)
+  // count the prefix before them and row (b, n) attends to the cache's first
+  // P' + b * N keys plus its own block.  prefill_rows = B1 * N (0 = off); the launcher
+  // passes P + prefill_rows as the key bound.
+  int prefill_rows;
 };
 
 // The prefix length a kernel attends to: *P_dev when given, clamped to the bound P the
@@ -271,6 +277,17 @@ __device__ __forceinline__ int prefix_len(const int32_t* P_dev, int P, int* err)
     return v < 0 ? 0 : P;
   }
   return v;
+}
+
+// keys of the cache an attention launch covers: P' = the prefix before any prefill rows,
+// keys = P' + prefill_rows (a prefill block b sees P' + b * N of them)
+struct KeyRange {
+  int base, keys;
+};
+__device__ __forceinline__ KeyRange attn_keys(const int32_t* P_dev, int P_bound, int prefill_rows,
+                                              int* err) {
+  const int base = prefix_len(P_dev, P_bound - prefill_rows, err);
+  return {base, base + prefill_rows};
 }
 // rows_total > 0: room for partials indexed by flat block row (launch_attention_rows)
 size_t attn_scratch_bytes(int dtype, int bucket, int H, int Hkv, int hd, int P,

@@ -17,10 +17,11 @@ computed, cache hits -- are those of the reference loop.
 
 ``B200Executor`` stands in for ``FastDLLMModelExecutor.forward`` (fastdllm_model_executor.
 py:59-107), whose Fast-dLLM v2 model code is HF remote code outside the reference: the
-prefill and the block commit run the dense block forward on the same kernels, one block
-at a time (each block attends bidirectionally to itself and to every earlier block), and
-append the block's keys and values to a preallocated cache inside the forward
-(``commit_block_forward``).
+prefill and the block commit run the dense block forward on the same kernels with a
+block-causal pattern (each block attends bidirectionally to itself and to every earlier
+block) and append the blocks' keys and values to a preallocated cache inside the forward:
+``commit_block_forward`` for one block, ``prefill_forward`` for up to 16 prompt blocks per
+forward.
 """
 
 from __future__ import annotations
@@ -58,6 +59,8 @@ class B200Executor:
         # False: a multi-block prefill returns the logits of its last block only (the rows
         # the loops read); True: of every block, as the model's forward does
         self.all_logits = all_logits
+        # True: multi-block prompts use the batched block-causal prefill forward
+        self.batched_prefill = True
         self.model = generator.model_executor.model
 
     def new_cache(self, device) -> PreallocatedKVCache:
@@ -95,8 +98,14 @@ class B200Executor:
         if T % self.block:
             raise ValueError(f"prefill / commit of {T} tokens: a multiple of {self.block} expected")
         # every block is committed; the logits of the last one are the ones the loops read
-        # (the next token, fastdllm_v2_generation.py:522-524 / :571), so the earlier blocks
-        # skip the LM head unless all_logits
+        # (the next token, fastdllm_v2_generation.py:522-524 / :571).  A multi-block
+        # prompt goes through the batched block-causal prefill (one forward per 16 blocks,
+        # the same attention pattern as committing the blocks one by one) unless every
+        # block's logits are wanted
+        P0 = cache.get_seq_length()
+        if T > self.block and not self.all_logits and self.batched_prefill:
+            lg = self.gen.prefill_forward(input_seq, cache, self.block, logits=True)
+            return ExecutorOutput(self._bias(lg, P0 + T - self.block), cache)
         outs = []
         for s in range(0, T, self.block):
             P = cache.get_seq_length()

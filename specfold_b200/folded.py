@@ -330,8 +330,41 @@ class FoldedVerifyB200:
         cache.advance(N)
         return out
 
+    @torch.no_grad()
+    def prefill_forward(self, tokens: torch.Tensor, cache, block: int = 32, logits: bool = True,
+                        max_blocks: int = 16):
+        """Commit a prompt of k * block tokens ([1, T] or [T]) to a PreallocatedKVCache in
+        block-causal forwards of up to ``max_blocks`` blocks each (sf_verify_args.prefill):
+        the same result as committing the blocks one at a time -- each block attends to
+        the prefix, to the earlier blocks and to itself bidirectionally -- with the weights
+        streamed once per chunk instead of once per block.  Returns the unshifted logits
+        [1, block, V] of the last block (the executor's next-token row), or None."""
+        from .kv_cache import PreallocatedKVCache
+        if not isinstance(cache, PreallocatedKVCache):
+            raise TypeError("the prefill forward appends to a PreallocatedKVCache")
+        ids = tokens.reshape(-1)
+        T = ids.numel()
+        if T == 0 or T % block:
+            raise ValueError(f"prefill of {T} tokens: a positive multiple of {block} expected")
+        out = None
+        for s0 in range(0, T, block * max_blocks):
+            chunk = ids[s0:s0 + block * max_blocks]
+            k = chunk.numel() // block
+            last = s0 + chunk.numel() >= T
+            cache.reserve(k * block)
+            if k == 1:
+                out, _ = self._run(chunk.view(1, block), cache, block, count_stats=False,
+                                   delta=-1.0, commit=True, shift=False,
+                                   want_logits=logits and last)
+            else:
+                out, _ = self._run(chunk.view(k, block), cache, k * block, count_stats=False,
+                                   delta=-1.0, commit=True, shift=False,
+                                   want_logits=logits and last, prefill=True)
+            cache.advance(k * block)
+        return out
+
     def _run(self, batched_input, past_key_values, bucket, count_stats=True, delta=None,
-             commit=False, shift=None, want_logits=True):
+             commit=False, shift=None, want_logits=True, prefill=False):
         lib = _lib.load()
         m_ = self.model_executor.model
         base = self._base()
@@ -351,18 +384,20 @@ class FoldedVerifyB200:
         dtype = emb.weight.dtype if table else hidden.dtype
         shift = (self.family == "fastdllm") if shift is None else bool(shift)
         st = self._static_state(batched_input, past_key_values, dtype, P, bucket,
-                                commit=commit, shift=shift, want_logits=want_logits)
+                                commit=commit, shift=shift, want_logits=want_logits,
+                                prefill=prefill)
         L = st["L"]
         if st["P_dev"] is not None:
             # one state (and captured graph) for every prefix length of the cache: the
             # length and its RoPE rows go to the device, the launches stay the same
-            if P + N > st["cap"]:
-                raise ValueError(f"prefix {P} + block {N} exceeds the cache capacity {st['cap']}")
+            nr = B1 * N if prefill else N          # rows with their own positions
+            if P + nr > st["cap"]:
+                raise ValueError(f"prefix {P} + {nr} rows exceeds the cache capacity {st['cap']}")
             st["P_dev"].fill_(P)
-            st["cos"].copy_(st["cos_all"][P:P + N])
-            st["sin"].copy_(st["sin_all"][P:P + N])
+            st["cos"].copy_(st["cos_all"][P:P + nr])
+            st["sin"].copy_(st["sin_all"][P:P + nr])
             if st["q_scale"] is not None:
-                st["q_scale"].copy_(st["q_scale_all"][P:P + N])
+                st["q_scale"].copy_(st["q_scale_all"][P:P + nr])
 
         # per call: parent map on the device (the reference's :263-265 host round trip),
         # embeddings into the fixed input buffer, then the forward (a CUDA graph replay
@@ -434,7 +469,7 @@ class FoldedVerifyB200:
             self._settle(st)
 
     def _static_state(self, batched_input, past_key_values, dtype, P, bucket, commit=False,
-                      shift=True, want_logits=True) -> dict:
+                      shift=True, want_logits=True, prefill=False) -> dict:
         """Buffers and the C argument struct of one configuration (shape, prefix cache
         tensors, bucket), kept at fixed addresses across calls so that the library
         replays its CUDA graph of the forward.  RoPE tables and the query scale depend
@@ -467,7 +502,7 @@ class FoldedVerifyB200:
             fast = (dev.index, dtype, B1, N, "store", past_key_values._store.data_ptr(),
                     past_key_values.capacity, bucket, bool(self.record_masks), tp_size, tp_comm,
                     getattr(self, "_tp_peers", None), bool(commit), bool(shift),
-                    bool(want_logits))
+                    bool(want_logits), bool(prefill))
             st = statics.get(fast)
             if st is not None:
                 return st
@@ -505,16 +540,17 @@ class FoldedVerifyB200:
         I = layers[0].mlp.gate_proj.weight.shape[0] // tp_size
         V = self._head().weight.shape[0]
         scale = float(layers[0].self_attn.scaling)
-        probe = torch.zeros(1, N, D, dtype=dtype, device=dev)
-        pos = torch.arange(P, P + N, device=dev).unsqueeze(0)
+        nr = BN if prefill else N                    # rows with their own RoPE position
+        probe = torch.zeros(1, nr, D, dtype=dtype, device=dev)
+        pos = torch.arange(P, P + nr, device=dev).unsqueeze(0)
         cos, sin = base.rotary_emb(probe, pos)
         st = {"L": L, "keep": keep, "P_dev": None, "pending": None}
         st["cos"] = cos[0].to(dtype).contiguous()
         st["sin"] = sin[0].to(dtype).contiguous()
-        st["q_scale"] = self._q_scale(cfg, P, N, dev)
+        st["q_scale"] = self._q_scale(cfg, P, nr, dev)
         P_bound = P
         if prealloc:
-            P_bound = cap - N
+            P_bound = cap - nr
             st["cap"] = cap
             st["P_dev"] = torch.full((1,), P, dtype=torch.int32, device=dev)
             probe_all = torch.zeros(1, cap, D, dtype=dtype, device=dev)
@@ -523,15 +559,16 @@ class FoldedVerifyB200:
             st["sin_all"] = sin_all[0].to(dtype).contiguous()
             qs_all = self._q_scale(cfg, 0, cap, dev, force=True)
             st["q_scale_all"] = qs_all
-            st["q_scale"] = None if qs_all is None else qs_all[P:P + N].clone()
+            st["q_scale"] = None if qs_all is None else qs_all[P:P + nr].clone()
         st["hidden"] = torch.empty(BN, D, dtype=dtype, device=dev)
         st["par"] = torch.zeros(B1, dtype=torch.int64, device=dev)
-        st["logits"] = torch.empty(B1, N, V, dtype=dtype, device=dev) if want_logits else None
+        st["logits"] = (torch.empty(1 if prefill else B1, N, V, dtype=dtype, device=dev)
+                        if want_logits else None)
         st["slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32, device=dev)
         st["host_slab"] = torch.zeros(L + L * B1 + 1, dtype=torch.int32).pin_memory()
         st["rec"] = torch.zeros(L * BN, dtype=torch.int8, device=dev) if self.record_masks else None
         need = lib.sf_verify_workspace_bytes(dtype_code(st["hidden"]), B1, N, D, H, Hkv, hd, I, V,
-                                             P_bound)
+                                             P_bound + (BN if prefill else 0))
         st["ws"] = torch.empty(need, dtype=torch.uint8, device=dev)
 
         layer_arr = (_lib.SfLayer * L)()
@@ -553,6 +590,7 @@ class FoldedVerifyB200:
         args.kv_head_stride = kv_stride
         args.P_dev = None if st["P_dev"] is None else st["P_dev"].data_ptr()
         args.commit = 1 if commit else 0
+        args.prefill = 1 if prefill else 0
         args.bucket = bucket
         args.delta = self.delta
         args.eps = float(getattr(cfg, "rms_norm_eps", 1e-6))

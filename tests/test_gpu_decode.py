@@ -8,6 +8,8 @@
   device memory, so one captured graph serves every prefix length): bit-identical
   logits to the same prefix passed with a host-side length, across lengths whose key
   split counts differ, before and after graph capture.
+* The batched block-causal prefill (k prompt blocks in one forward) against the oracle
+  executor committing the blocks one at a time: cache rows and last-block logits.
 * The decode loops (specfold_b200/decode.py) against golden runs of the reference's own
   loops (``generate_with_draft_speculation``, fastdllm_v2_generation.py:483-720, with the
   reference's PyTorch folded generator, and ``generate``, :188-385), made on the CPU by
@@ -120,3 +122,51 @@ def test_decode_matches_reference_loop(name):
         assert st["drafts_computed"] == ref["drafts_computed"], f"{mode}: drafts differ"
         if mode != "vanilla":
             assert fwd == ref["forwards"], f"{mode}: branch counts of the verify calls differ"
+
+
+@pytest.mark.parametrize("name", ["tiny_fp32_tree", "tiny_bf16_tree", "tiny128_bf16"])
+@pytest.mark.parametrize("prefix", [0, 24])
+def test_batched_prefill_matches_block_commits(name, prefix):
+    """The batched block-causal prefill (sf_verify_args.prefill: k prompt blocks in one
+    forward, every block attending to the prefix, the earlier blocks and itself) against
+    the executor restatement of the oracle, which commits one block at a time
+    (oracle/decode_standin.py): the cache rows and the last block's unshifted logits."""
+    from oracle.decode_standin import GrowingCache, OracleExecutor
+    from specfold_b200 import synthetic as syn
+    if name == "tiny128_bf16":
+        dims = syn.SHAPES["tiny128"]
+        model = build_model(dims, family="fastdllm", dtype=torch.bfloat16, seed=0)
+        cache = random_prefix_cache(dims, 24, dtype=torch.bfloat16, seed=1)
+    else:
+        _, model, cache, _, _ = build_case(name)
+    dtype = next(model.parameters()).dtype
+    vocab = model.config.vocab_size
+    T = 4 * 32
+    tokens = torch.randint(0, vocab, (1, T), generator=torch.Generator().manual_seed(9))
+    L = len(model.model.layers)
+    # oracle: block-by-block commits on top of the same prefix
+    ref_cache = GrowingCache(L)
+    if prefix:
+        for li in range(L):
+            ref_cache.update(cache[li][0][:, :, :prefix].clone(), cache[li][1][:, :, :prefix].clone(), li)
+    ex = OracleExecutor(model, block=32)
+    ref = ex.forward(tokens, ref_cache if prefix else None, update_past_key_values=True)
+    ref_last = ref.logits[:, -32:]
+    gen = SpecFoldB200FastDLLMV2Generation(model_executor=StandinExecutor(to_cuda_model(model)),
+                                           delta=0.1)
+    hkv, hd = cache[0][0].shape[1], cache[0][0].shape[3]
+    pre = PreallocatedKVCache(L, hkv, hd, capacity=prefix + T + 64, dtype=dtype, device="cuda")
+    if prefix:
+        for li in range(L):
+            pre.update(cache[li][0][:, :, :prefix].cuda(), cache[li][1][:, :, :prefix].cuda(), li)
+    out = gen.prefill_forward(tokens.cuda(), pre, block=32, logits=True)
+    torch.cuda.synchronize()
+    assert pre.get_seq_length() == prefix + T
+    assert out.shape == ref_last.shape
+    assert_close(out.cpu(), ref_last, dtype, f"{name} prefill logits (last block)")
+    got_cache = ref.past_key_values
+    for li in range(L):
+        k, v = pre[li]
+        rk, rv = got_cache[li]
+        assert_close(k.cpu(), rk, dtype, f"layer {li} prefill keys")
+        assert_close(v.cpu(), rv, dtype, f"layer {li} prefill values")
