@@ -187,6 +187,8 @@ FwdBufs carve_forward(void* ws, int dtype, int B1, int N, int D, int H, int Hkv,
   g = std::max(g, ws_gemm(dtype, bucket, 2 * I, D, EPI_SWIGLU, I));
   g = std::max(g, ws_gemm(dtype, bucket, D, I, EPI_SCATTER, 0));
   g = std::max(g, ws_gemm(dtype, BN, V, D, EPI_LOGITS, 0));
+  // a prefill forward runs its LM head on the last block's N rows only
+  g = std::max(g, ws_gemm(dtype, N, V, D, EPI_LOGITS, 0));
   // the chained o_proj's partials live beside the later phases' (its split reduction is
   // deferred to the post-attention norm)
   const size_t o_ws = ws_gemm(dtype, BN, D, qd, EPI_RESID, 0);
