@@ -569,7 +569,8 @@ def run_triton_reference(args):
 def run_tp(args):
     """The 14B tensor-parallel configuration: a Llama-style 14B-shape model, tensor
     parallel over all torchrun ranks (heads and the intermediate dimension sharded, o_proj
-    and down all-reduced over NVLink), one verify stream, prefix 2048.  Strong scaling:
+    and down partials summed over NVLink: peer memory by default, NCCL with
+    SF_TP_TRANSPORT=nccl), one verify stream, prefix 2048.  Strong scaling:
     the whole group serves one stream; value = verify steps/s of that stream."""
     from specfold_b200 import SpecFoldB200NLDGeneration, _lib
     from specfold_b200 import synthetic as syn
@@ -590,8 +591,11 @@ def run_tp(args):
                                 frac_recompute=FRAC_RECOMPUTE)
     syn.inject_hidden(model, hidden.to(dev))
     gen = SpecFoldB200NLDGeneration(model_executor=syn.StandinExecutor(model), delta=DELTA)
+    transport = "one GPU"
     if ws > 1:
         gen.set_tensor_parallel(rank, ws)
+        transport = ("NCCL all-reduce" if gen._tp_transport == "nccl"
+                     else "peer memory (NVLink loads, flag handshake)")
     ids = torch.zeros(B1, N, dtype=torch.int64, device=dev)
     for _ in range(args.warmup):
         gen._batched_block_forward(ids, cache)
@@ -632,8 +636,8 @@ def run_tp(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init 14B shape)",
         "config": {"workload": "folded verify step, Llama-style 14B shape, B1=8, N=32, prefix 2048, "
                                "delta 0.1", "shape": "llama14b", "prefix": P,
-                   "parallelism": f"tp{ws} (heads / intermediate sharded; NCCL fp32 all-reduce "
-                                  "after o_proj and down)",
+                   "parallelism": f"tp{ws} (heads / intermediate sharded; fp32 partials of o_proj "
+                                  f"and down summed over {transport})",
                    "fold_ratio": round(gen.fold_ratio, 4)},
         "roofline": {"bound": "hbm", "per_gpu_bytes": int(per_gpu),
                      "achieved": round(per_gpu / (step_ms / 1e3) / 1e9, 1), "peak": hbm,

@@ -215,29 +215,57 @@ __device__ bool tp_handshake(const TpPeers& t, int kind, int seq, int* err) {
 
 __global__ void tp_epoch_kernel(unsigned* epoch) { *epoch += 1u; }
 
+// Every rank's float4 at element offsets i + k * stride (k < kU), all loads in flight
+// before any is used (the peers' are NVLink round trips); acc[k] = sum in rank order.
+// S >= t.size bounds the register array (2, 4 or 8 ranks).
+constexpr int kU = 4;
+template <int S>
+__device__ __forceinline__ void tp_gather_sum(const TpPeers& t, int64_t off, int64_t i,
+                                              int64_t stride, int64_t n, float4* acc) {
+  float4 v[S][kU];
+#pragma unroll
+  for (int q = 0; q < S; ++q)
+#pragma unroll
+    for (int k = 0; k < kU; ++k)
+      if (q < t.size && i + k * stride < n)
+        v[q][k] = __ldcv(reinterpret_cast<const float4*>(t.part[q] + off + i + k * stride));
+#pragma unroll
+  for (int k = 0; k < kU; ++k) {
+    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < S; ++q)
+      if (q < t.size && i + k * stride < n) {
+        acc[k].x += v[q][k].x; acc[k].y += v[q][k].y; acc[k].z += v[q][k].z; acc[k].w += v[q][k].w;
+      }
+  }
+}
+
 // hp[i] = T(resid[i] + T(sum_q part_q[i])), i < n (the EPI_RESID arithmetic)
-template <typename T>
+template <int S, typename T>
 __global__ void __launch_bounds__(256) tp_reduce_resid_kernel(TpPeers t, int layer, int L,
                                                               const T* __restrict__ resid,
                                                               T* out, int64_t n, int* err) {
   const int seq = static_cast<int>(*t.epoch) * 2 * L + 2 * layer;
   if (!tp_handshake(t, 0, seq, err)) return;
-  for (int64_t i = (blockIdx.x * 256ll + threadIdx.x) * 4; i < n; i += 256ll * gridDim.x * 4) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 0; q < t.size; ++q) {
-      const float4 v = __ldcv(reinterpret_cast<const float4*>(t.part[q] + i));
-      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    }
-    const float sv[4] = {acc.x, acc.y, acc.z, acc.w};
+  const int64_t stride = 256ll * gridDim.x * 4;
+  for (int64_t i = (blockIdx.x * 256ll + threadIdx.x) * 4; i < n; i += stride * kU) {
+    float4 acc[kU];
+    tp_gather_sum<S>(t, 0, i, stride, n, acc);
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      out[i + k] = Elt<T>::from_f(__fadd_rn(Elt<T>::to_f(resid[i + k]), Elt<T>::rnd(sv[k])));
+    for (int k = 0; k < kU; ++k) {
+      const int64_t e = i + k * stride;
+      if (e >= n) break;
+      const float sv[4] = {acc[k].x, acc[k].y, acc[k].z, acc[k].w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        out[e + c] = Elt<T>::from_f(__fadd_rn(Elt<T>::to_f(resid[e + c]), Elt<T>::rnd(sv[c])));
+    }
   }
 }
 
 // out[rows[j]][:] = T(sum_q part_q[j][:]) for j < min(*count, n) (the EPI_SCATTER
 // arithmetic); the down partials sit after the o_proj ones in every exchange buffer
-template <typename T>
+template <int S, typename T>
 __global__ void __launch_bounds__(256) tp_reduce_scatter_kernel(TpPeers t, int layer, int L,
                                                                 int64_t part_off,
                                                                 const int64_t* rows,
@@ -248,27 +276,30 @@ __global__ void __launch_bounds__(256) tp_reduce_scatter_kernel(TpPeers t, int l
   if (!tp_handshake(t, 1, seq, err)) return;
   const int cnt = min(*count, n);
   const int64_t total = static_cast<int64_t>(cnt) * D;
-  for (int64_t i = (blockIdx.x * 256ll + threadIdx.x) * 4; i < total; i += 256ll * gridDim.x * 4) {
-    const int64_t j = i / D, d = i % D;
-    const int64_t r = rows[j];
-    if (r < 0 || r >= n_out_rows) {
-      flag_error(err, SF_DEV_ERR_INDEX);
-      continue;
+  const int64_t stride = 256ll * gridDim.x * 4;
+  for (int64_t i = (blockIdx.x * 256ll + threadIdx.x) * 4; i < total; i += stride * kU) {
+    float4 acc[kU];
+    tp_gather_sum<S>(t, part_off, i, stride, total, acc);
+#pragma unroll
+    for (int k = 0; k < kU; ++k) {
+      const int64_t e = i + k * stride;
+      if (e >= total) break;
+      const int64_t j = e / D, d = e % D;
+      const int64_t r = rows[j];
+      if (r < 0 || r >= n_out_rows) {
+        flag_error(err, SF_DEV_ERR_INDEX);
+        continue;
+      }
+      out[r * D + d] = Elt<T>::from_f(acc[k].x);
+      out[r * D + d + 1] = Elt<T>::from_f(acc[k].y);
+      out[r * D + d + 2] = Elt<T>::from_f(acc[k].z);
+      out[r * D + d + 3] = Elt<T>::from_f(acc[k].w);
     }
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 0; q < t.size; ++q) {
-      const float4 v = __ldcv(reinterpret_cast<const float4*>(t.part[q] + part_off + i));
-      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    }
-    out[r * D + d] = Elt<T>::from_f(acc.x);
-    out[r * D + d + 1] = Elt<T>::from_f(acc.y);
-    out[r * D + d + 2] = Elt<T>::from_f(acc.z);
-    out[r * D + d + 3] = Elt<T>::from_f(acc.w);
   }
 }
 
 int reduce_grid(int64_t n) {
-  return static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256, 148 * 2));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n / 4 / kU + 255) / 256, 148 * 4)));
 }
 
 }  // namespace
@@ -278,33 +309,51 @@ cudaError_t launch_tp_epoch(const TpPeers& t, cudaStream_t st) {
   return launched();
 }
 
-cudaError_t launch_tp_reduce_resid(int dtype, const TpPeers& t, int layer, int L,
-                                   const void* resid, void* out, int64_t n, int* err,
-                                   cudaStream_t st) {
-  if (n % 4 != 0) return cudaErrorInvalidValue;
+template <int S>
+void reduce_resid_s(int dtype, const TpPeers& t, int layer, int L, const void* resid, void* out,
+                    int64_t n, int* err, cudaStream_t st) {
   const int blocks = reduce_grid(n);
   if (dtype == BF16)
-    tp_reduce_resid_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+    tp_reduce_resid_kernel<S, __nv_bfloat16><<<blocks, 256, 0, st>>>(
         t, layer, L, static_cast<const __nv_bfloat16*>(resid), static_cast<__nv_bfloat16*>(out),
         n, err);
   else
-    tp_reduce_resid_kernel<float><<<blocks, 256, 0, st>>>(t, layer, L, static_cast<const float*>(resid),
-                                                          static_cast<float*>(out), n, err);
+    tp_reduce_resid_kernel<S, float><<<blocks, 256, 0, st>>>(
+        t, layer, L, static_cast<const float*>(resid), static_cast<float*>(out), n, err);
+}
+
+cudaError_t launch_tp_reduce_resid(int dtype, const TpPeers& t, int layer, int L,
+                                   const void* resid, void* out, int64_t n, int* err,
+                                   cudaStream_t st) {
+  if (n % 4 != 0 || t.size < 1 || t.size > kMaxTp) return cudaErrorInvalidValue;
+  if (t.size <= 2) reduce_resid_s<2>(dtype, t, layer, L, resid, out, n, err, st);
+  else if (t.size <= 4) reduce_resid_s<4>(dtype, t, layer, L, resid, out, n, err, st);
+  else reduce_resid_s<8>(dtype, t, layer, L, resid, out, n, err, st);
   return launched();
+}
+
+template <int S>
+void reduce_scatter_s(int dtype, const TpPeers& t, int layer, int L, const int64_t* rows,
+                      const int32_t* count, int n, int D, int64_t n_out_rows, void* out, int* err,
+                      cudaStream_t st) {
+  const int blocks = reduce_grid(static_cast<int64_t>(n) * D);
+  const int64_t off = t.part_elems;
+  if (dtype == BF16)
+    tp_reduce_scatter_kernel<S, __nv_bfloat16><<<blocks, 256, 0, st>>>(
+        t, layer, L, off, rows, count, n, D, n_out_rows, static_cast<__nv_bfloat16*>(out), err);
+  else
+    tp_reduce_scatter_kernel<S, float><<<blocks, 256, 0, st>>>(
+        t, layer, L, off, rows, count, n, D, n_out_rows, static_cast<float*>(out), err);
 }
 
 cudaError_t launch_tp_reduce_scatter(int dtype, const TpPeers& t, int layer, int L,
                                      const int64_t* rows, const int32_t* count, int n, int D,
                                      int64_t n_out_rows, void* out, int* err, cudaStream_t st) {
   if (D % 4 != 0 || n <= 0) return n <= 0 ? cudaSuccess : cudaErrorInvalidValue;
-  const int blocks = reduce_grid(static_cast<int64_t>(n) * D);
-  const int64_t off = t.part_elems;
-  if (dtype == BF16)
-    tp_reduce_scatter_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-        t, layer, L, off, rows, count, n, D, n_out_rows, static_cast<__nv_bfloat16*>(out), err);
-  else
-    tp_reduce_scatter_kernel<float><<<blocks, 256, 0, st>>>(t, layer, L, off, rows, count, n, D,
-                                                            n_out_rows, static_cast<float*>(out), err);
+  if (t.size < 1 || t.size > kMaxTp) return cudaErrorInvalidValue;
+  if (t.size <= 2) reduce_scatter_s<2>(dtype, t, layer, L, rows, count, n, D, n_out_rows, out, err, st);
+  else if (t.size <= 4) reduce_scatter_s<4>(dtype, t, layer, L, rows, count, n, D, n_out_rows, out, err, st);
+  else reduce_scatter_s<8>(dtype, t, layer, L, rows, count, n, D, n_out_rows, out, err, st);
   return launched();
 }
 

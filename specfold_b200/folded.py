@@ -126,6 +126,7 @@ class FoldedVerifyB200:
     # -------------------------------------------------------------- tensor parallel
     # rank, size and the library's communicator of the 14B configuration; size 1 = off
     _tp = (0, 1, None)
+    _tp_transport = None
 
     def set_tensor_parallel(self, rank: int, size: int, transport: Optional[str] = None,
                             max_rows: int = 256) -> None:
@@ -145,6 +146,7 @@ class FoldedVerifyB200:
         if size <= 1:
             return
         transport = transport or os.environ.get("SF_TP_TRANSPORT", "p2p")
+        self._tp_transport = transport
         if transport == "nccl":
             uid = (ctypes.c_char * 128)()
             if rank == 0:
