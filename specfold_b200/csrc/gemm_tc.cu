@@ -1081,6 +1081,8 @@ struct TcTuning {
   int pf_mb = 0;       // SF_GEMM_PF_MB: L2 prefetch budget for the next GEMM's weights
                        // (off: measured, the step got slower at 40 and 80 MB)
   int qkv_splits = 0;  // SF_QKV_SPLITS: split-K count of the QKV GEMM (0: chosen)
+  int pf_kind_mb[6] = {-1, -1, -1, -1, -1, -1};   // SF_GEMM_PF_MB_<kind>: the budget of the
+                                                  // GEMM with epilogue <kind> (0..5) only
 };
 static const TcTuning& tc_tuning() {
   static TcTuning t;
@@ -1093,6 +1095,11 @@ static const TcTuning& tc_tuning() {
     if (const char* v = getenv("SF_GEMM_SMEM_KB")) t.smem_kb = std::max(64, std::min(kMaxSmemKb, atoi(v)));
     if (const char* v = getenv("SF_GEMM_PF_MB")) t.pf_mb = std::max(0, std::min(96, atoi(v)));
     if (const char* v = getenv("SF_QKV_SPLITS")) t.qkv_splits = std::max(0, std::min(16, atoi(v)));
+    for (int k = 0; k < 6; ++k) {
+      char name[32];
+      snprintf(name, sizeof(name), "SF_GEMM_PF_MB_%d", k);
+      if (const char* v = getenv(name)) t.pf_kind_mb[k] = std::max(0, std::min(96, atoi(v)));
+    }
   });
   return t;
 }
@@ -1152,7 +1159,9 @@ WPrefetch gemm_prefetch_plan(const GemmArgs& a) {
   if (a.dtype != BF16 || !a.w_tiled || a.W == nullptr) return f;
   const TcPlan pl = tc_plan(a.n_out, a.K, a.epi.kind, a.epi.inter, a.rows_cap);
   const int64_t per_kb = static_cast<int64_t>(pl.n_groups) * pl.splits * pl.sub * kWBytes;
-  const int64_t budget = static_cast<int64_t>(tc_tuning().pf_mb) << 20;
+  const TcTuning& tune = tc_tuning();
+  const int kind_mb = a.epi.kind >= 0 && a.epi.kind < 6 ? tune.pf_kind_mb[a.epi.kind] : -1;
+  const int64_t budget = static_cast<int64_t>(kind_mb >= 0 ? kind_mb : tune.pf_mb) << 20;
   const int npf = static_cast<int>(std::min<int64_t>(pl.kb_per_split, per_kb > 0 ? budget / per_kb : 0));
   if (npf <= 0) return f;
   f.w = a.W;
