@@ -20,7 +20,7 @@
 //      update the prefix state by the block scores and write P = exp(s - m) in bf16,
 //      K-major, the rounding the reference applies before its P V dot;
 //   4. one thread issues O_blk = P V (M 128, N = head_dim, K 32) into TMEM;
-//   5. all eight warps (two per lane quarter, half of the dims each) read O_blk and store
+//   5. all sixteen warps (four per lane quarter, a quarter of the dims each) read O_blk and store
 //      O = (exp(m_pre - m) O_pre + O_blk) / l in bf16; M = m, Z = l.
 // Every mbarrier wait is bounded; TMEM is freed on every path.
 #include <cstdlib>
@@ -35,7 +35,9 @@ namespace {
 constexpr int kTcTasks = 128;        // tasks per CTA = MMA M
 constexpr int kTcKeys = 32;          // block keys (MMA N of S, K of P V)
 constexpr int kTcSplits = 16;        // prefix split partials merged per task
-constexpr int kTcThreads = 256;
+// sixteen warps: the split merge and the gathers are bound by the loads each SM keeps in
+// flight, so more warps per CTA (one CTA per SM) move the partials faster
+constexpr int kTcThreads = 512;
 
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -190,10 +192,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     sL[tid] = l;
   }
   __syncthreads();
-  // merged prefix output: items (row, 4 dims), four items per thread at a time with all
-  // their split partials (four splits per round) in flight together
+  // merged prefix output: items (row, 4 dims), two items per thread at a time with all
+  // their split partials (four splits per round) in flight together (four items spilled
+  // at sixteen warps' 128 registers per thread)
   constexpr int DQ = HD / 4;
-  constexpr int IT = 4;
+  constexpr int IT = 2;
   for (int i0 = tid; i0 < kTcTasks * DQ; i0 += IT * kTcThreads) {
     float4 acc[IT];
     int64_t base[IT];
@@ -302,7 +305,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   // ---- 5. O = (al * O_pre + O_blk) / l
   {
-    const int q = warp & 3, half = warp >> 2;
+    const int q = warp & 3, part = warp >> 2;       // lane quarter, quarter of the dims
     const int r = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const bool done = mbar_wait(o_full, 0, p.err);
@@ -315,14 +318,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int64_t row = static_cast<int64_t>(b) * p.N + n;
     T* O = reinterpret_cast<T*>(p.O);
 #pragma unroll
-    for (int c = 0; c < HD / 2; c += 16) {
+    for (int c = 0; c < HD / 4; c += 16) {
       float o[16];
       if (go) {
-        tmem_ld16(tO + lane_off + half * (HD / 2) + c, o);
+        tmem_ld16(tO + lane_off + part * (HD / 4) + c, o);
         tmem_ld_wait();
       }
       if (live) {
-        const int d0 = half * (HD / 2) + c;
+        const int d0 = part * (HD / 4) + c;
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -336,7 +339,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
     }
-    if (live && half == 0) {
+    if (live && part == 0) {
       p.M[row * p.H + h] = sM[r];
       p.Z[row * p.H + h] = sL[r];
     }
