@@ -605,11 +605,12 @@ __device__ __forceinline__ void epi_unit(const TcParams& p, const EpiCtx& x, int
 }
 
 // RMSNorm of rows i = blockIdx.x, blockIdx.x + gridDim.x, ... by the 256 epilogue
-// threads (D <= 256 * 8 * 4): one load of the row into registers, block reduction,
+// threads (D <= 256 * 8 * MAXV): one load of the row into registers, block reduction,
 // normalised from the registers (the rmsnorm_cta_kernel arithmetic).
+template <int MAXV>
 __device__ __forceinline__ void pre_norm_rows(const PreNorm& pr, int et, float* red, int* err) {
   using T = __nv_bfloat16;
-  constexpr int V = 8, MAXV = 4;
+  constexpr int V = 8;
   int n = pr.n;
   if (pr.count) n = min(n, *pr.count);
   for (int i = blockIdx.x; i < n; i += gridDim.x) {
@@ -657,10 +658,11 @@ __device__ __forceinline__ void pre_norm_rows(const PreNorm& pr, int et, float* 
 //   out[i] = T(w * T(x[r] * rstd))                  (the pre_norm_rows arithmetic)
 // from the same registers: one pass over the partials instead of a reduction, a device
 // counter hop and a re-read.
+template <int MAXV>
 __device__ __forceinline__ void pre_resid_norm_rows(const PreNorm& pr, const TcParams& g, int et,
                                                     float* red, int* err) {
   using T = __nv_bfloat16;
-  constexpr int V = 8, MAXV = 4;
+  constexpr int V = 8;
   int n = pr.n;
   if (pr.count) n = min(n, *pr.count);
   const int64_t split_stride = static_cast<int64_t>(g.rows_cap) * g.n_out;
@@ -736,7 +738,11 @@ __device__ __forceinline__ void resid_rows_rest(const PreNorm& pr, const TcParam
   }
 }
 
-template <int K0, int K1, int K2>
+// NV: 0 for chains without a fused norm (its code left out: the single GEMMs and the
+// lm_head), else the 8-element vectors per thread the norm keeps in registers (D <= 2048
+// NV).  The norm's arrays set the register pressure of the whole kernel: sized for
+// D <= 8192 they made every chain kernel spill (the QKV GEMM 388 bytes per thread).
+template <int K0, int K1, int K2, int NV>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_chain_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW2_0,
                     const __grid_constant__ CUtensorMap tmX0, const __grid_constant__ CUtensorMap tmX64_0,
@@ -976,7 +982,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     x.abort_flag = abort_flag;
     int acc_it = 0;
     for (int k = 0; k < c.n_phases; ++k) {
-      if (c.norm[k].x != nullptr) {
+      if (NV > 0 && c.norm[k].x != nullptr) {
         // the norm reads every row of the previous phase's output
         if (k > 0) {
           bool ok = true;
@@ -985,9 +991,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!epi_vote_all(ok && !*abort_flag)) *abort_flag = 1;
         }
         const bool fused = k > 0 && c.ph[k - 1].defer_reduce;
-        if (!*abort_flag) {
-          if (fused) pre_resid_norm_rows(c.norm[k], c.ph[k - 1], x.et, red, c.err);
-          else pre_norm_rows(c.norm[k], x.et, red, c.err);
+        if constexpr (NV > 0) {
+          if (!*abort_flag) {
+            if (fused) pre_resid_norm_rows<NV>(c.norm[k], c.ph[k - 1], x.et, red, c.err);
+            else pre_norm_rows<NV>(c.norm[k], x.et, red, c.err);
+          }
         }
         epi_sync_all();
         if (x.et == 0) {
@@ -996,7 +1004,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           atomicAdd(c.dep + 2 * k, 1u);
         }
         // the residual rows no later phase reads, while phase k streams its weights
-        if (fused && !*abort_flag) resid_rows_rest(c.norm[k], c.ph[k - 1], x.et);
+        if constexpr (NV > 0)
+          if (fused && !*abort_flag) resid_rows_rest(c.norm[k], c.ph[k - 1], x.et);
       }
       // this CTA's units of phase k: u = blockIdx.x + j * gridDim.x in the phase's range
       const int base = c.unit_base[k];
@@ -1247,30 +1256,37 @@ using ChainFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUt
                          CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
                          ChainParams);
 
-static ChainFn chain_kernel(int n, const int* k) {
+// the instantiation for the phase kinds k[0..n) and the norm's vector count nv (0: none)
+template <int NV>
+static ChainFn chain_kernel_nv(int n, const int* k) {
+  if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_SCATTER)
+    return tc_chain_kernel<EPI_SWIGLU, EPI_SCATTER, EPI_SCATTER, NV>;
+  // tensor parallel: the down projection's fp32 partial sums go to the exchange
+  if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_RAW)
+    return tc_chain_kernel<EPI_SWIGLU, EPI_RAW, EPI_RAW, NV>;
+  if (n == 3 && k[0] == EPI_RESID && k[1] == EPI_SWIGLU && k[2] == EPI_SCATTER)
+    return tc_chain_kernel<EPI_RESID, EPI_SWIGLU, EPI_SCATTER, NV>;
+  return nullptr;
+}
+static ChainFn chain_kernel(int n, const int* k, int nv) {
+  if (nv == 3) return chain_kernel_nv<3>(n, k);
+  if (nv == 4) return chain_kernel_nv<4>(n, k);
+  if (nv != 0) return nullptr;
   if (n == 1) {
     switch (k[0]) {
-      case EPI_RAW: return tc_chain_kernel<EPI_RAW, EPI_RAW, EPI_RAW>;
-      case EPI_QKV: return tc_chain_kernel<EPI_QKV, EPI_QKV, EPI_QKV>;
-      case EPI_RESID: return tc_chain_kernel<EPI_RESID, EPI_RESID, EPI_RESID>;
-      case EPI_SWIGLU: return tc_chain_kernel<EPI_SWIGLU, EPI_SWIGLU, EPI_SWIGLU>;
-      case EPI_SCATTER: return tc_chain_kernel<EPI_SCATTER, EPI_SCATTER, EPI_SCATTER>;
-      case EPI_LOGITS: return tc_chain_kernel<EPI_LOGITS, EPI_LOGITS, EPI_LOGITS>;
+      case EPI_RAW: return tc_chain_kernel<EPI_RAW, EPI_RAW, EPI_RAW, 0>;
+      case EPI_QKV: return tc_chain_kernel<EPI_QKV, EPI_QKV, EPI_QKV, 0>;
+      case EPI_RESID: return tc_chain_kernel<EPI_RESID, EPI_RESID, EPI_RESID, 0>;
+      case EPI_SWIGLU: return tc_chain_kernel<EPI_SWIGLU, EPI_SWIGLU, EPI_SWIGLU, 0>;
+      case EPI_SCATTER: return tc_chain_kernel<EPI_SCATTER, EPI_SCATTER, EPI_SCATTER, 0>;
+      case EPI_LOGITS: return tc_chain_kernel<EPI_LOGITS, EPI_LOGITS, EPI_LOGITS, 0>;
       default: return nullptr;
     }
   }
-  // the FFN (gate/up -> down), and o_proj -> norm -> FFN
   // a long GEMM and its wave tail (independent phases of one epilogue kind)
   if (n == 2 && k[0] == k[1] && (k[0] == EPI_LOGITS || k[0] == EPI_RAW))
-    return k[0] == EPI_LOGITS ? tc_chain_kernel<EPI_LOGITS, EPI_LOGITS, EPI_LOGITS>
-                              : tc_chain_kernel<EPI_RAW, EPI_RAW, EPI_RAW>;
-  if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_SCATTER)
-    return tc_chain_kernel<EPI_SWIGLU, EPI_SCATTER, EPI_SCATTER>;
-  // tensor parallel: the down projection's fp32 partial sums go to the all-reduce
-  if (n == 2 && k[0] == EPI_SWIGLU && k[1] == EPI_RAW)
-    return tc_chain_kernel<EPI_SWIGLU, EPI_RAW, EPI_RAW>;
-  if (n == 3 && k[0] == EPI_RESID && k[1] == EPI_SWIGLU && k[2] == EPI_SCATTER)
-    return tc_chain_kernel<EPI_RESID, EPI_SWIGLU, EPI_SCATTER>;
+    return k[0] == EPI_LOGITS ? tc_chain_kernel<EPI_LOGITS, EPI_LOGITS, EPI_LOGITS, 0>
+                              : tc_chain_kernel<EPI_RAW, EPI_RAW, EPI_RAW, 0>;
   return nullptr;
 }
 
@@ -1303,6 +1319,7 @@ static cudaError_t chain_launch(const GemmArgs* g, int n, const PreNormArgs* con
   CUtensorMap tm[kMaxPhases][4];
   TcPlan pl[kMaxPhases];
   int kinds[kMaxPhases];
+  int max_norm_d = 0;
   int* counters = static_cast<int*>(g[0].ws);
   for (int k = 0; k < n; ++k) {
     // untiled SwiGLU reads its up half through phase 0's second weight map: phase 0 only
@@ -1315,6 +1332,7 @@ static cudaError_t chain_launch(const GemmArgs* g, int n, const PreNormArgs* con
     kinds[k] = g[k].epi.kind;
     if (norms != nullptr && norms[k] != nullptr) {
       if (norms[k]->D % 8 != 0 || norms[k]->D > kEpiThreads * 8 * 4) return cudaErrorInvalidValue;
+      max_norm_d = std::max(max_norm_d, norms[k]->D);
       set_norm(&c.norm[k], norms[k]);
     }
   }
@@ -1371,7 +1389,8 @@ static cudaError_t chain_launch(const GemmArgs* g, int n, const PreNormArgs* con
   c.err = g[0].err;
   c.dep = dep;
 
-  ChainFn kern = chain_kernel(n, kinds);
+  const int nv = max_norm_d == 0 ? 0 : (max_norm_d <= kEpiThreads * 8 * 3 ? 3 : 4);
+  ChainFn kern = chain_kernel(n, kinds, nv);
   if (kern == nullptr) return cudaErrorInvalidValue;
   const size_t smem = static_cast<size_t>(c.stage_budget) + kSmemFixed;
   {
