@@ -76,6 +76,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
   __shared__ int s_src[kTcKeys];
 
+  // launched with programmatic stream serialization when that is enabled: every read of
+  // an earlier kernel's output (src, queries, block K / V, split partials) comes after
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int G = p.H / p.Hkv;
   const int t0 = blockIdx.z * tpc;                   // tpc <= 128 tasks of this CTA
