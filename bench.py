@@ -183,7 +183,14 @@ class ClockSampler:
                  "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
-        time.sleep(0.3)
+        # nvidia-smi's start-up (driver / NVML initialisation) costs host CPU: wait for its
+        # first sample, so that it is not competing with the launches of the timed region
+        deadline = time.monotonic() + 5.0
+        while self.proc is not None and time.monotonic() < deadline:
+            if os.path.getsize(self.path) > 0 or self.proc.poll() is not None:
+                break
+            time.sleep(0.02)
+        time.sleep(0.15)
         return self
 
     def __exit__(self, *exc):
