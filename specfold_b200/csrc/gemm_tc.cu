@@ -327,6 +327,26 @@ __device__ __forceinline__ void sum_splits8_pair(const float* partial, int split
                                                  int64_t split_stride, int64_t off_a,
                                                  int64_t off_b, float* acc_a, float* acc_b) {
   int s = 0;
+  for (; s + 4 <= splits; s += 4) {                // four splits' loads in flight
+    float4 a[16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float* qa = partial + (s + u) * split_stride + off_a;
+      const float* qb = partial + (s + u) * split_stride + off_b;
+      a[4 * u] = __ldcg(reinterpret_cast<const float4*>(qa));
+      a[4 * u + 1] = __ldcg(reinterpret_cast<const float4*>(qa + 4));
+      a[4 * u + 2] = __ldcg(reinterpret_cast<const float4*>(qb));
+      a[4 * u + 3] = __ldcg(reinterpret_cast<const float4*>(qb + 4));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float va[8], vb[8];
+      vec_get(a[4 * u], va); vec_get(a[4 * u + 1], va + 4);
+      vec_get(a[4 * u + 2], vb); vec_get(a[4 * u + 3], vb + 4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { acc_a[i] += va[i]; acc_b[i] += vb[i]; }
+    }
+  }
   for (; s + 2 <= splits; s += 2) {
     float4 a[8];
 #pragma unroll
