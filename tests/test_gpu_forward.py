@@ -98,6 +98,11 @@ EXTRA = {
     "mid_bf16_qwen_vocab": ("fastdllm", ModelDims(hidden=512, heads=4, kv_heads=2, head_dim=128,
                                                   inter=1408, layers=1, vocab=152064), 64, "tree"),
 }
+# a hidden size past 6144: the layer tail's fused norm keeps four vectors of 8 per thread
+# (the instantiation every shape up to 6144 does not use)
+EXTRA["wide_bf16_d8192"] = ("fastdllm", ModelDims(hidden=8192, heads=64, kv_heads=8,
+                                                 head_dim=128, inter=1024, layers=1,
+                                                 vocab=512), 64, "tree")
 # long prefixes of the Llama-8B microbenchmark sweep (GQA group 4, RoPE theta 5e5): the
 # prefix attention caps its key splits at 16, so each split streams P / 16 keys
 _LONG = ModelDims(hidden=1024, heads=8, kv_heads=2, head_dim=128, inter=1024, layers=1,
