@@ -3,7 +3,9 @@ each rank holds a head / intermediate shard, the o_proj and down partial sums ar
 across the ranks -- by the consuming kernels reading every rank's partials over NVLink
 ("p2p", the default) or by NCCL all-reduces ("nccl") -- and every rank must return the
 oracle's logits and fold masks (same tolerances as the single-GPU forward), identical on
-both ranks.  Runs as two child processes, one per GPU; skipped with fewer than two GPUs."""
+both ranks.  Runs as two child processes, one per GPU; skipped with fewer than two GPUs.
+The failure path (a partner that never arrives) is tested on one GPU: the bounded waits
+end the forward with an error status instead of a hang."""
 import os
 import socket
 import sys
@@ -77,3 +79,41 @@ def test_tensor_parallel_two_ranks(name, transport):
     for r in range(ws):
         assert out[r][1] == "ok", f"rank {r}: {out[r][1]}"
     assert torch.equal(out[0][0], out[1][0]), "ranks disagree"
+
+
+def test_peer_wait_times_out_with_status():
+    """Failure detection of the peer-memory exchange, on one GPU and without a fault: rank
+    0 of a two-rank peer table whose partner never runs.  Every reduction's handshake waits
+    for a flag that nothing sets; the bounded wait (2 s) gives up, sets the timeout bit of
+    the device error word and returns, so the forward ends with SpecFoldError and the
+    context stays usable for the next forward."""
+    import ctypes
+    from specfold_b200 import SpecFoldB200FastDLLMV2Generation, _lib
+    from specfold_b200.synthetic import (ModelDims, StandinExecutor, build_model,
+                                         random_prefix_cache, tree_block_input)
+    dims = ModelDims(hidden=512, heads=4, kv_heads=2, head_dim=128, inter=1024, layers=1,
+                     vocab=256)
+    model = build_model(dims, family="fastdllm", dtype=torch.bfloat16, seed=0, device="cuda")
+    cache = random_prefix_cache(dims, 64, dtype=torch.bfloat16, seed=1, device="cuda")
+    ids = tree_block_input(dims.vocab, N=32, edits_per_level=3).cuda()
+    lib = _lib.load()
+    nbytes = lib.sf_tp_exchange_bytes(256, dims.hidden)
+    mine = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    absent = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")   # the partner's buffer
+    peers = ctypes.c_void_p()
+    _lib.check(lib.sf_tp_peers_init(0, 2, (ctypes.c_void_p * 2)(mine.data_ptr(), absent.data_ptr()),
+                                    256, dims.hidden, ctypes.byref(peers)), "tp peer table")
+    gen = SpecFoldB200FastDLLMV2Generation(model_executor=StandinExecutor(model), delta=0.1)
+    gen._tp, gen._tp_transport = (0, 2, None), "p2p"
+    gen._tp_peers, gen._tp_xbuf = peers.value, (mine, [])
+    try:
+        with pytest.raises(_lib.SpecFoldError, match="timed out"):
+            gen._batched_block_forward(ids, cache)
+            torch.cuda.synchronize()
+    finally:
+        gen.close_tensor_parallel()
+    # the context is intact: a plain single-GPU forward still runs
+    plain = SpecFoldB200FastDLLMV2Generation(model_executor=StandinExecutor(model), delta=0.1)
+    out = plain._batched_block_forward(ids, cache)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
