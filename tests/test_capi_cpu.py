@@ -112,3 +112,31 @@ def test_no_fallback_to_the_reference_sampler_or_drafts():
     with pytest.raises(NotImplementedError):
         nld.get_draft_blocks(torch.zeros(8, dtype=torch.int64), torch.zeros(8, 16),
                              torch.ones(8, dtype=torch.bool))
+
+
+def test_tensor_parallel_entries_without_device():
+    """The peer-memory exchange's host-side entry points: buffer sizing, the peer table's
+    argument checks (it only records addresses, so it needs no device), and the IPC
+    calls' rejection of missing arguments."""
+    lib = _lib.load()
+    assert lib.sf_tp_exchange_bytes(256, 3584) == 512 + 2 * 256 * 3584 * 4
+    assert lib.sf_tp_exchange_bytes(0, 3584) == 0
+    out = ctypes.c_void_p()
+    two = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+    assert lib.sf_tp_peers_init(0, 1, two, 256, 512, ctypes.byref(out)) == 1      # size < 2
+    assert lib.sf_tp_peers_init(2, 2, two, 256, 512, ctypes.byref(out)) == 1      # rank
+    assert lib.sf_tp_peers_init(0, 2, two, 256, 510, ctypes.byref(out)) == 1      # D % 4
+    odd = (ctypes.c_void_p * 2)(0x10000, 0x20008)
+    assert lib.sf_tp_peers_init(0, 2, odd, 256, 512, ctypes.byref(out)) == 1      # unaligned
+    assert b"unaligned" in lib.sf_last_error()
+    assert lib.sf_tp_peers_init(1, 2, two, 256, 512, ctypes.byref(out)) == 0
+    assert out.value
+    assert lib.sf_tp_peers_destroy(out) == 0
+    h = (ctypes.c_char * 64)()
+    off = ctypes.c_size_t()
+    assert lib.sf_tp_ipc_export(None, ctypes.cast(h, ctypes.c_void_p), 64, ctypes.byref(off)) == 1
+    assert lib.sf_tp_ipc_export(0x10000, ctypes.cast(h, ctypes.c_void_p), 8, ctypes.byref(off)) == 1
+    base = ctypes.c_void_p()
+    assert lib.sf_tp_ipc_open(None, 64, ctypes.byref(base)) == 1
+    assert lib.sf_tp_ipc_close(None) == 1
+
